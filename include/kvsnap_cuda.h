@@ -1,0 +1,166 @@
+/*
+ * kvsnap_cuda.h: the C ABI of kvsnap_b200/_native/_cuda_native.so.
+ *
+ * Two groups of entry points, all extern "C", plain pointers and sizes, no
+ * torch types. Every int-returning call returns 0 on success and -1 on error,
+ * with the message in the calling thread's kvsnap_cuda_error().
+ *
+ * 1. The pinned-pool ABI, version 2: the same symbols, argument meaning and
+ *    error behaviour as the reference's csrc/dataplane/cuda_pool.cpp, which
+ *    kvsnap/connector/dataplane.py:47-60 binds with ctypes. A build of this
+ *    library dropped in as kvsnap/_native/_cuda_native<EXT_SUFFIX>.so (or named
+ *    by KVSNAP_CUDA_LIBRARY) serves the reference's CudaPool unchanged.
+ *
+ * 2. The data-plane kernels (kvsnap_dp_*), sm_100a CUDA. They replace the
+ *    reference's restore kernel (kvsnap/connector/copy_kernel.py:23-49), its
+ *    torch save gather (kvsnap/connector/dataplane.py:409-427) and its host
+ *    checksums (csrc/dataplane/io.cpp:27-47 CRC32C, hashlib SHA-256 in
+ *    kvsnap/store/store.py:616-629 and kvsnap/connector/volatile.py:141-151).
+ *    Tables passed to them (spans, block ids, addresses) live in device memory
+ *    (or mapped pinned memory); packed-block addresses may be device memory or
+ *    pinned host memory from cudaHostAlloc, which the kernels read and write in
+ *    place over the host link.
+ */
+#ifndef KVSNAP_CUDA_H
+#define KVSNAP_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- 1. pinned pool (ABI 2) ------------------------------------------------ */
+
+/* Thread-local text of the last error (reference cuda_pool.cpp:50). */
+const char* kvsnap_cuda_error(void);
+/* Returns 2 (reference cuda_pool.cpp:52; checked at dataplane.py:64-66). */
+int kvsnap_pool_abi_version(void);
+/* A pinned arena of `capacity` bytes on `device` plus its own non-blocking copy
+   stream; NULL on error (reference cuda_pool.cpp:53-62). */
+void* kvsnap_pool_create(size_t capacity, int device);
+/* Frees the pool; if its stream cannot be drained the pinned memory is kept
+   (quarantined) instead of freed (reference cuda_pool.cpp:63, 30-38). */
+void kvsnap_pool_destroy(void* pool);
+/* Drains the copy stream, then frees; on a failed drain the pool stays intact
+   and -1 is returned (reference cuda_pool.cpp:66-74). */
+int kvsnap_pool_close_checked(void* pool);
+/* The copy stream's handle, borrowed (reference cuda_pool.cpp:78-85). */
+int kvsnap_pool_copy_stream(void* pool, uintptr_t* stream);
+/* First-fit reservation. Fails with a message containing "pinned capacity
+   exhausted" when it cannot fit (reference cuda_pool.cpp:86-104). Start offsets
+   are rounded up to 16 bytes so every allocation suits 16-byte vector access. */
+int kvsnap_pool_reserve(void* pool, size_t size, uint64_t* id, void** ptr);
+/* One async copy between device memory and an allocation on the copy stream;
+   a device-to-host copy first waits for `producer_stream` (reference
+   cuda_pool.cpp:107-133). */
+int kvsnap_pool_copy(void* pool, uint64_t id, size_t host_offset, void* device_ptr, size_t size, int to_host,
+                     uintptr_t producer_stream);
+/* `height` rows of `width` bytes, strided on both sides (reference cuda_pool.cpp:139-169). */
+int kvsnap_pool_copy_2d(void* pool, uint64_t id, size_t host_offset, size_t host_pitch, void* device_ptr,
+                        size_t device_pitch, size_t width, size_t height, int to_host, uintptr_t producer_stream);
+/* Block until the allocation's last copy completes (reference cuda_pool.cpp:170-177). */
+int kvsnap_pool_wait(void* pool, uint64_t id);
+/* 1 when idle, 0 while a copy is in flight, -1 on error (reference cuda_pool.cpp:178-189). */
+int kvsnap_pool_ready(void* pool, uint64_t id);
+/* Wait, then return the bytes to the arena (reference cuda_pool.cpp:190-199). */
+int kvsnap_pool_release(void* pool, uint64_t id);
+/* Extension (no reference counterpart): record the allocation's completion
+   event on the copy stream now, so wait/ready/release also fence kernels that
+   read or write the allocation in place on that stream. */
+int kvsnap_pool_mark(void* pool, uint64_t id);
+
+/* ---- 2. data-plane kernels --------------------------------------------------- */
+
+#define KVSNAP_DP_ABI_VERSION 1
+
+/* Status bits a kernel ORs into its status word instead of faulting. */
+#define KVSNAP_DP_MISALIGNED 1u      /* an address or size broke the vector width */
+#define KVSNAP_DP_BAD_BLOCK 2u       /* a block id outside its cache */
+#define KVSNAP_DP_CRC_MISMATCH 4u    /* a block's CRC32C differed from the expected one */
+
+/*
+ * One registered layer view, i.e. one span of every packed block. A packed
+ * block is the spans back to back in registration order (layer-name order,
+ * reference dataplane.py:226); span s of cache block b lives at
+ * base + b * pitch and is `bytes` long, dense, copied in storage order
+ * (dataplane.py:283-305). 64 bytes.
+ */
+typedef struct kvsnap_span {
+    int64_t base;         /* device address of block 0 of this view */
+    int64_t pitch;        /* bytes between consecutive blocks */
+    int64_t offset;       /* byte offset of the span inside a packed block */
+    int64_t bytes;        /* span bytes per block */
+    int64_t token_pitch;  /* bytes between consecutive token slots (tail zeroing) */
+    int32_t tokens;       /* token slots per block (the block size) */
+    int32_t row_bytes;    /* contiguous bytes of one (head, token) row */
+    int64_t nblocks;      /* blocks in this cache, for in-kernel bounds checks */
+    uint32_t crc_shift;   /* x^(8 * bytes after this span) mod P, filled by kvsnap_dp_plan */
+    uint32_t flags;       /* reserved, 0 */
+} kvsnap_span;
+
+int kvsnap_dp_abi_version(void);
+
+/* Fill `offset` and `crc_shift` of a host span array in registration order;
+   writes the packed block size to *block_bytes. Host-only, no CUDA. */
+int kvsnap_dp_plan(kvsnap_span* spans, int nspans, uint64_t* block_bytes);
+
+/* CRC32C of a host buffer with a prior value: the host library's semantics
+   (reference io.cpp:39-44), exported here for self-checks. Host-only. */
+uint32_t kvsnap_dp_crc32c_host(const void* data, size_t size, uint32_t prior);
+
+/*
+ * Save gather (replaces dataplane.py:388-437 and its host hashing). For each
+ * i < n and span s: copy the span of cache block blocks[i] to
+ * targets[i] + spans[s].offset. In block n-1, token slots >= valid_tokens are
+ * written as zeros when valid_tokens > 0 (dataplane.py:262-272, 433-436).
+ * When crc_out is not NULL, crc_out[i] receives the CRC32C of packed block i
+ * as written (zeros included). `vec` is 16 or 8: the alignment every address,
+ * pitch, offset and span size meets. `ctas` 0 picks a default. status (device
+ * word, may be NULL) receives KVSNAP_DP_* bits.
+ */
+int kvsnap_dp_gather(const kvsnap_span* spans, int nspans, uint64_t block_bytes, const int64_t* blocks,
+                     const int64_t* targets, int64_t n, int32_t valid_tokens, uint32_t* crc_out,
+                     uint32_t* status, int vec, int ctas, uintptr_t stream);
+
+/*
+ * Restore scatter (replaces copy_kernel.py:23-49 and the loader-thread CRC
+ * check, store.py:717-718). For each i < n and span s: copy
+ * sources[i] + spans[s].offset to the span of cache block blocks[i]. When
+ * crc_out is not NULL it receives the CRC32C of each source block; when
+ * expect is not NULL as well, a block whose CRC differs sets
+ * KVSNAP_DP_CRC_MISMATCH in *status (its bytes are already written: callers
+ * that must not write unverified bytes verify first with kvsnap_dp_crc32c).
+ * A non-NULL `gate` is read by every CTA first: when *gate is non-zero the
+ * kernel writes nothing.
+ */
+int kvsnap_dp_scatter(const kvsnap_span* spans, int nspans, uint64_t block_bytes, const int64_t* sources,
+                      const int64_t* blocks, int64_t n, uint32_t* crc_out, const uint32_t* expect,
+                      const uint32_t* gate, uint32_t* status, int vec, int ctas, uintptr_t stream);
+
+/* CRC32C of n packed blocks of block_bytes at addrs[i] (device or pinned host).
+   With expect not NULL, mismatches set KVSNAP_DP_CRC_MISMATCH in *status. */
+int kvsnap_dp_crc32c(const int64_t* addrs, int64_t n, uint64_t block_bytes, uint32_t* crc_out,
+                     const uint32_t* expect, uint32_t* status, int vec, int ctas, uintptr_t stream);
+
+/* SHA-256 of n packed blocks of block_bytes at addrs[i]; digest i is the 32
+   big-endian bytes at out + 32 * i, the bytes of hashlib.sha256(block).digest()
+   (the store's content id, store.py:623). One lane hashes one block. */
+int kvsnap_dp_sha256(const int64_t* addrs, int64_t n, uint64_t block_bytes, uint8_t* out, uintptr_t stream);
+
+/*
+ * The reference restore kernel's exact interface (copy_kernel.py:43-49): all
+ * six tables are device int64 arrays; job j copies layer_words[l] 8-byte words
+ * of layer l = j % n_layers from sources[b] + layer_offsets[l] to
+ * layer_bases[l] + blocks[b] * layer_pitches[l], b = j / n_layers. No checksums.
+ */
+int kvsnap_dp_copy_host_blocks(const int64_t* sources, const int64_t* blocks, int64_t n_blocks,
+                               const int64_t* layer_offsets, const int64_t* layer_bases,
+                               const int64_t* layer_pitches, const int64_t* layer_words, int64_t n_layers,
+                               int ctas, uintptr_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* KVSNAP_CUDA_H */

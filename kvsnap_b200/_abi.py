@@ -1,0 +1,96 @@
+"""ctypes declarations of include/kvsnap_cuda.h and include/kvsnap_io.h.
+
+Kept in one place so the pool, the data plane, the tests and the bench bind the
+same prototypes. Loading never initialises CUDA; a missing or mismatched
+library raises, there is no fallback.
+"""
+from __future__ import annotations
+
+import ctypes as C
+
+DP_ABI_VERSION = 1
+POOL_ABI_VERSION = 2
+IO_ABI_VERSION = 1
+
+MISALIGNED, BAD_BLOCK, CRC_MISMATCH = 1, 2, 4
+
+
+class Span(C.Structure):
+    """``kvsnap_span``: one registered layer view (64 bytes)."""
+    _fields_ = [("base", C.c_int64), ("pitch", C.c_int64), ("offset", C.c_int64), ("bytes", C.c_int64),
+                ("token_pitch", C.c_int64), ("tokens", C.c_int32), ("row_bytes", C.c_int32),
+                ("nblocks", C.c_int64), ("crc_shift", C.c_uint32), ("flags", C.c_uint32)]
+
+
+assert C.sizeof(Span) == 64
+
+_P = C.c_void_p
+_I64 = C.c_int64
+_U64 = C.c_uint64
+_SZ = C.c_size_t
+
+POOL_API = {
+    "kvsnap_pool_abi_version": ([], C.c_int),
+    "kvsnap_cuda_error": ([], C.c_char_p),
+    "kvsnap_pool_create": ([_SZ, C.c_int], _P),
+    "kvsnap_pool_destroy": ([_P], None),
+    "kvsnap_pool_close_checked": ([_P], C.c_int),
+    "kvsnap_pool_copy_stream": ([_P, C.POINTER(C.c_size_t)], C.c_int),
+    "kvsnap_pool_reserve": ([_P, _SZ, C.POINTER(C.c_uint64), C.POINTER(C.c_void_p)], C.c_int),
+    "kvsnap_pool_copy": ([_P, C.c_uint64, _SZ, _P, _SZ, C.c_int, _SZ], C.c_int),
+    "kvsnap_pool_copy_2d": ([_P, C.c_uint64, _SZ, _SZ, _P, _SZ, _SZ, _SZ, C.c_int, _SZ], C.c_int),
+    "kvsnap_pool_wait": ([_P, C.c_uint64], C.c_int),
+    "kvsnap_pool_ready": ([_P, C.c_uint64], C.c_int),
+    "kvsnap_pool_release": ([_P, C.c_uint64], C.c_int),
+}
+
+# Pool entry points this library adds to the reference's ABI 2 set.
+POOL_EXTRA = {
+    "kvsnap_pool_mark": ([_P, C.c_uint64], C.c_int),
+}
+
+DP_API = {
+    "kvsnap_dp_abi_version": ([], C.c_int),
+    "kvsnap_dp_plan": ([C.POINTER(Span), C.c_int, C.POINTER(C.c_uint64)], C.c_int),
+    "kvsnap_dp_crc32c_host": ([_P, _SZ, C.c_uint32], C.c_uint32),
+    "kvsnap_dp_gather": ([_P, C.c_int, _U64, _P, _P, _I64, C.c_int32, _P, _P, C.c_int, C.c_int, _SZ], C.c_int),
+    "kvsnap_dp_scatter": ([_P, C.c_int, _U64, _P, _P, _I64, _P, _P, _P, _P, C.c_int, C.c_int, _SZ], C.c_int),
+    "kvsnap_dp_crc32c": ([_P, _I64, _U64, _P, _P, _P, C.c_int, C.c_int, _SZ], C.c_int),
+    "kvsnap_dp_sha256": ([_P, _I64, _U64, _P, _SZ], C.c_int),
+    "kvsnap_dp_copy_host_blocks": ([_P, _P, _I64, _P, _P, _P, _P, _I64, C.c_int, _SZ], C.c_int),
+}
+
+IO_API = {
+    "kvsnap_io_abi_version": ([], C.c_int),
+    "kvsnap_crc32c_extend": ([_P, _SZ, C.c_uint32], C.c_uint32),
+    "kvsnap_crc32c": ([_P, _SZ], C.c_uint32),
+    "kvsnap_pwrite_all": ([C.c_int, _P, _SZ, C.c_int64, C.c_int], C.c_int),
+    "kvsnap_pread_all": ([C.c_int, _P, _SZ, C.c_int64], C.c_int),
+    "kvsnap_io_pool_create": ([_SZ, _SZ], _P),
+    "kvsnap_io_pool_destroy": ([_P], None),
+    "kvsnap_io_pool_transfer": ([_P, C.c_int, _P, _SZ, C.c_int64, C.c_int, C.c_int], C.c_int),
+}
+
+
+def declare(lib, api: dict, *, required: bool = True):
+    """Set argtypes/restype; a symbol missing from the library raises when ``required``."""
+    for name, (args, result) in api.items():
+        try:
+            fn = getattr(lib, name)
+        except AttributeError:
+            if required:
+                raise RuntimeError(f"{lib._name}: missing symbol {name}; rebuild with python -m kvsnap_b200.build")
+            continue
+        fn.argtypes, fn.restype = args, result
+    return lib
+
+
+_cache = {}
+
+
+def load(path, api: dict):
+    """Load a library once per path and declare ``api`` on it."""
+    key = str(path)
+    if key not in _cache:
+        _cache[key] = declare(C.CDLL(key), api)
+    return _cache[key]

@@ -1,0 +1,642 @@
+// sm_100a data-plane kernels of _cuda_native.so: save gather, restore scatter,
+// CRC32C and SHA-256 of packed snapshot blocks.
+//
+// Reference behaviour reproduced (paths in the kvsnap source tree):
+//   * packed block = the registered layer spans back to back in layer-name
+//     order, each span a dense block copied in storage order
+//     (kvsnap/connector/dataplane.py:221-249, 283-305);
+//   * save: gather a request's blocks into packed blocks and zero the token
+//     slots past the last computed token of the last block
+//     (dataplane.py:262-272, 388-437);
+//   * restore: copy each packed (block, layer) span into its cache row
+//     (kvsnap/connector/copy_kernel.py:23-49);
+//   * checksums: CRC32C, reflected Castagnoli 0x82F63B78 with inverted
+//     register and output (csrc/dataplane/io.cpp:16-47), and the content id
+//     SHA-256 (FIPS 180-4) of each packed block (kvsnap/store/store.py:623).
+//
+// CRC32C on a GPU. A CRC is linear over GF(2): for a raw register (no
+// inversions) raw(0, A||B) = raw(0, A) * x^(8|B|) + raw(0, B) mod P. So each
+// warp CRCs its own (block, span) unit, the 32 lanes each keep a partial
+// register over the 16-byte vectors they load (coalesced: lane j takes bytes
+// 16j..16j+15 of every 512-byte step), the partials are moved into place by
+// multiplying with x^(8k) mod P and XOR-reduced over the warp, the span's
+// result is moved to its place in the packed block the same way, and units of
+// one block meet in one word through atomicXor. Bytes are folded in with
+// slicing-by-16 tables in shared memory (T_k[v] = raw CRC of byte v followed
+// by k zero bytes), built at compile time.
+#include <cuda_runtime.h>
+
+#include <cstdint>
+#include <cstdio>
+
+#include "kvsnap_cuda.h"
+#include "kvsnap_internal.h"
+
+namespace {
+
+constexpr uint32_t kPoly = 0x82F63B78u;
+
+// ---- GF(2) arithmetic, reflected (bit 31 = coefficient of x^0) --------------
+
+__host__ __device__ constexpr uint32_t gf_mulmod(uint32_t a, uint32_t b) {
+    uint32_t p = 0;
+    for (int k = 31; k >= 0; --k) {
+        p ^= b & (0u - ((a >> k) & 1u));
+        b = (b >> 1) ^ (kPoly & (0u - (b & 1u)));
+    }
+    return p;
+}
+
+__host__ __device__ constexpr uint32_t gf_xpow8n(uint64_t n) {
+    uint32_t result = 1u << 31, square = 1u << 23;   // x^0, x^8
+    for (; n; n >>= 1) {
+        if (n & 1u) result = gf_mulmod(result, square);
+        square = gf_mulmod(square, square);
+    }
+    return result;
+}
+
+// Tables: slots 0..15 hold T_0..T_15, slots 16..19 T_492..T_495 (moving a lane's
+// register 496 bytes ahead), slots 20..23 T_244..T_247 (the same for 8-byte vectors).
+struct CrcTables {
+    uint32_t t[24][256];
+};
+
+constexpr CrcTables make_tables() {
+    CrcTables r{};
+    for (uint32_t v = 0; v < 256; ++v) {
+        uint32_t x = v;
+        for (int k = 0; k < 8; ++k) x = (x >> 1) ^ (kPoly & (0u - (x & 1u)));
+        r.t[0][v] = x;
+    }
+    for (int k = 1; k < 16; ++k)
+        for (int v = 0; v < 256; ++v) r.t[k][v] = (r.t[k - 1][v] >> 8) ^ r.t[0][r.t[k - 1][v] & 0xFFu];
+    for (int j = 0; j < 4; ++j) {
+        const uint32_t far16 = gf_xpow8n(492 + j), far8 = gf_xpow8n(244 + j);
+        for (int v = 0; v < 256; ++v) {
+            r.t[16 + j][v] = gf_mulmod(r.t[0][v], far16);
+            r.t[20 + j][v] = gf_mulmod(r.t[0][v], far8);
+        }
+    }
+    return r;
+}
+
+struct Pow8 {
+    uint32_t p[48];   // x^(8 * 2^k) mod P
+};
+
+constexpr Pow8 make_pow8() {
+    Pow8 r{};
+    uint32_t s = 1u << 23;
+    for (int k = 0; k < 48; ++k) {
+        r.p[k] = s;
+        s = gf_mulmod(s, s);
+    }
+    return r;
+}
+
+__device__ const CrcTables g_tables = make_tables();
+__device__ const Pow8 g_pow8 = make_pow8();
+
+__device__ __forceinline__ uint32_t dev_xpow8n(uint64_t n) {
+    uint32_t r = 1u << 31;
+    for (int k = 0; n; ++k, n >>= 1)
+        if (n & 1u) r = gf_mulmod(r, g_pow8.p[k]);
+    return r;
+}
+
+// ---- vectors ------------------------------------------------------------------
+
+template <int VEC>
+struct Vec;
+template <>
+struct Vec<16> {
+    using T = uint4;
+    static constexpr int kTables = 20;
+    __device__ static T zero() { return make_uint4(0, 0, 0, 0); }
+    __device__ static T load(const char* p) { return __ldcs(reinterpret_cast<const uint4*>(p)); }
+    __device__ static void store(char* p, T v) { *reinterpret_cast<uint4*>(p) = v; }
+    __device__ static uint32_t word(const T& v, int i) { return i == 0 ? v.x : i == 1 ? v.y : i == 2 ? v.z : v.w; }
+    __device__ static void set_word(T& v, int i, uint32_t w) {
+        if (i == 0) v.x = w; else if (i == 1) v.y = w; else if (i == 2) v.z = w; else v.w = w;
+    }
+};
+template <>
+struct Vec<8> {
+    using T = uint2;
+    static constexpr int kTables = 12;
+    __device__ static T zero() { return make_uint2(0, 0); }
+    __device__ static T load(const char* p) { return __ldcs(reinterpret_cast<const uint2*>(p)); }
+    __device__ static void store(char* p, T v) { *reinterpret_cast<uint2*>(p) = v; }
+    __device__ static uint32_t word(const T& v, int i) { return i == 0 ? v.x : v.y; }
+    __device__ static void set_word(T& v, int i, uint32_t w) {
+        if (i == 0) v.x = w; else v.y = w;
+    }
+};
+
+// Shared-memory copy of the tables one vector width needs: T_0..T_{VEC-1}, then
+// the four "far" tables for moving a register 32*VEC - VEC bytes ahead.
+template <int VEC>
+__device__ __forceinline__ void load_tables(uint32_t* tb) {
+    const uint32_t* g = &g_tables.t[0][0];
+    for (int i = threadIdx.x; i < Vec<VEC>::kTables * 256; i += blockDim.x) {
+        const int slot = i >> 8, v = i & 255;
+        const int src = slot < VEC ? slot : (VEC == 16 ? 16 : 20) + (slot - VEC);
+        tb[i] = g[src * 256 + v];
+    }
+}
+
+#define KV_T(slot, byte) tb[(slot) * 256 + (byte)]
+
+// One Horner step of a lane's register: r <- r * x^(8*32*VEC) + raw(0, v).
+__device__ __forceinline__ uint32_t crc_step(const uint32_t* tb, uint32_t r, uint4 v) {
+    const uint32_t far = KV_T(19, r & 255) ^ KV_T(18, (r >> 8) & 255) ^ KV_T(17, (r >> 16) & 255) ^ KV_T(16, r >> 24);
+    const uint32_t w = v.x ^ far;
+    return KV_T(15, w & 255) ^ KV_T(14, (w >> 8) & 255) ^ KV_T(13, (w >> 16) & 255) ^ KV_T(12, w >> 24) ^
+           KV_T(11, v.y & 255) ^ KV_T(10, (v.y >> 8) & 255) ^ KV_T(9, (v.y >> 16) & 255) ^ KV_T(8, v.y >> 24) ^
+           KV_T(7, v.z & 255) ^ KV_T(6, (v.z >> 8) & 255) ^ KV_T(5, (v.z >> 16) & 255) ^ KV_T(4, v.z >> 24) ^
+           KV_T(3, v.w & 255) ^ KV_T(2, (v.w >> 8) & 255) ^ KV_T(1, (v.w >> 16) & 255) ^ KV_T(0, v.w >> 24);
+}
+
+__device__ __forceinline__ uint32_t crc_step(const uint32_t* tb, uint32_t r, uint2 v) {
+    const uint32_t far = KV_T(11, r & 255) ^ KV_T(10, (r >> 8) & 255) ^ KV_T(9, (r >> 16) & 255) ^ KV_T(8, r >> 24);
+    const uint32_t w = v.x ^ far;
+    return KV_T(7, w & 255) ^ KV_T(6, (w >> 8) & 255) ^ KV_T(5, (w >> 16) & 255) ^ KV_T(4, w >> 24) ^
+           KV_T(3, v.y & 255) ^ KV_T(2, (v.y >> 8) & 255) ^ KV_T(1, (v.y >> 16) & 255) ^ KV_T(0, v.y >> 24);
+}
+
+#undef KV_T
+
+__device__ __forceinline__ uint32_t warp_xor(uint32_t v) {
+#pragma unroll
+    for (int d = 16; d; d >>= 1) v ^= __shfl_xor_sync(0xFFFFFFFFu, v, d);
+    return v;
+}
+
+__device__ __forceinline__ void flag(uint32_t* status, uint32_t bits) {
+    if (status) atomicOr(status, bits);
+}
+
+// Zero the bytes of a vector at span offset `at` whose token slot is >= valid.
+template <int VEC>
+__device__ typename Vec<VEC>::T mask_tail(typename Vec<VEC>::T v, int64_t at, const kvsnap_span& sp, int valid) {
+    if (sp.row_bytes % VEC == 0) {   // the vector lies inside one (head, token) row
+        const int64_t token = (at / sp.token_pitch) % sp.tokens;
+        return token >= valid ? Vec<VEC>::zero() : v;
+    }
+    for (int w = 0; w < VEC / 4; ++w) {
+        uint32_t word = Vec<VEC>::word(v, w);
+        for (int b = 0; b < 4; ++b) {
+            const int64_t token = ((at + 4 * w + b) / sp.token_pitch) % sp.tokens;
+            if (token >= valid) word &= ~(0xFFu << (8 * b));
+        }
+        Vec<VEC>::set_word(v, w, word);
+    }
+    return v;
+}
+
+// One warp moves (STORE) and/or checksums `len` bytes from src to dst. The
+// span is front-padded with zeros to a whole number of 32*VEC-byte steps, which
+// leaves a zero-initialised raw CRC unchanged. Returns the lane's register:
+// its vectors' raw CRC as if the unit ended at the lane's last vector + 32*VEC
+// - (lane+1)*VEC; the caller multiplies by x^(8*VEC*(31-lane)).
+template <int VEC, bool STORE, bool CRC>
+__device__ __forceinline__ uint32_t warp_unit(const uint32_t* tb, const char* __restrict__ src,
+                                              char* __restrict__ dst, int64_t len, int lane, bool tail,
+                                              const kvsnap_span& sp, int valid) {
+    using V = typename Vec<VEC>::T;
+    constexpr int kStep = 32 * VEC;
+    constexpr int kUnroll = 4;
+    const int64_t steps = (len + kStep - 1) / kStep;
+    const int64_t first = (int64_t)lane * VEC - (steps * kStep - len);
+    uint32_t r = 0;
+    int64_t t = 0;
+    for (; t + kUnroll <= steps; t += kUnroll) {
+        V v[kUnroll];
+#pragma unroll
+        for (int u = 0; u < kUnroll; ++u) {
+            const int64_t at = first + (t + u) * kStep;
+            v[u] = at >= 0 ? Vec<VEC>::load(src + at) : Vec<VEC>::zero();
+        }
+#pragma unroll
+        for (int u = 0; u < kUnroll; ++u) {
+            const int64_t at = first + (t + u) * kStep;
+            if (at >= 0) {
+                if (tail) v[u] = mask_tail<VEC>(v[u], at, sp, valid);
+                if (STORE) Vec<VEC>::store(dst + at, v[u]);
+            }
+        }
+        if (CRC) {
+#pragma unroll
+            for (int u = 0; u < kUnroll; ++u) r = crc_step(tb, r, v[u]);
+        }
+    }
+    for (; t < steps; ++t) {
+        const int64_t at = first + t * kStep;
+        V v = Vec<VEC>::zero();
+        if (at >= 0) {
+            v = Vec<VEC>::load(src + at);
+            if (tail) v = mask_tail<VEC>(v, at, sp, valid);
+            if (STORE) Vec<VEC>::store(dst + at, v);
+        }
+        if (CRC) r = crc_step(tb, r, v);
+    }
+    return r;
+}
+
+enum Mode { kGather = 0, kScatter = 1 };
+
+struct SpanArgs {
+    const kvsnap_span* spans;
+    int nspans;
+    const int64_t* blocks;   // cache block ids
+    const int64_t* packed;   // packed block addresses: gather targets / scatter sources
+    int64_t n;
+    int32_t valid;           // gather: token slots kept in the last block (0: all)
+    uint32_t* crc;           // raw XOR accumulators, zeroed before launch, or null
+    const uint32_t* gate;    // scatter: skip all writes when *gate != 0
+    uint32_t* status;
+};
+
+template <int VEC, int MODE>
+__global__ void __launch_bounds__(256) span_kernel(SpanArgs a) {
+    __shared__ uint32_t tb[Vec<VEC>::kTables * 256];
+    const bool crc = a.crc != nullptr;
+    if (crc) load_tables<VEC>(tb);
+    __syncthreads();
+    if (MODE == kScatter && a.gate && *a.gate) return;
+    const int lane = threadIdx.x & 31;
+    const uint32_t lane_shift = crc ? dev_xpow8n((uint64_t)VEC * (31 - lane)) : 0;
+    const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
+    const int64_t units = a.n * a.nspans;
+    for (int64_t u = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); u < units; u += warps) {
+        const int64_t i = u / a.nspans;
+        const kvsnap_span sp = a.spans[u - i * a.nspans];
+        const int64_t block = a.blocks[i];
+        if (block < 0 || block >= sp.nblocks) {
+            if (lane == 0) flag(a.status, KVSNAP_DP_BAD_BLOCK);
+            continue;
+        }
+        const int64_t packed = a.packed[i] + sp.offset;
+        const int64_t cache = sp.base + block * sp.pitch;
+        if ((packed | cache | sp.bytes) & (VEC - 1)) {
+            if (lane == 0) flag(a.status, KVSNAP_DP_MISALIGNED);
+            continue;
+        }
+        const char* src = reinterpret_cast<const char*>(MODE == kGather ? cache : packed);
+        char* dst = reinterpret_cast<char*>(MODE == kGather ? packed : cache);
+        const bool tail = MODE == kGather && a.valid > 0 && i == a.n - 1;
+        uint32_t r;
+        if (crc)
+            r = warp_unit<VEC, true, true>(tb, src, dst, sp.bytes, lane, tail, sp, a.valid);
+        else
+            r = warp_unit<VEC, true, false>(tb, src, dst, sp.bytes, lane, tail, sp, a.valid);
+        if (crc) {
+            r = warp_xor(gf_mulmod(r, gf_mulmod(lane_shift, sp.crc_shift)));
+            if (lane == 0) atomicXor(&a.crc[i], r);
+        }
+    }
+}
+
+// CRC32C of whole packed blocks, in pieces of kPiece bytes per warp.
+constexpr int64_t kPiece = 64 << 10;
+
+template <int VEC>
+__global__ void __launch_bounds__(256) crc_kernel(const int64_t* addrs, int64_t n, int64_t block_bytes,
+                                                  uint32_t* crc, uint32_t* status) {
+    __shared__ uint32_t tb[Vec<VEC>::kTables * 256];
+    load_tables<VEC>(tb);
+    __syncthreads();
+    const int lane = threadIdx.x & 31;
+    const uint32_t lane_shift = dev_xpow8n((uint64_t)VEC * (31 - lane));
+    const int64_t pieces = (block_bytes + kPiece - 1) / kPiece;
+    const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
+    kvsnap_span none{};
+    for (int64_t u = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); u < n * pieces; u += warps) {
+        const int64_t i = u / pieces, p = u - i * pieces;
+        const int64_t at = p * kPiece, len = min(kPiece, block_bytes - at);
+        const int64_t base = addrs[i] + at;
+        if ((base | len) & (VEC - 1)) {
+            if (lane == 0) flag(status, KVSNAP_DP_MISALIGNED);
+            continue;
+        }
+        uint32_t r = warp_unit<VEC, false, true>(tb, reinterpret_cast<const char*>(base), nullptr, len, lane,
+                                                 false, none, 0);
+        const uint32_t after = dev_xpow8n((uint64_t)(block_bytes - at - len));
+        r = warp_xor(gf_mulmod(r, gf_mulmod(lane_shift, after)));
+        if (lane == 0) atomicXor(&crc[i], r);
+    }
+}
+
+// crc[i] <- crc[i] ^ (~0 ^ ~0 * x^(8*block_bytes)): the inverted register and
+// output of the standard CRC32C, applied once per block; then the comparison.
+__global__ void finish_kernel(uint32_t* crc, const uint32_t* expect, int64_t n, uint32_t init_term,
+                              uint32_t* status) {
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    const uint32_t value = crc[i] ^ init_term;
+    crc[i] = value;
+    if (expect && value != expect[i]) flag(status, KVSNAP_DP_CRC_MISMATCH);
+}
+
+// ---- SHA-256 (FIPS 180-4) -----------------------------------------------------
+
+__constant__ uint32_t kSha256K[64] = {
+    0x428a2f98, 0x71374491, 0xb5c0fbcf, 0xe9b5dba5, 0x3956c25b, 0x59f111f1, 0x923f82a4, 0xab1c5ed5,
+    0xd807aa98, 0x12835b01, 0x243185be, 0x550c7dc3, 0x72be5d74, 0x80deb1fe, 0x9bdc06a7, 0xc19bf174,
+    0xe49b69c1, 0xefbe4786, 0x0fc19dc6, 0x240ca1cc, 0x2de92c6f, 0x4a7484aa, 0x5cb0a9dc, 0x76f988da,
+    0x983e5152, 0xa831c66d, 0xb00327c8, 0xbf597fc7, 0xc6e00bf3, 0xd5a79147, 0x06ca6351, 0x14292967,
+    0x27b70a85, 0x2e1b2138, 0x4d2c6dfc, 0x53380d13, 0x650a7354, 0x766a0abb, 0x81c2c92e, 0x92722c85,
+    0xa2bfe8a1, 0xa81a664b, 0xc24b8b70, 0xc76c51a3, 0xd192e819, 0xd6990624, 0xf40e3585, 0x106aa070,
+    0x19a4c116, 0x1e376c08, 0x2748774c, 0x34b0bcb5, 0x391c0cb3, 0x4ed8aa4a, 0x5b9cca4f, 0x682e6ff3,
+    0x748f82ee, 0x78a5636f, 0x84c87814, 0x8cc70208, 0x90befffa, 0xa4506ceb, 0xbef9a3f7, 0xc67178f2};
+
+__device__ __forceinline__ uint32_t rotr(uint32_t x, int n) { return __funnelshift_r(x, x, n); }
+__device__ __forceinline__ uint32_t be32(uint32_t x) { return __byte_perm(x, 0, 0x0123); }
+
+__device__ __forceinline__ void sha256_compress(uint32_t h[8], uint32_t w[16]) {
+    uint32_t a = h[0], b = h[1], c = h[2], d = h[3], e = h[4], f = h[5], g = h[6], k = h[7];
+#pragma unroll
+    for (int t = 0; t < 64; ++t) {
+        if (t >= 16) {
+            const uint32_t x = w[(t + 1) & 15], y = w[(t + 14) & 15];
+            const uint32_t s0 = rotr(x, 7) ^ rotr(x, 18) ^ (x >> 3);
+            const uint32_t s1 = rotr(y, 17) ^ rotr(y, 19) ^ (y >> 10);
+            w[t & 15] += s0 + w[(t + 9) & 15] + s1;
+        }
+        const uint32_t t1 = k + (rotr(e, 6) ^ rotr(e, 11) ^ rotr(e, 25)) + ((e & f) ^ (~e & g)) + kSha256K[t] +
+                            w[t & 15];
+        const uint32_t t2 = (rotr(a, 2) ^ rotr(a, 13) ^ rotr(a, 22)) + ((a & b) ^ (a & c) ^ (b & c));
+        k = g;
+        g = f;
+        f = e;
+        e = d + t1;
+        d = c;
+        c = b;
+        b = a;
+        a = t1 + t2;
+    }
+    h[0] += a; h[1] += b; h[2] += c; h[3] += d; h[4] += e; h[5] += f; h[6] += g; h[7] += k;
+}
+
+// One lane per block: the whole 64-byte chunks straight from memory (the next
+// chunk's loads issued before the current chunk's rounds), then the padded tail.
+__global__ void __launch_bounds__(32) sha256_kernel(const int64_t* addrs, int64_t n, int64_t block_bytes,
+                                                    uint8_t* out) {
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    const char* p = reinterpret_cast<const char*>(addrs[i]);
+    uint32_t h[8] = {0x6a09e667, 0xbb67ae85, 0x3c6ef372, 0xa54ff53a, 0x510e527f, 0x9b05688c, 0x1f83d9ab, 0x5be0cd19};
+    uint32_t w[16];
+    const int64_t chunks = block_bytes / 64;
+    if ((reinterpret_cast<uintptr_t>(p) & 15) == 0 && chunks > 0) {
+        uint4 next[4];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) next[q] = __ldcs(reinterpret_cast<const uint4*>(p) + q);
+        for (int64_t c = 0; c < chunks; ++c) {
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                w[4 * q + 0] = be32(next[q].x);
+                w[4 * q + 1] = be32(next[q].y);
+                w[4 * q + 2] = be32(next[q].z);
+                w[4 * q + 3] = be32(next[q].w);
+            }
+            if (c + 1 < chunks) {
+#pragma unroll
+                for (int q = 0; q < 4; ++q) next[q] = __ldcs(reinterpret_cast<const uint4*>(p + 64 * (c + 1)) + q);
+            }
+            sha256_compress(h, w);
+        }
+    } else {
+        const unsigned char* b = reinterpret_cast<const unsigned char*>(p);
+        for (int64_t c = 0; c < chunks; ++c) {
+            for (int j = 0; j < 16; ++j) {
+                const unsigned char* q = b + 64 * c + 4 * j;
+                w[j] = (uint32_t(q[0]) << 24) | (uint32_t(q[1]) << 16) | (uint32_t(q[2]) << 8) | q[3];
+            }
+            sha256_compress(h, w);
+        }
+    }
+    // Tail: the remaining bytes, 0x80, zeros, then the bit length big-endian.
+    const int rest = int(block_bytes - chunks * 64);
+    const unsigned char* tailp = reinterpret_cast<const unsigned char*>(p) + chunks * 64;
+    const uint64_t bits = uint64_t(block_bytes) * 8;
+    for (int round = 0; round < (rest < 56 ? 1 : 2); ++round) {
+        for (int j = 0; j < 16; ++j) {
+            uint32_t word = 0;
+            for (int q = 0; q < 4; ++q) {
+                const int at = round * 64 + 4 * j + q;
+                const uint32_t byte = at < rest ? tailp[at] : (at == rest ? 0x80u : 0u);
+                word = (word << 8) | byte;
+            }
+            w[j] = word;
+        }
+        if (round == (rest < 56 ? 0 : 1)) {
+            w[14] = uint32_t(bits >> 32);
+            w[15] = uint32_t(bits);
+        }
+        sha256_compress(h, w);
+    }
+    uint32_t* o = reinterpret_cast<uint32_t*>(out + 32 * i);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) o[j] = be32(h[j]);
+}
+
+// ---- the reference restore kernel's interface ------------------------------------
+
+__global__ void __launch_bounds__(256) copy_host_blocks_kernel(const int64_t* sources, const int64_t* blocks,
+                                                               int64_t n_blocks, const int64_t* offsets,
+                                                               const int64_t* bases, const int64_t* pitches,
+                                                               const int64_t* words, int64_t n_layers) {
+    const int lane = threadIdx.x & 31;
+    const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
+    for (int64_t j = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); j < n_blocks * n_layers;
+         j += warps) {
+        const int64_t b = j / n_layers, l = j - b * n_layers;
+        const char* src = reinterpret_cast<const char*>(sources[b] + offsets[l]);
+        char* dst = reinterpret_cast<char*>(bases[l] + blocks[b] * pitches[l]);
+        const int64_t len = words[l] * 8;
+        if (((reinterpret_cast<uintptr_t>(src) | reinterpret_cast<uintptr_t>(dst) | len) & 15) == 0) {
+            for (int64_t at = 16 * lane; at < len; at += 512)
+                *reinterpret_cast<uint4*>(dst + at) = __ldcs(reinterpret_cast<const uint4*>(src + at));
+        } else {
+            for (int64_t at = 8 * lane; at < len; at += 256)
+                *reinterpret_cast<uint2*>(dst + at) = __ldcs(reinterpret_cast<const uint2*>(src + at));
+        }
+    }
+}
+
+// ---- host side ----------------------------------------------------------------------
+
+struct Fail {
+    const char* what;
+};
+
+void check(cudaError_t rc) {
+    if (rc != cudaSuccess) throw Fail{cudaGetErrorString(rc)};
+}
+
+template <typename F>
+int guarded(F&& body) {
+    try {
+        body();
+        return 0;
+    } catch (const Fail& f) {
+        kvsnap_internal_set_error(f.what);
+        return -1;
+    }
+}
+
+// Make the stream's device current and return its SM count.
+int enter_stream(uintptr_t stream) {
+    int device = 0;
+    if (stream) {
+        check(cudaStreamGetDevice(reinterpret_cast<cudaStream_t>(stream), &device));
+        check(cudaSetDevice(device));
+    } else {
+        check(cudaGetDevice(&device));
+    }
+    int sms = 0;
+    check(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device));
+    return sms;
+}
+
+int grid_for(int64_t warps_of_work, int ctas, int sms) {
+    if (ctas > 0) return ctas;
+    int64_t want = (warps_of_work + 7) / 8;   // 8 warps a CTA
+    int64_t cap = 4LL * sms;
+    return int(want < 1 ? 1 : (want > cap ? cap : want));
+}
+
+uint32_t init_term(uint64_t block_bytes) { return ~0u ^ gf_mulmod(~0u, gf_xpow8n(block_bytes)); }
+
+void finish(uint32_t* crc, const uint32_t* expect, int64_t n, uint64_t block_bytes, uint32_t* status,
+            cudaStream_t s) {
+    finish_kernel<<<int((n + 255) / 256), 256, 0, s>>>(crc, expect, n, init_term(block_bytes), status);
+    check(cudaGetLastError());
+}
+
+}  // namespace
+
+extern "C" int kvsnap_dp_abi_version() { return KVSNAP_DP_ABI_VERSION; }
+
+extern "C" uint32_t kvsnap_dp_crc32c_host(const void* data, size_t size, uint32_t prior) {
+    // Bytewise, from the tables: a self-check of the device tables' generator.
+    static const CrcTables tables = make_tables();
+    const unsigned char* p = static_cast<const unsigned char*>(data);
+    uint32_t r = ~prior;
+    for (size_t i = 0; i < size; ++i) r = tables.t[0][(r ^ p[i]) & 0xFFu] ^ (r >> 8);
+    return ~r;
+}
+
+extern "C" int kvsnap_dp_plan(kvsnap_span* spans, int nspans, uint64_t* block_bytes) {
+    return guarded([&] {
+        if (!spans || nspans <= 0 || !block_bytes) throw Fail{"plan needs at least one span"};
+        uint64_t total = 0;
+        for (int s = 0; s < nspans; ++s) {
+            if (spans[s].bytes <= 0) throw Fail{"span without bytes"};
+            spans[s].offset = int64_t(total);
+            total += uint64_t(spans[s].bytes);
+        }
+        for (int s = 0; s < nspans; ++s)
+            spans[s].crc_shift = gf_xpow8n(total - uint64_t(spans[s].offset) - uint64_t(spans[s].bytes));
+        *block_bytes = total;
+    });
+}
+
+namespace {
+
+template <int MODE>
+int launch_spans(const kvsnap_span* spans, int nspans, uint64_t block_bytes, const int64_t* blocks,
+                 const int64_t* packed, int64_t n, int32_t valid, uint32_t* crc, const uint32_t* expect,
+                 const uint32_t* gate, uint32_t* status, int vec, int ctas, uintptr_t stream) {
+    return guarded([&] {
+        if (n < 0 || nspans <= 0 || !spans) throw Fail{"invalid span table"};
+        if (vec != 16 && vec != 8) throw Fail{"vector width must be 16 or 8"};
+        if (n == 0) return;
+        if (!blocks || !packed) throw Fail{"block and address tables are required"};
+        if (expect && !crc) throw Fail{"verifying needs a CRC output"};
+        const int sms = enter_stream(stream);
+        cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+        if (crc) check(cudaMemsetAsync(crc, 0, sizeof(uint32_t) * size_t(n), s));
+        SpanArgs a{spans, nspans, blocks, packed, n, valid, crc, gate, status};
+        const int grid = grid_for(n * nspans, ctas, sms);
+        if (vec == 16)
+            span_kernel<16, MODE><<<grid, 256, 0, s>>>(a);
+        else
+            span_kernel<8, MODE><<<grid, 256, 0, s>>>(a);
+        check(cudaGetLastError());
+        if (crc) finish(crc, expect, n, block_bytes, status, s);
+    });
+}
+
+}  // namespace
+
+extern "C" int kvsnap_dp_gather(const kvsnap_span* spans, int nspans, uint64_t block_bytes, const int64_t* blocks,
+                                const int64_t* targets, int64_t n, int32_t valid_tokens, uint32_t* crc_out,
+                                uint32_t* status, int vec, int ctas, uintptr_t stream) {
+    if (valid_tokens < 0) {
+        kvsnap_internal_set_error("valid_tokens must be non-negative");
+        return -1;
+    }
+    return launch_spans<kGather>(spans, nspans, block_bytes, blocks, targets, n, valid_tokens, crc_out, nullptr,
+                                 nullptr, status, vec, ctas, stream);
+}
+
+extern "C" int kvsnap_dp_scatter(const kvsnap_span* spans, int nspans, uint64_t block_bytes,
+                                 const int64_t* sources, const int64_t* blocks, int64_t n, uint32_t* crc_out,
+                                 const uint32_t* expect, const uint32_t* gate, uint32_t* status, int vec,
+                                 int ctas, uintptr_t stream) {
+    return launch_spans<kScatter>(spans, nspans, block_bytes, blocks, sources, n, 0, crc_out, expect, gate,
+                                  status, vec, ctas, stream);
+}
+
+extern "C" int kvsnap_dp_crc32c(const int64_t* addrs, int64_t n, uint64_t block_bytes, uint32_t* crc_out,
+                                const uint32_t* expect, uint32_t* status, int vec, int ctas, uintptr_t stream) {
+    return guarded([&] {
+        if (n < 0 || vec != 16 && vec != 8) throw Fail{"invalid CRC request"};
+        if (n == 0) return;
+        if (!addrs || !crc_out || block_bytes == 0) throw Fail{"CRC needs addresses, output and a block size"};
+        const int sms = enter_stream(stream);
+        cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+        check(cudaMemsetAsync(crc_out, 0, sizeof(uint32_t) * size_t(n), s));
+        const int64_t pieces = (int64_t(block_bytes) + kPiece - 1) / kPiece;
+        const int grid = grid_for(n * pieces, ctas, sms);
+        if (vec == 16)
+            crc_kernel<16><<<grid, 256, 0, s>>>(addrs, n, int64_t(block_bytes), crc_out, status);
+        else
+            crc_kernel<8><<<grid, 256, 0, s>>>(addrs, n, int64_t(block_bytes), crc_out, status);
+        check(cudaGetLastError());
+        finish(crc_out, expect, n, block_bytes, status, s);
+    });
+}
+
+extern "C" int kvsnap_dp_sha256(const int64_t* addrs, int64_t n, uint64_t block_bytes, uint8_t* out,
+                                uintptr_t stream) {
+    return guarded([&] {
+        if (n < 0) throw Fail{"invalid digest request"};
+        if (n == 0) return;
+        if (!addrs || !out) throw Fail{"digests need addresses and an output"};
+        if (reinterpret_cast<uintptr_t>(out) & 3) throw Fail{"digest output must be 4-byte aligned"};
+        enter_stream(stream);
+        cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+        sha256_kernel<<<int((n + 31) / 32), 32, 0, s>>>(addrs, n, int64_t(block_bytes), out);
+        check(cudaGetLastError());
+    });
+}
+
+extern "C" int kvsnap_dp_copy_host_blocks(const int64_t* sources, const int64_t* blocks, int64_t n_blocks,
+                                          const int64_t* layer_offsets, const int64_t* layer_bases,
+                                          const int64_t* layer_pitches, const int64_t* layer_words,
+                                          int64_t n_layers, int ctas, uintptr_t stream) {
+    return guarded([&] {
+        if (n_blocks < 0 || n_layers < 0) throw Fail{"negative table size"};
+        if (n_blocks == 0 || n_layers == 0) return;
+        const int sms = enter_stream(stream);
+        cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+        const int grid = grid_for(n_blocks * n_layers, ctas, sms);
+        copy_host_blocks_kernel<<<grid, 256, 0, s>>>(sources, blocks, n_blocks, layer_offsets, layer_bases,
+                                                     layer_pitches, layer_words, n_layers);
+        check(cudaGetLastError());
+    });
+}

@@ -1,0 +1,761 @@
+"""The KV snapshot data plane: a drop-in for kvsnap's ``kvsnap.connector.dataplane``.
+
+Same module surface as the reference (kvsnap/connector/dataplane.py):
+``resolve_cuda_library``, ``copy_host_blocks``, ``PinnedCapacityError``,
+``CudaPool``, ``PinnedAllocation`` and ``TorchBlockDataPlane`` with the
+constructor, attributes (``caches``, ``block_size``, ``layers``,
+``block_bytes``, ``pool``) and methods the connector uses (``warm_up``,
+``staging``, ``producer_event``, ``wait_on_engine_stream``, ``load_scatter``,
+``save_gather``, ``close``), the same argument meaning, return values and
+exceptions. The copies run in sm_100a kernels from ``_cuda_native.so``
+(include/kvsnap_cuda.h) instead of torch ops and a Triton kernel, and the
+checksums the store needs are computed on the GPU in the same call:
+
+* ``save_gather(..., digests=out)`` fills ``out`` with ``(sha256 hex, crc32c)``
+  per block, the values kvsnap/store/store.py:616-629 and
+  kvsnap/connector/volatile.py:141-151 compute on the host;
+* ``load_scatter(..., expected_crc32c=crcs)`` checks every block's CRC32C on
+  the GPU before any KV byte is written (the check kvsnap/store/store.py:717-718
+  runs on the loader thread), raising :class:`CorruptBlockError` on a mismatch.
+
+There is no CPU path: without the CUDA library or a CUDA device these raise.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+import threading
+from contextlib import contextmanager
+from importlib.machinery import EXTENSION_SUFFIXES
+from pathlib import Path
+
+from . import _abi
+
+_NATIVE = Path(__file__).resolve().parent / "_native"
+
+
+def resolve_cuda_library(library=None):
+    """The C ABI library's path, without loading it or initialising CUDA (reference dataplane.py:12-25).
+
+    ``library`` or ``KVSNAP_CUDA_LIBRARY`` wins; otherwise this package's
+    ``_native/_cuda_native<suffix>`` built by ``python -m kvsnap_b200.build``.
+    """
+    override = library or os.environ.get("KVSNAP_CUDA_LIBRARY")
+    if override:
+        return Path(override)
+    for suffix in EXTENSION_SUFFIXES:
+        candidate = _NATIVE / ("_cuda_native" + suffix)
+        if candidate.is_file():
+            return candidate
+    packaged = sorted(_NATIVE.glob("_cuda_native*.so"))
+    return packaged[0] if packaged else _NATIVE / "_cuda_native.so"
+
+
+def _load(library=None):
+    path = resolve_cuda_library(library)
+    if not path.is_file():
+        raise RuntimeError(f"kvsnap CUDA library not found at {path}; build it with python -m kvsnap_b200.build")
+    lib = _abi.load(path, _abi.POOL_API)
+    _abi.declare(lib, _abi.POOL_EXTRA, required=False)
+    _abi.declare(lib, _abi.DP_API, required=False)
+    return lib
+
+
+def _dp(lib):
+    """The library's data-plane entry points, or an error naming what is missing."""
+    if not hasattr(lib, "kvsnap_dp_abi_version") or lib.kvsnap_dp_abi_version.restype is None:
+        raise RuntimeError("the CUDA library has no data-plane kernels; rebuild with python -m kvsnap_b200.build")
+    if lib.kvsnap_dp_abi_version() != _abi.DP_ABI_VERSION:
+        raise RuntimeError("unsupported kvsnap data-plane ABI; rebuild with python -m kvsnap_b200.build")
+    return lib
+
+
+def copy_host_blocks(sources, blocks, layer_offsets, layer_bases, layer_pitches, layer_words):
+    """The reference restore kernel's launch (copy_kernel.py:43-49), on the current stream.
+
+    ``sources``: address of each packed block (pinned host or device memory);
+    ``blocks``: its target block id; the ``layer_*`` tables: per layer, its
+    offset in a packed block, the cache's base address and block pitch in bytes,
+    and its span in 8-byte words. All int64 CUDA tensors.
+    """
+    import torch
+    lib = _dp(_load())
+    tables = (sources, blocks, layer_offsets, layer_bases, layer_pitches, layer_words)
+    for table in tables:
+        if table.dtype != torch.int64 or not table.is_cuda or not table.is_contiguous():
+            raise ValueError("copy_host_blocks takes contiguous int64 CUDA tensors")
+    if sources.numel() != blocks.numel():
+        raise ValueError("one source per block is required")
+    stream = torch.cuda.current_stream(sources.device).cuda_stream
+    rc = lib.kvsnap_dp_copy_host_blocks(sources.data_ptr(), blocks.data_ptr(), sources.numel(),
+                                        layer_offsets.data_ptr(), layer_bases.data_ptr(), layer_pitches.data_ptr(),
+                                        layer_words.data_ptr(), layer_offsets.numel(), 0, stream)
+    if rc < 0:
+        raise RuntimeError(lib.kvsnap_cuda_error().decode())
+
+
+class PinnedCapacityError(MemoryError):
+    """The pinned pool cannot fit a reservation. Nothing was copied."""
+
+
+class CorruptBlockError(ValueError):
+    """A packed block's CRC32C differs from the one recorded for it. No KV byte was written."""
+
+    def __init__(self, message, blocks=()):
+        super().__init__(message)
+        self.blocks = list(blocks)
+
+
+class CudaPool:
+    """A pinned host arena with one copy stream, over the C ABI v2 (reference dataplane.py:38-131)."""
+
+    def __init__(self, capacity_bytes: int, device: int = 0, library=None):
+        self._pid = os.getpid()
+        self._lock = threading.RLock()
+        # Python owners of allocations the native pool may still be copying; see close().
+        self._allocations = {}
+        self.lib = _load(library)
+        self.abi_version = self.lib.kvsnap_pool_abi_version()
+        if self.abi_version != _abi.POOL_ABI_VERSION:
+            raise RuntimeError("unsupported kvsnap CUDA pool ABI; rebuild both CUDA and torch extensions")
+        self.device = device
+        self.handle = self.lib.kvsnap_pool_create(capacity_bytes, device)
+        if not self.handle:
+            raise RuntimeError(self.lib.kvsnap_cuda_error().decode())
+
+    def check(self, result):
+        if result < 0:
+            raise RuntimeError(self.lib.kvsnap_cuda_error().decode())
+        return result
+
+    def reserve(self, size):
+        with self.operation():
+            ident, ptr = C.c_uint64(), C.c_void_p()
+            if self.lib.kvsnap_pool_reserve(self.handle, size, C.byref(ident), C.byref(ptr)) < 0:
+                message = self.lib.kvsnap_cuda_error().decode()
+                if "pinned capacity exhausted" in message:
+                    raise PinnedCapacityError(message)
+                raise RuntimeError(message)
+            allocation = PinnedAllocation(self, ident.value, ptr.value, size)
+            self._allocations[ident.value] = allocation
+            return allocation
+
+    @contextmanager
+    def operation(self):
+        if self._pid != os.getpid():
+            raise RuntimeError("CUDA pools must not be inherited across fork")
+        with self._lock:
+            if not self.handle:
+                raise RuntimeError("pool closed")
+            yield
+
+    def close(self):
+        if self._pid != os.getpid():
+            raise RuntimeError("CUDA pools must not be inherited across fork")
+        with self._lock:
+            if self.handle:
+                self.check(self.lib.kvsnap_pool_close_checked(self.handle))
+                self.handle = None
+                for allocation in self._allocations.values():
+                    allocation.closed = True
+                    if hasattr(allocation, "_tensor_references"):
+                        allocation._tensor_references.clear()
+                self._allocations.clear()
+
+    def stream_handle(self) -> int:
+        """The copy stream's handle (borrowed; valid while the pool is open)."""
+        with self.operation():
+            handle = C.c_size_t()
+            self.check(self.lib.kvsnap_pool_copy_stream(self.handle, C.byref(handle)))
+            if not handle.value:
+                raise RuntimeError("native copy stream handle is invalid")
+            return handle.value
+
+    @contextmanager
+    def borrow_copy_stream(self):
+        """Borrow the copy stream's handle; the context excludes a concurrent close (reference dataplane.py:110-131)."""
+        with self.operation():
+            handle = C.c_size_t()
+            self.check(self.lib.kvsnap_pool_copy_stream(self.handle, C.byref(handle)))
+            if not handle.value:
+                raise RuntimeError("native copy stream handle is invalid")
+            yield handle.value
+
+
+class PinnedAllocation:
+    """One reservation in a :class:`CudaPool` (reference dataplane.py:134-211)."""
+
+    def __init__(self, pool, ident, pointer, size):
+        self.pool, self.ident, self.pointer, self.size = pool, ident, pointer, size
+        self.closed = False
+
+    def _open(self):
+        if self.closed or not self.pool.handle:
+            raise RuntimeError("pinned allocation closed")
+
+    @contextmanager
+    def operation(self):
+        with self.pool.operation():
+            self._open()
+            yield
+
+    def copy(self, device_ptr, size, offset=0, *, to_host, producer_stream=0):
+        with self.operation():
+            if min(size, offset, device_ptr, producer_stream) < 0:
+                raise ValueError("negative copy argument")
+            self.pool.check(self.pool.lib.kvsnap_pool_copy(
+                self.pool.handle, self.ident, offset, device_ptr, size, int(bool(to_host)), producer_stream))
+
+    def copy_2d(self, device_ptr, device_pitch, host_offset, host_pitch, width, height, *,
+                to_host, producer_stream=0):
+        """``height`` rows of ``width`` bytes between strided device and host memory."""
+        with self.operation():
+            if min(device_ptr, device_pitch, host_offset, host_pitch, width, height, producer_stream) < 0:
+                raise ValueError("negative copy argument")
+            self.pool.check(self.pool.lib.kvsnap_pool_copy_2d(
+                self.pool.handle, self.ident, host_offset, host_pitch, device_ptr, device_pitch,
+                width, height, int(bool(to_host)), producer_stream))
+
+    def mark(self):
+        """Fence work queued on the pool's copy stream so far under this allocation's wait/ready/release.
+
+        Kernels that read or write the allocation in place run on that stream;
+        marking after them makes the allocation's lifetime cover them.
+        """
+        with self.operation():
+            self.pool.check(self.pool.lib.kvsnap_pool_mark(self.pool.handle, self.ident))
+
+    def wait(self):
+        with self.operation():
+            self.pool.check(self.pool.lib.kvsnap_pool_wait(self.pool.handle, self.ident))
+            if hasattr(self, "_tensor_references"):
+                self._tensor_references.clear()
+
+    def ready(self):
+        with self.operation():
+            return bool(self.pool.check(self.pool.lib.kvsnap_pool_ready(self.pool.handle, self.ident)))
+
+    def read(self):
+        with self.operation():
+            self.wait()
+            return C.string_at(self.pointer, self.size)
+
+    def read_range(self, offset, size):
+        with self.operation():
+            self.wait()
+            if type(offset) is not int or type(size) is not int or offset < 0 or size < 0 or offset + size > self.size:
+                raise ValueError("pinned read outside allocation")
+            return C.string_at(self.pointer + offset, size)
+
+    def zero(self, offset, size):
+        with self.operation():
+            self.wait()
+            if offset < 0 or size < 0 or offset + size > self.size:
+                raise ValueError("pinned zero outside allocation")
+            C.memset(self.pointer + offset, 0, size)
+
+    def write(self, data):
+        with self.operation():
+            self.wait()
+            if len(data) != self.size:
+                raise ValueError("pinned allocation length mismatch")
+            C.memmove(self.pointer, data, self.size)
+
+    def close(self):
+        if self.pool._pid != os.getpid():
+            raise RuntimeError("CUDA pools must not be inherited across fork")
+        with self.pool._lock:
+            if not self.closed and self.pool.handle:
+                self.pool.check(self.pool.lib.kvsnap_pool_release(self.pool.handle, self.ident))
+            self.closed = True
+            self.pool._allocations.pop(self.ident, None)
+            if hasattr(self, "_tensor_references"):
+                self._tensor_references.clear()
+
+
+def _split_paged(caches, block_size):
+    """Registered 4-D views: a 5-D ``[2, B, block_size, H, D]`` layer becomes ``name.k`` / ``name.v``.
+
+    Both are ``t[i].permute(0, 2, 1, 3)``, a [B, H, N, D] view of [B, N, H, D]
+    storage, K before V in name order: the registration under which the
+    reference's 4-D data plane packs a paged FlashAttention cache.
+    """
+    views = {}
+    for name, tensor in caches.items():
+        shape = tuple(getattr(tensor, "shape", ()))
+        if getattr(tensor, "ndim", 0) == 5 and shape[0] == 2 and shape[2] == block_size:
+            views[f"{name}.k"] = tensor[0].permute(0, 2, 1, 3)
+            views[f"{name}.v"] = tensor[1].permute(0, 2, 1, 3)
+        else:
+            views[name] = tensor
+    return views
+
+
+def _u32(values):
+    """Python ints in [0, 2**32) as the int32 bit patterns a torch int32 tensor holds."""
+    return [v - (1 << 32) if v >= 1 << 31 else v for v in values]
+
+
+class TorchBlockDataPlane:
+    """Packed physical blocks: layer-name order, dense [H,N,C] stride permutations (reference dataplane.py:214-249).
+
+    The actual layout is recorded and compared; unsupported views fail closed.
+    Allocations stay live until the copies that touch them complete, including
+    on error paths.
+
+    ``save_mode``: ``"staged"`` gathers into device memory and moves the packed
+    blocks to pinned memory with the copy engine (the default, and always
+    used when digests are requested); ``"direct"`` has the gather kernel
+    write the pinned blocks in place over the host link. ``restore_mode``:
+    ``"direct"`` has the scatter kernel read pinned blocks in place (the
+    default); ``"staged"`` copies them to device memory with the copy engine
+    first. A restore with ``expected_crc32c`` is always staged, so the check
+    completes before any KV byte changes.
+    """
+
+    save_mode = "staged"
+    restore_mode = "direct"
+
+    def __init__(self, caches, block_size, capacity_bytes, *, save_mode=None, restore_mode=None, ctas=0):
+        import torch
+        if not caches:
+            raise ValueError("empty KV cache registration")
+        self.torch = torch
+        self.caches = dict(sorted(_split_paged(caches, block_size).items()))
+        self.block_size = block_size
+        self.layers = []
+        device = next(iter(self.caches.values())).device
+        for name, tensor in self.caches.items():
+            if tensor.device != device or tensor.device.type != "cuda":
+                raise ValueError("one CUDA device required")
+            if tensor.ndim != 4 or tensor.shape[2] != block_size or tensor.stride(3) != 1:
+                raise ValueError(f"unsupported KV layout for {name}: need dense [B,H,N,C] blocks with contiguous C")
+            # A block must be one dense span: its H/N axes may be permuted (vLLM's
+            # LBNHC storage seen as BHNC) but may not leave holes or overlap.
+            dense = 1
+            for stride, size in sorted((tensor.stride(i), tensor.shape[i]) for i in (1, 2, 3) if tensor.shape[i] > 1):
+                if stride != dense:
+                    raise ValueError(f"unsupported KV layout for {name}: block has holes or overlapping axes")
+                dense *= size
+            if tensor.stride(0) < dense:
+                raise ValueError(f"unsupported KV layout for {name}: overlapping blocks")
+            self.layers.append({"name": name, "shape": list(tensor.shape[1:]),
+                                "dtype": str(tensor.dtype), "stride": list(tensor.stride()[1:]),
+                                "bytes": tensor[0].numel() * tensor.element_size()})
+        self.block_bytes = sum(layer["bytes"] for layer in self.layers)
+        self.save_mode = save_mode or self.save_mode
+        self.restore_mode = restore_mode or self.restore_mode
+        if self.save_mode not in ("staged", "direct") or self.restore_mode not in ("staged", "direct"):
+            raise ValueError("save_mode and restore_mode are 'staged' or 'direct'")
+        self.ctas = ctas
+        self.pool = CudaPool(capacity_bytes, device.index)
+
+    # ---- registration-time tables ------------------------------------------------------------
+
+    def _device(self):
+        return next(iter(self.caches.values())).device
+
+    def _spans(self):
+        """The device span table (include/kvsnap_cuda.h ``kvsnap_span``), built on first use."""
+        if getattr(self, "_span_table", None) is None:
+            torch = self.torch
+            lib = _dp(self.pool.lib)
+            spans = (_abi.Span * len(self.layers))()
+            vec = 16
+            for span, layer, tensor in zip(spans, self.layers, self.caches.values()):
+                size = tensor.element_size()
+                base, pitch = tensor.data_ptr(), tensor.stride(0) * size
+                if pitch % 8 or base % 8 or layer["bytes"] % 8:
+                    raise ValueError(f"KV layer {layer['name']} is not 8-byte aligned for the scatter path")
+                if pitch % 16 or base % 16 or layer["bytes"] % 16:
+                    vec = 8
+                span.base, span.pitch, span.bytes = base, pitch, layer["bytes"]
+                span.token_pitch = tensor.stride(2) * size
+                span.tokens, span.row_bytes = tensor.shape[2], tensor.shape[3] * size
+                span.nblocks = tensor.shape[0]
+            total = C.c_uint64()
+            if lib.kvsnap_dp_plan(spans, len(spans), C.byref(total)) < 0:
+                raise RuntimeError(lib.kvsnap_cuda_error().decode())
+            if total.value != self.block_bytes:
+                raise RuntimeError("packed block size disagrees with the registered layers")
+            host = torch.frombuffer(bytearray(bytes(spans)), dtype=torch.uint8)
+            self._span_vec = vec
+            self._min_blocks = min(t.shape[0] for t in self.caches.values())
+            self._span_table = host.to(self._device())
+            self._sha_stream = torch.cuda.Stream(self._device())
+        return self._span_table
+
+    def _scatter_targets(self):
+        """Build the tables on first use and borrow the pool's copy stream as a torch stream."""
+        self._spans()
+        if getattr(self, "_copy_stream", None) is None:
+            with self.pool.borrow_copy_stream() as handle:
+                self._copy_stream = self.torch.cuda.ExternalStream(handle, device=self._device())
+        return self._copy_stream
+
+    def _load_tables(self):
+        """Per layer, as int64 device tensors: its offset in a packed block, its cache's base address and
+        block pitch in bytes, and its span in 8-byte words (the tables of :func:`copy_host_blocks`)."""
+        if getattr(self, "_tables", None) is None:
+            self._scatter_targets()
+            columns, offset = ([], [], [], []), 0
+            for layer, tensor in zip(self.layers, self.caches.values()):
+                columns[0].append(offset)
+                columns[1].append(tensor.data_ptr())
+                columns[2].append(tensor.stride(0) * tensor.element_size())
+                columns[3].append(layer["bytes"] // 8)
+                offset += layer["bytes"]
+            self._tables = tuple(self.torch.tensor(c, dtype=self.torch.int64, device=self._device()) for c in columns)
+        return self._tables
+
+    def warm_up(self):
+        """Build the tables and load every kernel once at registration, not on the first save or restore.
+
+        Nothing is written to the KV cache: the gather reads block 0 into a
+        scratch buffer, and the scatter runs gated shut.
+        """
+        torch = self.torch
+        tables = self._load_tables()
+        spans = self._spans()
+        lib = _dp(self.pool.lib)
+        device = self._device()
+        with torch.cuda.stream(self._copy_stream):
+            stream = self._copy_stream.cuda_stream
+            scratch = torch.empty(self.block_bytes, dtype=torch.uint8, device=device)
+            table = torch.tensor([0, scratch.data_ptr()], dtype=torch.int64, device=device)
+            crc = torch.empty(1, dtype=torch.int32, device=device)
+            digest = torch.empty(32, dtype=torch.uint8, device=device)
+            gate = torch.ones(1, dtype=torch.int32, device=device)
+            status = torch.zeros(1, dtype=torch.int32, device=device)
+            vec = self._span_vec
+            calls = [
+                lib.kvsnap_dp_gather(spans.data_ptr(), len(self.layers), self.block_bytes, table.data_ptr(),
+                                     table.data_ptr() + 8, 1, 0, crc.data_ptr(), status.data_ptr(), vec,
+                                     self.ctas, stream),
+                lib.kvsnap_dp_scatter(spans.data_ptr(), len(self.layers), self.block_bytes, table.data_ptr() + 8,
+                                      table.data_ptr(), 1, 0, 0, gate.data_ptr(), status.data_ptr(), vec, self.ctas,
+                                      stream),
+                lib.kvsnap_dp_crc32c(table.data_ptr() + 8, 1, self.block_bytes, crc.data_ptr(), 0,
+                                     status.data_ptr(), vec, self.ctas, stream),
+                lib.kvsnap_dp_sha256(table.data_ptr() + 8, 1, self.block_bytes, digest.data_ptr(), stream),
+            ]
+            if min(calls) < 0:
+                raise RuntimeError(lib.kvsnap_cuda_error().decode())
+            empty = torch.zeros(1, dtype=torch.int64, device=device)
+            copy_host_blocks(empty[:0], empty[:0], *tables)
+        self._copy_stream.synchronize()
+        if int(status.item()):
+            raise RuntimeError(f"data-plane warm-up reported status {int(status.item())}")
+
+    # ---- engine stream -----------------------------------------------------------------------
+
+    def _validate_ids(self, ids):
+        if getattr(self, "_min_blocks", None) is None:
+            self._min_blocks = min(t.shape[0] for t in self.caches.values())
+        limit = self._min_blocks
+        for i in ids:
+            if type(i) is not int or i < 0 or i >= limit:
+                raise ValueError("GPU block id out of range")
+
+    def producer_event(self):
+        """A CUDA event recorded now on the engine's current stream."""
+        event = self.torch.cuda.Event()
+        event.record(self.torch.cuda.current_stream(self._device()))
+        return event
+
+    def wait_on_engine_stream(self, event):
+        """Make the engine's current stream wait, on the GPU, for ``event``."""
+        self.torch.cuda.current_stream(self._device()).wait_event(event)
+
+    @contextmanager
+    def staging(self, nblocks):
+        """A packed pinned buffer for ``nblocks`` blocks, released (after its copies fence) on exit."""
+        allocation = self.pool.reserve(self.block_bytes * nblocks)
+        try:
+            yield allocation
+        finally:
+            allocation.close()
+
+    # ---- helpers ------------------------------------------------------------------------------
+
+    def _vec_for(self, addresses):
+        if self._span_vec == 16 and all(a % 16 == 0 for a in addresses):
+            return 16
+        if any(a % 8 for a in addresses):
+            raise ValueError("packed blocks must be 8-byte aligned")
+        return 8
+
+    def _check(self, rc):
+        if rc < 0:
+            raise RuntimeError(self.pool.lib.kvsnap_cuda_error().decode())
+
+    @staticmethod
+    def _runs(endpoints, first, stop, size):
+        """Runs [i, j) of consecutive blocks whose packed places are adjacent in one allocation."""
+        i = first
+        while i < stop:
+            allocation, offset = endpoints[i]
+            j = i + 1
+            while j < stop and endpoints[j][0] is allocation and endpoints[j][1] == offset + (j - i) * size:
+                j += 1
+            yield i, j
+            i = j
+
+    def _status_error(self, status):
+        value = int(status.item())
+        if value & _abi.BAD_BLOCK:
+            raise RuntimeError("data-plane kernel saw a block id outside its cache")
+        if value & _abi.MISALIGNED:
+            raise RuntimeError("data-plane kernel saw a misaligned address")
+        return value
+
+    # ---- restore ------------------------------------------------------------------------------
+
+    def load_scatter(self, block_ids, sources, *, progress=None, chunk_bytes=64 << 20, expected_crc32c=None):
+        """Copy packed host blocks into ``block_ids`` and wait for it (reference dataplane.py:334-386).
+
+        ``sources[i]`` is ``(allocation, offset)`` holding block i packed, in
+        this pool's pinned memory. One kernel launch per ``chunk_bytes`` of
+        blocks on the pool's copy stream; a ``progress`` list receives
+        ``(None, total bytes)`` and then, as each launch is queued, ``(its
+        completion event, bytes left once it completes)``. Returns the number
+        of launches.
+
+        ``expected_crc32c``: the recorded CRC32C of each block. When given, the
+        blocks are copied to device memory, every CRC is checked there, and only
+        then are the scatter launches queued (and ``progress`` filled): a
+        mismatch raises :class:`CorruptBlockError` with the KV cache untouched
+        and no progress reported, so it stays a miss.
+        """
+        torch = self.torch
+        self._validate_ids(block_ids)
+        if len(sources) != len(block_ids):
+            raise ValueError("one source per block is required")
+        if expected_crc32c is not None and len(expected_crc32c) != len(block_ids):
+            raise ValueError("one expected CRC32C per block is required")
+        if not block_ids:
+            return 0
+        spans = self._spans()
+        stream = self._scatter_targets()
+        lib = _dp(self.pool.lib)
+        device = self._device()
+        n, size = len(block_ids), self.block_bytes
+        per_launch = max(1, chunk_bytes // size)
+        staged = expected_crc32c is not None or self.restore_mode == "staged"
+        launches = 0
+        done = None
+        with self.pool.operation():
+            # The pool lock keeps every source allocation open until the launches are queued.
+            addresses = []
+            for allocation, offset in sources:
+                allocation._open()
+                if offset < 0 or offset + size > allocation.size:
+                    raise ValueError("load source outside its allocation")
+                addresses.append(allocation.pointer + offset)
+            with torch.cuda.stream(stream):
+                status = torch.zeros(1, dtype=torch.int32, device=device)
+                try:
+                    if staged:
+                        stage = torch.empty(n * size, dtype=torch.uint8, device=device)
+                        base = stage.data_ptr()
+                        for i, j in self._runs(sources, 0, n, size):
+                            allocation, offset = sources[i]
+                            allocation.copy(base + i * size, (j - i) * size, offset, to_host=False)
+                        read_from = [base + i * size for i in range(n)]
+                    else:
+                        read_from = addresses
+                    vec = self._vec_for(read_from)
+                    table = torch.tensor(read_from + list(block_ids), dtype=torch.int64).pin_memory().to(
+                        device, non_blocking=True)
+                    if expected_crc32c is not None:
+                        self._verify(table, n, expected_crc32c, status, vec)
+                    if progress is not None:
+                        progress.append((None, n * size))
+                    for first in range(0, n, per_launch):
+                        last = min(n, first + per_launch)
+                        self._check(lib.kvsnap_dp_scatter(
+                            spans.data_ptr(), len(self.layers), size, table[first:].data_ptr(),
+                            table[n + first:].data_ptr(), last - first, 0, 0, 0, status.data_ptr(), vec, self.ctas,
+                            stream.cuda_stream))
+                        launches += 1
+                        done = torch.cuda.Event()
+                        done.record()
+                        if progress is not None:
+                            progress.append((done, (n - last) * size))
+                    if not staged:
+                        for allocation in {id(a): a for a, _ in sources}.values():
+                            allocation.mark()
+                except BaseException:
+                    # A launch that failed part way may still be queued: nothing
+                    # may release the sources before the copy stream drains.
+                    stream.synchronize()
+                    raise
+        done.synchronize()
+        self._status_error(status)
+        return launches
+
+    def _verify(self, table, n, expected, status, vec):
+        """CRC32C of the staged blocks (table[:n]) against ``expected``; raises before any scatter is queued."""
+        torch = self.torch
+        lib = _dp(self.pool.lib)
+        crc = torch.empty(n, dtype=torch.int32, device=table.device)
+        expect = torch.tensor(_u32(expected), dtype=torch.int32).pin_memory().to(table.device, non_blocking=True)
+        self._check(lib.kvsnap_dp_crc32c(table.data_ptr(), n, self.block_bytes, crc.data_ptr(), expect.data_ptr(),
+                                         status.data_ptr(), vec, self.ctas, torch.cuda.current_stream().cuda_stream))
+        flags = int(status.item())          # synchronises the copy stream
+        if flags & _abi.CRC_MISMATCH:
+            got = [v & 0xFFFFFFFF for v in crc.tolist()]
+            bad = [i for i, (g, e) in enumerate(zip(got, expected)) if g != e]
+            raise CorruptBlockError(f"packed block checksum mismatch at block index {bad[0]}", bad)
+        if flags:
+            self._status_error(status)
+
+    # ---- save ---------------------------------------------------------------------------------
+
+    def save_gather(self, block_ids, targets, num_kv_tokens, *, chunk_bytes=64 << 20, digests=None):
+        """Gather blocks on the GPU and land them packed in pinned memory (reference dataplane.py:388-437).
+
+        ``targets[i]`` is ``(allocation, offset)`` receiving block i packed, the
+        layout :meth:`load_scatter` reads. The caller must have fenced the
+        producer stream. Token slots past ``num_kv_tokens`` in the last block
+        are written as zeros, so a snapshot never carries stale KV. Returns the
+        number of device-to-host copies (staged mode: one per run of adjacent
+        targets in one allocation, per ``chunk_bytes`` of blocks) or of kernel
+        launches (direct mode).
+
+        ``digests``: a list that receives ``(sha256 hex, crc32c)`` for each
+        packed block, the store's content id and checksum, computed on the GPU
+        from the same bytes the targets receive.
+        """
+        torch = self.torch
+        self._validate_ids(block_ids)
+        expected = (num_kv_tokens + self.block_size - 1) // self.block_size
+        if len(block_ids) != expected or len(targets) != len(block_ids):
+            raise ValueError("block count does not cover computed tokens")
+        if not block_ids:
+            return 0
+        spans = self._spans()
+        stream = self._scatter_targets()
+        lib = _dp(self.pool.lib)
+        device = self._device()
+        n, size = len(block_ids), self.block_bytes
+        valid = num_kv_tokens % self.block_size
+        per_chunk = max(1, min(n, chunk_bytes // size))
+        direct = self.save_mode == "direct" and digests is None
+        copies = 0
+        with torch.cuda.stream(stream):
+            status = torch.zeros(1, dtype=torch.int32, device=device)
+            crc = torch.empty(n, dtype=torch.int32, device=device) if digests is not None else None
+            if direct:
+                for allocation, offset in targets:
+                    allocation._open()
+                    if offset < 0 or offset + size > allocation.size:
+                        raise ValueError("save target outside its allocation")
+                write_to = [a.pointer + o for a, o in targets]
+            else:
+                stage = torch.empty(n * size, dtype=torch.uint8, device=device)
+                write_to = [stage.data_ptr() + i * size for i in range(n)]
+            vec = self._vec_for(write_to)
+            table = torch.tensor(list(block_ids) + write_to, dtype=torch.int64).pin_memory().to(
+                device, non_blocking=True)
+            try:
+                if direct:
+                    for first in range(0, n, per_chunk):
+                        last = min(n, first + per_chunk)
+                        self._check(lib.kvsnap_dp_gather(
+                            spans.data_ptr(), len(self.layers), size, table[first:].data_ptr(),
+                            table[n + first:].data_ptr(), last - first, valid if last == n else 0, 0,
+                            status.data_ptr(), vec, self.ctas, stream.cuda_stream))
+                        copies += 1
+                    for allocation in {id(a): a for a, _ in targets}.values():
+                        allocation.mark()
+                else:
+                    self._check(lib.kvsnap_dp_gather(
+                        spans.data_ptr(), len(self.layers), size, table.data_ptr(), table[n:].data_ptr(), n, valid,
+                        crc.data_ptr() if crc is not None else 0, status.data_ptr(), vec, self.ctas,
+                        stream.cuda_stream))
+                    if digests is not None:
+                        digest = self._sha256_after(stage, table[n:], n, stream)
+                    for first in range(0, n, per_chunk):
+                        for i, j in self._runs(targets, first, min(n, first + per_chunk), size):
+                            allocation, offset = targets[i]
+                            allocation.copy(stage.data_ptr() + i * size, (j - i) * size, offset, to_host=True)
+                            copies += 1
+                done = torch.cuda.Event()
+                done.record()
+            except BaseException:
+                stream.synchronize()
+                raise
+        done.synchronize()
+        for allocation in {id(a): a for a, _ in targets}.values():
+            allocation.wait()
+        self._status_error(status)
+        if digests is not None:
+            self._sha_stream.synchronize()
+            crcs = [v & 0xFFFFFFFF for v in crc.cpu().tolist()]
+            raw = digest.cpu().numpy().tobytes()
+            digests.extend((raw[32 * i:32 * i + 32].hex(), crcs[i]) for i in range(n))
+        return copies
+
+    def _sha256_after(self, stage, addresses, n, stream):
+        """SHA-256 of the staged blocks on a side stream, after the work queued on ``stream`` so far."""
+        torch = self.torch
+        lib = _dp(self.pool.lib)
+        ready = torch.cuda.Event()
+        ready.record(stream)
+        side = self._sha_stream
+        side.wait_event(ready)
+        with torch.cuda.stream(side):
+            out = torch.empty(n * 32, dtype=torch.uint8, device=addresses.device)
+            self._check(lib.kvsnap_dp_sha256(addresses.data_ptr(), n, self.block_bytes, out.data_ptr(),
+                                             side.cuda_stream))
+        # The staging buffer and tables belong to the copy stream's allocator pool;
+        # keep them from reuse until the side stream is done with them.
+        stage.record_stream(side)
+        addresses.record_stream(side)
+        return out
+
+    # ---- checksums of blocks already in pinned memory ---------------------------------------------
+
+    def digest(self, sources):
+        """``(sha256 hex, crc32c)`` of packed blocks in pinned memory, computed on the GPU.
+
+        ``sources[i]`` is ``(allocation, offset)``; each block is copied to
+        device memory by the copy engine and hashed there. The values of the
+        reference's host ``_digest`` (kvsnap/connector/volatile.py:141-151).
+        """
+        torch = self.torch
+        if not sources:
+            return []
+        self._spans()
+        stream = self._scatter_targets()
+        lib = _dp(self.pool.lib)
+        device = self._device()
+        n, size = len(sources), self.block_bytes
+        with self.pool.operation():
+            for allocation, offset in sources:
+                allocation._open()
+                if offset < 0 or offset + size > allocation.size:
+                    raise ValueError("digest source outside its allocation")
+            with torch.cuda.stream(stream):
+                stage = torch.empty(n * size, dtype=torch.uint8, device=device)
+                for i, j in self._runs(sources, 0, n, size):
+                    allocation, offset = sources[i]
+                    allocation.copy(stage.data_ptr() + i * size, (j - i) * size, offset, to_host=False)
+                addresses = torch.tensor([stage.data_ptr() + i * size for i in range(n)],
+                                         dtype=torch.int64).pin_memory().to(device, non_blocking=True)
+                crc = torch.empty(n, dtype=torch.int32, device=device)
+                status = torch.zeros(1, dtype=torch.int32, device=device)
+                out = torch.empty(n * 32, dtype=torch.uint8, device=device)
+                vec = 16 if size % 16 == 0 else 8
+                self._check(lib.kvsnap_dp_crc32c(addresses.data_ptr(), n, size, crc.data_ptr(), 0,
+                                                 status.data_ptr(), vec, self.ctas, stream.cuda_stream))
+                self._check(lib.kvsnap_dp_sha256(addresses.data_ptr(), n, size, out.data_ptr(), stream.cuda_stream))
+            stream.synchronize()
+        self._status_error(status)
+        crcs = [v & 0xFFFFFFFF for v in crc.cpu().tolist()]
+        raw = out.cpu().numpy().tobytes()
+        return [(raw[32 * i:32 * i + 32].hex(), crcs[i]) for i in range(n)]
+
+    def close(self):
+        self.pool.close()
