@@ -58,6 +58,8 @@ def parse():
     p.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     p.add_argument("--explore", type=str, default="", help="write a per-phase / CTA sweep breakdown to this path")
     p.add_argument("--seed", type=int, default=0)
+    p.add_argument("--quick", action="store_true",
+                   help="only the device-timed steps (a short run for profiling captures)")
     return p.parse_args()
 
 
@@ -451,6 +453,13 @@ def main():
     if int(engine.status.item()) != 0:
         raise RuntimeError(f"kernel status {int(engine.status.item())} during the timed steps")
     digests_ok = True
+    if args.quick:
+        if rank == 0:
+            print(json.dumps({"quick": True, "ms_per_step": round(ms, 3),
+                              "phases_ms": {k: round(v, 3) for k, v in phases.items()}}), flush=True)
+        engine.snapshot.close()
+        plane.close()
+        return
 
     # End to end through the public API, host tier (one pinned allocation per block).
     targets = [plane.pool.reserve(size) for _ in range(n)]

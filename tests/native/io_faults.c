@@ -1,0 +1,56 @@
+/* Test-only syscall fault injection for kvsnap_b200/csrc/io.cpp, linked with
+   -Wl,--wrap=pwrite,--wrap=pread,--wrap=fdatasync. Each wrapper counts its calls
+   and, while a plan for it is armed, fails, shortens or stalls the next calls. */
+#include <errno.h>
+#include <sys/types.h>
+#include <unistd.h>
+
+enum { PWRITE = 0, PREAD = 1, FDATASYNC = 2 };
+enum { FAIL = 1, SHORT = 2, NOTHING = 3 };
+
+static int plan_call = -1, plan_kind = 0, plan_left = 0, plan_errno = 0;
+static int calls[3];
+
+ssize_t __real_pwrite(int, const void*, size_t, off_t);
+ssize_t __real_pread(int, void*, size_t, off_t);
+int __real_fdatasync(int);
+
+void io_fault(int call, int kind, int times, int err) {
+    plan_call = call; plan_kind = kind; plan_left = times; plan_errno = err;
+}
+
+int io_calls(int call) {
+    int n = calls[call];
+    calls[call] = 0;
+    return n;
+}
+
+static int armed(int call) {
+    calls[call]++;
+    if (plan_call != call || plan_left <= 0) return 0;
+    plan_left--;
+    return plan_kind;
+}
+
+ssize_t __wrap_pwrite(int fd, const void* data, size_t size, off_t offset) {
+    switch (armed(PWRITE)) {
+    case FAIL: errno = plan_errno; return -1;
+    case SHORT: return __real_pwrite(fd, data, size ? 1 : 0, offset);
+    case NOTHING: return 0;
+    }
+    return __real_pwrite(fd, data, size, offset);
+}
+
+ssize_t __wrap_pread(int fd, void* data, size_t size, off_t offset) {
+    switch (armed(PREAD)) {
+    case FAIL: errno = plan_errno; return -1;
+    case SHORT: return __real_pread(fd, data, size ? 1 : 0, offset);
+    case NOTHING: return 0;
+    }
+    return __real_pread(fd, data, size, offset);
+}
+
+int __wrap_fdatasync(int fd) {
+    if (armed(FDATASYNC) == FAIL) { errno = plan_errno; return -1; }
+    return __real_fdatasync(fd);
+}
