@@ -239,7 +239,7 @@ class Engine:
             e["t0"].record(self.copy)
         self._ok(lib.kvsnap_dp_gather(self.spans.data_ptr(), nspans, size, self.save_ids.data_ptr(),
                                       self.stage_addrs.data_ptr(), n, 0, self.crc.data_ptr(), self.status.data_ptr(),
-                                      16, self.ctas, self.copy_handle))
+                                      16 | self.plane._hbm, self.ctas, self.copy_handle))
         launches += 2   # gather + CRC finish
         gathered = torch.cuda.Event()
         gathered.record(self.copy)
@@ -265,9 +265,10 @@ class Engine:
             sources = self.stage2_addrs
         else:
             sources = self.pinned_addrs
+        vec = 16 | (self.plane._hbm if self.restore_mode == "staged" else 0)
         self._ok(lib.kvsnap_dp_scatter(self.spans.data_ptr(), nspans, size, sources.data_ptr(),
                                        self.restore_ids.data_ptr(), n, self.crc_restore.data_ptr(),
-                                       self.crc.data_ptr(), 0, self.status.data_ptr(), 16, self.ctas,
+                                       self.crc.data_ptr(), 0, self.status.data_ptr(), vec, self.ctas,
                                        self.copy_handle))
         launches += 2   # scatter + CRC verify finish
         self.copy.wait_event(hashed)
@@ -589,6 +590,21 @@ def explore_phases(plane, engine, save_ids, restore_ids, link):
                                   engine.restore_ids.data_ptr(), n, engine.crc_restore.data_ptr(), 0, 0,
                                   engine.status.data_ptr(), 16, ctas, engine.copy_handle)
 
+        def scatter_lc():
+            lib.kvsnap_dp_scatter(engine.spans.data_ptr(), nspans, size, engine.stage_addrs.data_ptr(),
+                                  engine.restore_ids.data_ptr(), n, engine.crc_restore.data_ptr(), 0, 0,
+                                  engine.status.data_ptr(), 16 | plane._hbm, ctas, engine.copy_handle)
+
+        def gather_lc():
+            lib.kvsnap_dp_gather(engine.spans.data_ptr(), nspans, size, engine.save_ids.data_ptr(),
+                                 engine.stage_addrs.data_ptr(), n, 0, engine.crc.data_ptr(), engine.status.data_ptr(),
+                                 16 | plane._hbm, ctas, engine.copy_handle)
+
+        def gather_lc_nocrc():
+            lib.kvsnap_dp_gather(engine.spans.data_ptr(), nspans, size, engine.save_ids.data_ptr(),
+                                 engine.stage_addrs.data_ptr(), n, 0, 0, engine.status.data_ptr(),
+                                 16 | plane._hbm, ctas, engine.copy_handle)
+
         def gather_direct():
             lib.kvsnap_dp_gather(engine.spans.data_ptr(), nspans, size, engine.save_ids.data_ptr(),
                                  engine.pinned_addrs.data_ptr(), n, 0, engine.crc.data_ptr(),
@@ -598,6 +614,8 @@ def explore_phases(plane, engine, save_ids, restore_ids, link):
         for name, fn, nbytes in (("restore_direct", restore, size * n), ("restore_direct_crc", restore_crc, size * n),
                                  ("gather_hbm_crc", gather, 2 * size * n), ("gather_hbm", gather_nocrc, 2 * size * n),
                                  ("scatter_hbm_crc", scatter_hbm, 2 * size * n),
+                                 ("scatter_lc_crc", scatter_lc, 2 * size * n), ("gather_lc_crc", gather_lc, 2 * size * n),
+                                 ("gather_lc", gather_lc_nocrc, 2 * size * n),
                                  ("gather_direct_crc", gather_direct, size * n)):
             ms = timed(fn)
             row[name] = {"ms": round(ms, 3), "gbs": round(nbytes / (ms / 1e3) / 1e9, 2)}

@@ -80,6 +80,12 @@ int kvsnap_pool_mark(void* pool, uint64_t id);
 #define KVSNAP_DP_BAD_BLOCK 2u       /* a block id outside its cache */
 #define KVSNAP_DP_CRC_MISMATCH 4u    /* a block's CRC32C differed from the expected one */
 
+/* OR into a `vec` argument when every packed address is device memory: the
+   kernels then walk both sides in lane-contiguous 64-byte runs with per-lane
+   CRC tables (HBM-friendly) instead of 512-byte coalesced steps (host-link
+   friendly). Needs vec 16 and spans that are multiples of 512 bytes. */
+#define KVSNAP_DP_HBM 0x100
+
 /*
  * One registered layer view, i.e. one span of every packed block. A packed
  * block is the spans back to back in registration order (layer-name order,

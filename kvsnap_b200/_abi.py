@@ -13,6 +13,8 @@ POOL_ABI_VERSION = 2
 IO_ABI_VERSION = 1
 
 MISALIGNED, BAD_BLOCK, CRC_MISMATCH = 1, 2, 4
+# OR into a kernel's `vec` when every packed address is device memory.
+HBM = 0x100
 
 
 class Span(C.Structure):

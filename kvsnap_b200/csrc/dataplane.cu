@@ -298,6 +298,139 @@ __global__ void __launch_bounds__(256) span_kernel(SpanArgs a) {
     }
 }
 
+// ---- lane-contiguous kernels, for packed blocks in device memory ----------------
+//
+// When both sides of a copy are HBM, lane j of a warp takes bytes
+// [j*len/32, (j+1)*len/32) of a unit and walks them in order, 64 bytes (two
+// sectors) a step. Its CRC register then runs straight through its bytes with
+// slicing-by-4, and the four 256-entry tables are replicated once per lane
+// (128 KiB of shared memory): entry (k, v) of lane l lies in bank l, so a
+// warp's 32 lookups never conflict. Lane registers are moved into place with
+// x^(8*(31-j)*len/32) and XOR-reduced as in the coalesced kernels. One CTA of
+// 1024 threads per SM. Units must be multiples of 512 bytes.
+constexpr int kRepWords = 4 * 256 * 32;
+constexpr int kRepBytes = kRepWords * 4;
+
+__device__ __forceinline__ void load_rep_tables(uint32_t* tb) {
+    const uint32_t* g = &g_tables.t[0][0];   // slots 0..3 hold T_0..T_3
+    for (int i = threadIdx.x; i < kRepWords; i += blockDim.x) tb[i] = g[i >> 5];
+}
+
+// r <- raw(r, 4 bytes of w), little-endian byte order; tl = tables + lane.
+__device__ __forceinline__ uint32_t crc_word(const uint32_t* tl, uint32_t r, uint32_t w) {
+    const uint32_t x = r ^ w;
+    return tl[(768 + (x & 255)) << 5] ^ tl[(512 + ((x >> 8) & 255)) << 5] ^ tl[(256 + ((x >> 16) & 255)) << 5] ^
+           tl[(x >> 24) << 5];
+}
+
+__device__ __forceinline__ uint32_t crc_vec(const uint32_t* tl, uint32_t r, const uint4& v) {
+    r = crc_word(tl, r, v.x);
+    r = crc_word(tl, r, v.y);
+    r = crc_word(tl, r, v.z);
+    return crc_word(tl, r, v.w);
+}
+
+// One warp over one unit of `len` bytes (len % 512 == 0), lane-contiguous.
+template <bool STORE, bool CRC>
+__device__ __forceinline__ uint32_t warp_unit_hbm(const uint32_t* tl, const char* __restrict__ src,
+                                                  char* __restrict__ dst, int64_t len, int lane, bool tail,
+                                                  const kvsnap_span& sp, int valid) {
+    const int64_t seg = len >> 5;
+    const int64_t base = (int64_t)lane * seg;
+    uint32_t r = 0;
+    int64_t at = 0;
+    for (; at + 64 <= seg; at += 64) {
+        uint4 v[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) v[k] = *reinterpret_cast<const uint4*>(src + base + at + 16 * k);
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            if (tail) v[k] = mask_tail<16>(v[k], base + at + 16 * k, sp, valid);
+            if (STORE) *reinterpret_cast<uint4*>(dst + base + at + 16 * k) = v[k];
+        }
+        if (CRC) {
+#pragma unroll
+            for (int k = 0; k < 4; ++k) r = crc_vec(tl, r, v[k]);
+        }
+    }
+    for (; at < seg; at += 16) {
+        uint4 v = *reinterpret_cast<const uint4*>(src + base + at);
+        if (tail) v = mask_tail<16>(v, base + at, sp, valid);
+        if (STORE) *reinterpret_cast<uint4*>(dst + base + at) = v;
+        if (CRC) r = crc_vec(tl, r, v);
+    }
+    return r;
+}
+
+template <int MODE>
+__global__ void __launch_bounds__(1024, 1) span_kernel_hbm(SpanArgs a) {
+    extern __shared__ uint32_t tb[];
+    const bool crc = a.crc != nullptr;
+    if (crc) load_rep_tables(tb);
+    __syncthreads();
+    if (MODE == kScatter && a.gate && *a.gate) return;
+    const int lane = threadIdx.x & 31;
+    const uint32_t* tl = tb + lane;
+    int64_t shift_for = -1;
+    uint32_t lane_shift = 0;
+    const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
+    const int64_t units = a.n * a.nspans;
+    for (int64_t u = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); u < units; u += warps) {
+        const int64_t i = u / a.nspans;
+        const kvsnap_span sp = a.spans[u - i * a.nspans];
+        const int64_t block = a.blocks[i];
+        if (block < 0 || block >= sp.nblocks) {
+            if (lane == 0) flag(a.status, KVSNAP_DP_BAD_BLOCK);
+            continue;
+        }
+        const int64_t packed = a.packed[i] + sp.offset;
+        const int64_t cache = sp.base + block * sp.pitch;
+        if (((packed | cache) & 15) || (sp.bytes & 511)) {
+            if (lane == 0) flag(a.status, KVSNAP_DP_MISALIGNED);
+            continue;
+        }
+        const char* src = reinterpret_cast<const char*>(MODE == kGather ? cache : packed);
+        char* dst = reinterpret_cast<char*>(MODE == kGather ? packed : cache);
+        const bool tail = MODE == kGather && a.valid > 0 && i == a.n - 1;
+        if (crc) {
+            if (sp.bytes != shift_for) {
+                lane_shift = dev_xpow8n((uint64_t)(31 - lane) * uint64_t(sp.bytes >> 5));
+                shift_for = sp.bytes;
+            }
+            uint32_t r = warp_unit_hbm<true, true>(tl, src, dst, sp.bytes, lane, tail, sp, a.valid);
+            r = gf_mulmod(warp_xor(gf_mulmod(r, lane_shift)), sp.crc_shift);
+            if (lane == 0) atomicXor(&a.crc[i], r);
+        } else {
+            warp_unit_hbm<true, false>(tl, src, dst, sp.bytes, lane, tail, sp, a.valid);
+        }
+    }
+}
+
+__global__ void __launch_bounds__(1024, 1) crc_kernel_hbm(const int64_t* addrs, int64_t n, int64_t block_bytes,
+                                                          int64_t piece, uint32_t* crc, uint32_t* status) {
+    extern __shared__ uint32_t tb[];
+    load_rep_tables(tb);
+    __syncthreads();
+    const int lane = threadIdx.x & 31;
+    const uint32_t* tl = tb + lane;
+    const uint32_t lane_shift = dev_xpow8n((uint64_t)(31 - lane) * uint64_t(piece >> 5));
+    const int64_t pieces = block_bytes / piece;
+    const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
+    kvsnap_span none{};
+    for (int64_t u = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); u < n * pieces; u += warps) {
+        const int64_t i = u / pieces, p = u - i * pieces;
+        const int64_t base = addrs[i] + p * piece;
+        if (base & 15) {
+            if (lane == 0) flag(status, KVSNAP_DP_MISALIGNED);
+            continue;
+        }
+        uint32_t r = warp_unit_hbm<false, true>(tl, reinterpret_cast<const char*>(base), nullptr, piece, lane, false,
+                                                none, 0);
+        r = gf_mulmod(warp_xor(gf_mulmod(r, lane_shift)), dev_xpow8n(uint64_t(block_bytes - (p + 1) * piece)));
+        if (lane == 0) atomicXor(&crc[i], r);
+    }
+}
+
 // CRC32C of whole packed blocks, in pieces of kPiece bytes per warp.
 constexpr int64_t kPiece = 64 << 10;
 
@@ -354,92 +487,135 @@ __constant__ uint32_t kSha256K[64] = {
 __device__ __forceinline__ uint32_t rotr(uint32_t x, int n) { return __funnelshift_r(x, x, n); }
 __device__ __forceinline__ uint32_t be32(uint32_t x) { return __byte_perm(x, 0, 0x0123); }
 
-__device__ __forceinline__ void sha256_compress(uint32_t h[8], uint32_t w[16]) {
-    uint32_t a = h[0], b = h[1], c = h[2], d = h[3], e = h[4], f = h[5], g = h[6], k = h[7];
+// Message words of chunk c of a block at p (bytes, block_bytes long), big-endian,
+// SHA-256 padding included: chunks [0, full) are data, the last one or two carry
+// the remaining bytes, 0x80, zeros and the bit length.
+__device__ __forceinline__ void sha256_words(const unsigned char* p, bool aligned, int64_t c, int64_t full,
+                                             int rest, uint64_t bits, uint32_t w[16]) {
+    if (c < full) {
+        if (aligned) {
+            const uint4* q = reinterpret_cast<const uint4*>(p + 64 * c);
 #pragma unroll
-    for (int t = 0; t < 64; ++t) {
-        if (t >= 16) {
-            const uint32_t x = w[(t + 1) & 15], y = w[(t + 14) & 15];
-            const uint32_t s0 = rotr(x, 7) ^ rotr(x, 18) ^ (x >> 3);
-            const uint32_t s1 = rotr(y, 17) ^ rotr(y, 19) ^ (y >> 10);
-            w[t & 15] += s0 + w[(t + 9) & 15] + s1;
+            for (int k = 0; k < 4; ++k) {
+                const uint4 v = __ldcs(q + k);
+                w[4 * k + 0] = be32(v.x);
+                w[4 * k + 1] = be32(v.y);
+                w[4 * k + 2] = be32(v.z);
+                w[4 * k + 3] = be32(v.w);
+            }
+        } else {
+            for (int j = 0; j < 16; ++j) {
+                const unsigned char* b = p + 64 * c + 4 * j;
+                w[j] = (uint32_t(b[0]) << 24) | (uint32_t(b[1]) << 16) | (uint32_t(b[2]) << 8) | b[3];
+            }
         }
-        const uint32_t t1 = k + (rotr(e, 6) ^ rotr(e, 11) ^ rotr(e, 25)) + ((e & f) ^ (~e & g)) + kSha256K[t] +
-                            w[t & 15];
-        const uint32_t t2 = (rotr(a, 2) ^ rotr(a, 13) ^ rotr(a, 22)) + ((a & b) ^ (a & c) ^ (b & c));
-        k = g;
-        g = f;
-        f = e;
-        e = d + t1;
-        d = c;
-        c = b;
-        b = a;
-        a = t1 + t2;
+        return;
     }
-    h[0] += a; h[1] += b; h[2] += c; h[3] += d; h[4] += e; h[5] += f; h[6] += g; h[7] += k;
+    const int k = int(c - full);                     // 0, or 1 when the tail needs two chunks
+    const unsigned char* tail = p + 64 * full;
+    for (int j = 0; j < 16; ++j) {
+        uint32_t word = 0;
+        for (int q = 0; q < 4; ++q) {
+            const int at = 64 * k + 4 * j + q;
+            const uint32_t byte = at < rest ? tail[at] : (at == rest ? 0x80u : 0u);
+            word = (word << 8) | byte;
+        }
+        w[j] = word;
+    }
+    if (k == (rest < 56 ? 0 : 1)) {
+        w[14] = uint32_t(bits >> 32);
+        w[15] = uint32_t(bits);
+    }
 }
 
-// One lane per block: the whole 64-byte chunks straight from memory (the next
-// chunk's loads issued before the current chunk's rounds), then the padded tail.
-__global__ void __launch_bounds__(32) sha256_kernel(const int64_t* addrs, int64_t n, int64_t block_bytes,
-                                                    uint8_t* out) {
-    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-    if (i >= n) return;
-    const char* p = reinterpret_cast<const char*>(addrs[i]);
+// SHA-256 with the work of one block split over two warps on two SM
+// sub-partitions. One lane of each hashes one block, 32 blocks a warp pair:
+// the schedule warp loads each 64-byte chunk and expands it into the 64 words
+// W[t] + K[t] in a shared-memory ring; the compress warp runs only the 64
+// rounds, reading those words. Per block the rounds are a serial chain and
+// their integer issue rate bounds the hash time, so the compress warp gets a
+// sub-partition to itself. The two warps hand ring slots over with named
+// barriers (bar.arrive / bar.sync, 64 threads): both run the same number of
+// chunks, so every wait is matched.
+constexpr int kShaPairs = 2;          // warp pairs a CTA
+constexpr int kShaSlots = 3;          // ring slots a pair
+constexpr int kShaSlotWords = 64 * 32;
+
+__device__ __forceinline__ void named_arrive(int id) { asm volatile("bar.arrive %0, 64;" ::"r"(id) : "memory"); }
+__device__ __forceinline__ void named_sync(int id) { asm volatile("bar.sync %0, 64;" ::"r"(id) : "memory"); }
+
+__global__ void __launch_bounds__(64 * kShaPairs) sha256_kernel(const int64_t* addrs, int64_t n,
+                                                               int64_t block_bytes, uint8_t* out) {
+    extern __shared__ uint32_t ring[];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int pair = warp >> 1;
+    // Warps 0,1 / 2,3 form pairs; even warps compress and odd warps schedule, so
+    // within a CTA the compress warps sit on sub-partitions 0 and 2.
+    const bool compress = (warp & 1) == 0;
+    const int64_t first = ((int64_t)blockIdx.x * kShaPairs + pair) * 32;
+    if (first >= n) return;                          // the whole pair idles together
+    const int64_t i = first + lane;
+    const bool live = i < n;
+    uint32_t* slots = ring + pair * kShaSlots * kShaSlotWords;
+    const int full_id = 1 + pair * 2 * kShaSlots;    // barrier ids: FULL[s], EMPTY[s] per pair
+    const int empty_id = full_id + kShaSlots;
+    const int64_t full = block_bytes / 64;
+    const int rest = int(block_bytes - full * 64);
+    const int64_t chunks = full + (rest < 56 ? 1 : 2);
+
+    if (!compress) {
+        const unsigned char* p = reinterpret_cast<const unsigned char*>(addrs[live ? i : n - 1]);
+        const bool aligned = (reinterpret_cast<uintptr_t>(p) & 15) == 0;
+        const uint64_t bits = uint64_t(block_bytes) * 8;
+        for (int64_t c = 0; c < chunks; ++c) {
+            const int s = int(c % kShaSlots);
+            uint32_t w[16];
+            sha256_words(p, aligned, c, full, rest, bits, w);
+            if (c >= kShaSlots) named_sync(empty_id + s);
+            uint32_t* slot = slots + s * kShaSlotWords + lane;
+#pragma unroll
+            for (int t = 0; t < 64; ++t) {
+                if (t >= 16) {
+                    const uint32_t x = w[(t + 1) & 15], y = w[(t + 14) & 15];
+                    w[t & 15] += (rotr(x, 7) ^ rotr(x, 18) ^ (x >> 3)) + w[(t + 9) & 15] +
+                                 (rotr(y, 17) ^ rotr(y, 19) ^ (y >> 10));
+                }
+                slot[t * 32] = w[t & 15] + kSha256K[t];
+            }
+            named_arrive(full_id + s);
+        }
+        // Match the compress warp's last releases, so every barrier generation completes.
+        for (int64_t c = chunks > kShaSlots ? chunks - kShaSlots : 0; c < chunks; ++c)
+            named_sync(empty_id + int(c % kShaSlots));
+        return;
+    }
     uint32_t h[8] = {0x6a09e667, 0xbb67ae85, 0x3c6ef372, 0xa54ff53a, 0x510e527f, 0x9b05688c, 0x1f83d9ab, 0x5be0cd19};
-    uint32_t w[16];
-    const int64_t chunks = block_bytes / 64;
-    if ((reinterpret_cast<uintptr_t>(p) & 15) == 0 && chunks > 0) {
-        uint4 next[4];
+    for (int64_t c = 0; c < chunks; ++c) {
+        const int s = int(c % kShaSlots);
+        named_sync(full_id + s);
+        const uint32_t* slot = slots + s * kShaSlotWords + lane;
+        uint32_t a = h[0], b = h[1], cc = h[2], d = h[3], e = h[4], f = h[5], g = h[6], k = h[7];
 #pragma unroll
-        for (int q = 0; q < 4; ++q) next[q] = __ldcs(reinterpret_cast<const uint4*>(p) + q);
-        for (int64_t c = 0; c < chunks; ++c) {
-#pragma unroll
-            for (int q = 0; q < 4; ++q) {
-                w[4 * q + 0] = be32(next[q].x);
-                w[4 * q + 1] = be32(next[q].y);
-                w[4 * q + 2] = be32(next[q].z);
-                w[4 * q + 3] = be32(next[q].w);
-            }
-            if (c + 1 < chunks) {
-#pragma unroll
-                for (int q = 0; q < 4; ++q) next[q] = __ldcs(reinterpret_cast<const uint4*>(p + 64 * (c + 1)) + q);
-            }
-            sha256_compress(h, w);
+        for (int t = 0; t < 64; ++t) {
+            const uint32_t t1 = k + (rotr(e, 6) ^ rotr(e, 11) ^ rotr(e, 25)) + ((e & f) ^ (~e & g)) + slot[t * 32];
+            const uint32_t t2 = (rotr(a, 2) ^ rotr(a, 13) ^ rotr(a, 22)) + ((a & b) ^ (a & cc) ^ (b & cc));
+            k = g;
+            g = f;
+            f = e;
+            e = d + t1;
+            d = cc;
+            cc = b;
+            b = a;
+            a = t1 + t2;
         }
-    } else {
-        const unsigned char* b = reinterpret_cast<const unsigned char*>(p);
-        for (int64_t c = 0; c < chunks; ++c) {
-            for (int j = 0; j < 16; ++j) {
-                const unsigned char* q = b + 64 * c + 4 * j;
-                w[j] = (uint32_t(q[0]) << 24) | (uint32_t(q[1]) << 16) | (uint32_t(q[2]) << 8) | q[3];
-            }
-            sha256_compress(h, w);
-        }
+        named_arrive(empty_id + s);
+        h[0] += a; h[1] += b; h[2] += cc; h[3] += d; h[4] += e; h[5] += f; h[6] += g; h[7] += k;
     }
-    // Tail: the remaining bytes, 0x80, zeros, then the bit length big-endian.
-    const int rest = int(block_bytes - chunks * 64);
-    const unsigned char* tailp = reinterpret_cast<const unsigned char*>(p) + chunks * 64;
-    const uint64_t bits = uint64_t(block_bytes) * 8;
-    for (int round = 0; round < (rest < 56 ? 1 : 2); ++round) {
-        for (int j = 0; j < 16; ++j) {
-            uint32_t word = 0;
-            for (int q = 0; q < 4; ++q) {
-                const int at = round * 64 + 4 * j + q;
-                const uint32_t byte = at < rest ? tailp[at] : (at == rest ? 0x80u : 0u);
-                word = (word << 8) | byte;
-            }
-            w[j] = word;
-        }
-        if (round == (rest < 56 ? 0 : 1)) {
-            w[14] = uint32_t(bits >> 32);
-            w[15] = uint32_t(bits);
-        }
-        sha256_compress(h, w);
-    }
-    uint32_t* o = reinterpret_cast<uint32_t*>(out + 32 * i);
+    if (live) {
+        uint32_t* o = reinterpret_cast<uint32_t*>(out + 32 * i);
 #pragma unroll
-    for (int j = 0; j < 8; ++j) o[j] = be32(h[j]);
+        for (int j = 0; j < 8; ++j) o[j] = be32(h[j]);
+    }
 }
 
 // ---- the reference restore kernel's interface ------------------------------------
@@ -551,8 +727,11 @@ int launch_spans(const kvsnap_span* spans, int nspans, uint64_t block_bytes, con
                  const int64_t* packed, int64_t n, int32_t valid, uint32_t* crc, const uint32_t* expect,
                  const uint32_t* gate, uint32_t* status, int vec, int ctas, uintptr_t stream) {
     return guarded([&] {
+        const bool hbm = (vec & KVSNAP_DP_HBM) != 0;
+        vec &= ~KVSNAP_DP_HBM;
         if (n < 0 || nspans <= 0 || !spans) throw Fail{"invalid span table"};
         if (vec != 16 && vec != 8) throw Fail{"vector width must be 16 or 8"};
+        if (hbm && vec != 16) throw Fail{"the device-memory kernels need 16-byte alignment"};
         if (n == 0) return;
         if (!blocks || !packed) throw Fail{"block and address tables are required"};
         if (expect && !crc) throw Fail{"verifying needs a CRC output"};
@@ -560,6 +739,20 @@ int launch_spans(const kvsnap_span* spans, int nspans, uint64_t block_bytes, con
         cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
         if (crc) check(cudaMemsetAsync(crc, 0, sizeof(uint32_t) * size_t(n), s));
         SpanArgs a{spans, nspans, blocks, packed, n, valid, crc, gate, status};
+        if (hbm) {
+            static bool configured = false;
+            if (!configured) {
+                check(cudaFuncSetAttribute(span_kernel_hbm<MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           kRepBytes));
+                configured = true;
+            }
+            const int64_t want = (n * nspans + 31) / 32;
+            const int grid = ctas > 0 ? ctas : int(want < sms ? want : sms);
+            span_kernel_hbm<MODE><<<grid, 1024, crc ? kRepBytes : 0, s>>>(a);
+            check(cudaGetLastError());
+            if (crc) finish(crc, expect, n, block_bytes, status, s);
+            return;
+        }
         const int grid = grid_for(n * nspans, ctas, sms);
         if (vec == 16)
             span_kernel<16, MODE><<<grid, 256, 0, s>>>(a);
@@ -594,12 +787,31 @@ extern "C" int kvsnap_dp_scatter(const kvsnap_span* spans, int nspans, uint64_t 
 extern "C" int kvsnap_dp_crc32c(const int64_t* addrs, int64_t n, uint64_t block_bytes, uint32_t* crc_out,
                                 const uint32_t* expect, uint32_t* status, int vec, int ctas, uintptr_t stream) {
     return guarded([&] {
+        const bool hbm = (vec & KVSNAP_DP_HBM) != 0;
+        vec &= ~KVSNAP_DP_HBM;
         if (n < 0 || vec != 16 && vec != 8) throw Fail{"invalid CRC request"};
         if (n == 0) return;
         if (!addrs || !crc_out || block_bytes == 0) throw Fail{"CRC needs addresses, output and a block size"};
         const int sms = enter_stream(stream);
         cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
         check(cudaMemsetAsync(crc_out, 0, sizeof(uint32_t) * size_t(n), s));
+        // Device-memory blocks: lane-contiguous pieces of the largest power of two
+        // up to 64 KiB dividing the block, when that is a multiple of 512 bytes.
+        int64_t piece = int64_t(block_bytes & (~block_bytes + 1));
+        if (piece > kPiece) piece = kPiece;
+        if (hbm && vec == 16 && piece >= 512) {
+            static bool configured = false;
+            if (!configured) {
+                check(cudaFuncSetAttribute(crc_kernel_hbm, cudaFuncAttributeMaxDynamicSharedMemorySize, kRepBytes));
+                configured = true;
+            }
+            const int64_t want = (n * (int64_t(block_bytes) / piece) + 31) / 32;
+            const int grid = ctas > 0 ? ctas : int(want < sms ? want : sms);
+            crc_kernel_hbm<<<grid, 1024, kRepBytes, s>>>(addrs, n, int64_t(block_bytes), piece, crc_out, status);
+            check(cudaGetLastError());
+            finish(crc_out, expect, n, block_bytes, status, s);
+            return;
+        }
         const int64_t pieces = (int64_t(block_bytes) + kPiece - 1) / kPiece;
         const int grid = grid_for(n * pieces, ctas, sms);
         if (vec == 16)
@@ -620,7 +832,15 @@ extern "C" int kvsnap_dp_sha256(const int64_t* addrs, int64_t n, uint64_t block_
         if (reinterpret_cast<uintptr_t>(out) & 3) throw Fail{"digest output must be 4-byte aligned"};
         enter_stream(stream);
         cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-        sha256_kernel<<<int((n + 31) / 32), 32, 0, s>>>(addrs, n, int64_t(block_bytes), out);
+        constexpr int smem = kShaPairs * kShaSlots * kShaSlotWords * int(sizeof(uint32_t));
+        static bool configured = false;   // per process; the attribute is per function, not per device
+        if (!configured) {
+            check(cudaFuncSetAttribute(sha256_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+            configured = true;
+        }
+        const int64_t per_cta = 32 * kShaPairs;
+        sha256_kernel<<<int((n + per_cta - 1) / per_cta), 64 * kShaPairs, smem, s>>>(addrs, n,
+                                                                                    int64_t(block_bytes), out);
         check(cudaGetLastError());
     });
 }

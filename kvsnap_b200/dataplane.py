@@ -380,6 +380,8 @@ class TorchBlockDataPlane:
                 raise RuntimeError("packed block size disagrees with the registered layers")
             host = torch.frombuffer(bytearray(bytes(spans)), dtype=torch.uint8)
             self._span_vec = vec
+            # Device-side copies may use the lane-contiguous HBM kernels.
+            self._hbm = _abi.HBM if vec == 16 and all(layer["bytes"] % 512 == 0 for layer in self.layers) else 0
             self._min_blocks = min(t.shape[0] for t in self.caches.values())
             self._span_table = host.to(self._device())
             self._sha_stream = torch.cuda.Stream(self._device())
@@ -427,18 +429,19 @@ class TorchBlockDataPlane:
             digest = torch.empty(32, dtype=torch.uint8, device=device)
             gate = torch.ones(1, dtype=torch.int32, device=device)
             status = torch.zeros(1, dtype=torch.int32, device=device)
-            vec = self._span_vec
-            calls = [
-                lib.kvsnap_dp_gather(spans.data_ptr(), len(self.layers), self.block_bytes, table.data_ptr(),
-                                     table.data_ptr() + 8, 1, 0, crc.data_ptr(), status.data_ptr(), vec,
-                                     self.ctas, stream),
-                lib.kvsnap_dp_scatter(spans.data_ptr(), len(self.layers), self.block_bytes, table.data_ptr() + 8,
-                                      table.data_ptr(), 1, 0, 0, gate.data_ptr(), status.data_ptr(), vec, self.ctas,
-                                      stream),
-                lib.kvsnap_dp_crc32c(table.data_ptr() + 8, 1, self.block_bytes, crc.data_ptr(), 0,
-                                     status.data_ptr(), vec, self.ctas, stream),
-                lib.kvsnap_dp_sha256(table.data_ptr() + 8, 1, self.block_bytes, digest.data_ptr(), stream),
-            ]
+            calls = []
+            for vec in sorted({self._span_vec, self._span_vec | self._hbm}):
+                calls += [
+                    lib.kvsnap_dp_gather(spans.data_ptr(), len(self.layers), self.block_bytes, table.data_ptr(),
+                                         table.data_ptr() + 8, 1, 0, crc.data_ptr(), status.data_ptr(), vec,
+                                         self.ctas, stream),
+                    lib.kvsnap_dp_scatter(spans.data_ptr(), len(self.layers), self.block_bytes,
+                                          table.data_ptr() + 8, table.data_ptr(), 1, 0, 0, gate.data_ptr(),
+                                          status.data_ptr(), vec, self.ctas, stream),
+                    lib.kvsnap_dp_crc32c(table.data_ptr() + 8, 1, self.block_bytes, crc.data_ptr(), 0,
+                                         status.data_ptr(), vec, self.ctas, stream),
+                ]
+            calls.append(lib.kvsnap_dp_sha256(table.data_ptr() + 8, 1, self.block_bytes, digest.data_ptr(), stream))
             if min(calls) < 0:
                 raise RuntimeError(lib.kvsnap_cuda_error().decode())
             empty = torch.zeros(1, dtype=torch.int64, device=device)
@@ -565,6 +568,8 @@ class TorchBlockDataPlane:
                     else:
                         read_from = addresses
                     vec = self._vec_for(read_from)
+                    if staged and vec == 16:
+                        vec |= self._hbm
                     table = torch.tensor(read_from + list(block_ids), dtype=torch.int64).pin_memory().to(
                         device, non_blocking=True)
                     if expected_crc32c is not None:
@@ -656,6 +661,8 @@ class TorchBlockDataPlane:
                 stage = torch.empty(n * size, dtype=torch.uint8, device=device)
                 write_to = [stage.data_ptr() + i * size for i in range(n)]
             vec = self._vec_for(write_to)
+            if not direct and vec == 16:
+                vec |= self._hbm
             table = torch.tensor(list(block_ids) + write_to, dtype=torch.int64).pin_memory().to(
                 device, non_blocking=True)
             try:
@@ -747,7 +754,7 @@ class TorchBlockDataPlane:
                 crc = torch.empty(n, dtype=torch.int32, device=device)
                 status = torch.zeros(1, dtype=torch.int32, device=device)
                 out = torch.empty(n * 32, dtype=torch.uint8, device=device)
-                vec = 16 if size % 16 == 0 else 8
+                vec = (16 | _abi.HBM) if size % 16 == 0 else 8
                 self._check(lib.kvsnap_dp_crc32c(addresses.data_ptr(), n, size, crc.data_ptr(), 0,
                                                  status.data_ptr(), vec, self.ctas, stream.cuda_stream))
                 self._check(lib.kvsnap_dp_sha256(addresses.data_ptr(), n, size, out.data_ptr(), stream.cuda_stream))

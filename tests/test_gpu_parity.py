@@ -192,8 +192,9 @@ def _dp():
     return _dp(_load())
 
 
+@pytest.mark.parametrize("hbm", [False, True])
 @pytest.mark.parametrize("length", [8, 16, 24, 504, 512, 520, 4096 + 8, 65536, 65536 + 16, 3 * 65536 + 8, 1835008])
-def test_crc32c_kernel_matches_the_reference_crc(length):
+def test_crc32c_kernel_matches_the_reference_crc(length, hbm):
     lib = _dp()
     n = 5
     data = [kvgen.random_bytes(1000 + length + i, length) for i in range(n)]
@@ -202,6 +203,8 @@ def test_crc32c_kernel_matches_the_reference_crc(length):
     crc = torch.empty(n, dtype=torch.int32, device="cuda")
     status = torch.zeros(1, dtype=torch.int32, device="cuda")
     vec = 16 if length % 16 == 0 else 8
+    if hbm:
+        vec |= 0x100          # KVSNAP_DP_HBM: lane-contiguous kernel where the block allows it
     s = torch.cuda.current_stream().cuda_stream
     assert lib.kvsnap_dp_crc32c(addrs.data_ptr(), n, length, crc.data_ptr(), 0, status.data_ptr(), vec, 0, s) == 0
     torch.cuda.synchronize()
