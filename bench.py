@@ -265,11 +265,12 @@ class Engine:
             sources = self.stage2_addrs
         else:
             sources = self.pinned_addrs
-        vec = 16 | (self.plane._hbm if self.restore_mode == "staged" else 0)
+        staged = self.restore_mode == "staged"
+        vec = 16 | (self.plane._hbm if staged else 0)
         self._ok(lib.kvsnap_dp_scatter(self.spans.data_ptr(), nspans, size, sources.data_ptr(),
                                        self.restore_ids.data_ptr(), n, self.crc_restore.data_ptr(),
-                                       self.crc.data_ptr(), 0, self.status.data_ptr(), vec, self.ctas,
-                                       self.copy_handle))
+                                       self.crc.data_ptr(), 0, self.status.data_ptr(), vec,
+                                       self.ctas if staged else self.plane.host_ctas, self.copy_handle))
         launches += 2   # scatter + CRC verify finish
         self.copy.wait_event(hashed)
         if e:

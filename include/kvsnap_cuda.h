@@ -81,9 +81,9 @@ int kvsnap_pool_mark(void* pool, uint64_t id);
 #define KVSNAP_DP_CRC_MISMATCH 4u    /* a block's CRC32C differed from the expected one */
 
 /* OR into a `vec` argument when every packed address is device memory: the
-   kernels then walk both sides in lane-contiguous 64-byte runs with per-lane
-   CRC tables (HBM-friendly) instead of 512-byte coalesced steps (host-link
-   friendly). Needs vec 16 and spans that are multiples of 512 bytes. */
+   kernels then take 64 contiguous bytes a lane in 2 KiB warp steps with
+   per-lane CRC tables (HBM-friendly) instead of 16 bytes a lane in 512-byte
+   steps (host-link friendly). Needs vec 16. */
 #define KVSNAP_DP_HBM 0x100
 
 /*

@@ -57,9 +57,10 @@ __host__ __device__ constexpr uint32_t gf_xpow8n(uint64_t n) {
 }
 
 // Tables: slots 0..15 hold T_0..T_15, slots 16..19 T_492..T_495 (moving a lane's
-// register 496 bytes ahead), slots 20..23 T_244..T_247 (the same for 8-byte vectors).
+// register 496 bytes ahead), slots 20..23 T_244..T_247 (the same for 8-byte
+// vectors), slots 24..27 T_1980..T_1983 (1984 bytes ahead, for the HBM kernels).
 struct CrcTables {
-    uint32_t t[24][256];
+    uint32_t t[28][256];
 };
 
 constexpr CrcTables make_tables() {
@@ -72,10 +73,11 @@ constexpr CrcTables make_tables() {
     for (int k = 1; k < 16; ++k)
         for (int v = 0; v < 256; ++v) r.t[k][v] = (r.t[k - 1][v] >> 8) ^ r.t[0][r.t[k - 1][v] & 0xFFu];
     for (int j = 0; j < 4; ++j) {
-        const uint32_t far16 = gf_xpow8n(492 + j), far8 = gf_xpow8n(244 + j);
+        const uint32_t far16 = gf_xpow8n(492 + j), far8 = gf_xpow8n(244 + j), far64 = gf_xpow8n(1980 + j);
         for (int v = 0; v < 256; ++v) {
             r.t[16 + j][v] = gf_mulmod(r.t[0][v], far16);
             r.t[20 + j][v] = gf_mulmod(r.t[0][v], far8);
+            r.t[24 + j][v] = gf_mulmod(r.t[0][v], far64);
         }
     }
     return r;
@@ -298,81 +300,96 @@ __global__ void __launch_bounds__(256) span_kernel(SpanArgs a) {
     }
 }
 
-// ---- lane-contiguous kernels, for packed blocks in device memory ----------------
+// ---- wide-lane kernels, for packed blocks in device memory ------------------------
 //
-// When both sides of a copy are HBM, lane j of a warp takes bytes
-// [j*len/32, (j+1)*len/32) of a unit and walks them in order, 64 bytes (two
-// sectors) a step. Its CRC register then runs straight through its bytes with
-// slicing-by-4, and the four 256-entry tables are replicated once per lane
-// (128 KiB of shared memory): entry (k, v) of lane l lies in bank l, so a
-// warp's 32 lookups never conflict. Lane registers are moved into place with
-// x^(8*(31-j)*len/32) and XOR-reduced as in the coalesced kernels. One CTA of
-// 1024 threads per SM. Units must be multiples of 512 bytes.
-constexpr int kRepWords = 4 * 256 * 32;
-constexpr int kRepBytes = kRepWords * 4;
+// When both sides of a copy are HBM the CRC lookups, not the bytes, limit the
+// coalesced kernels: slicing-by-16 lookups of 32 random bytes hit a 256-word
+// table with ~3.5-way bank conflicts. Here lane j takes the 64 contiguous bytes
+// [64j, 64j+64) of every 2 KiB warp step (four 16-byte loads; a warp still
+// reads 2 KiB contiguous per step), runs its register straight through them
+// with slicing-by-4, and jumps it 1984 bytes ahead between steps. The four
+// slicing-by-4 tables are replicated once per lane (128 KiB): entry (k, v) of
+// lane l lies in bank l, so those lookups never conflict; only the four jump
+// lookups per 64 bytes use shared, conflicting tables. One 1024-thread CTA per SM.
+constexpr int kRepWords = 4 * 256 * 32;                 // replicated T_0..T_3
+constexpr int kWideSmemBytes = (kRepWords + 4 * 256) * 4;
+constexpr int kWideStep = 2048;
 
-__device__ __forceinline__ void load_rep_tables(uint32_t* tb) {
-    const uint32_t* g = &g_tables.t[0][0];   // slots 0..3 hold T_0..T_3
+__device__ __forceinline__ void load_wide_tables(uint32_t* tb) {
+    const uint32_t* g = &g_tables.t[0][0];
     for (int i = threadIdx.x; i < kRepWords; i += blockDim.x) tb[i] = g[i >> 5];
+    for (int i = threadIdx.x; i < 4 * 256; i += blockDim.x) tb[kRepWords + i] = g[24 * 256 + i];
 }
 
-// r <- raw(r, 4 bytes of w), little-endian byte order; tl = tables + lane.
+// r <- raw(r, 4 bytes of w), little-endian byte order; tl = replicated tables + lane.
 __device__ __forceinline__ uint32_t crc_word(const uint32_t* tl, uint32_t r, uint32_t w) {
     const uint32_t x = r ^ w;
     return tl[(768 + (x & 255)) << 5] ^ tl[(512 + ((x >> 8) & 255)) << 5] ^ tl[(256 + ((x >> 16) & 255)) << 5] ^
            tl[(x >> 24) << 5];
 }
 
-__device__ __forceinline__ uint32_t crc_vec(const uint32_t* tl, uint32_t r, const uint4& v) {
-    r = crc_word(tl, r, v.x);
-    r = crc_word(tl, r, v.y);
-    r = crc_word(tl, r, v.z);
-    return crc_word(tl, r, v.w);
+// r * x^(8*1984) mod P: four lookups in T_1980..T_1983.
+__device__ __forceinline__ uint32_t crc_jump(const uint32_t* far, uint32_t r) {
+    return far[3 * 256 + (r & 255)] ^ far[2 * 256 + ((r >> 8) & 255)] ^ far[256 + ((r >> 16) & 255)] ^ far[r >> 24];
 }
 
-// One warp over one unit of `len` bytes (len % 512 == 0), lane-contiguous.
-template <bool STORE, bool CRC>
-__device__ __forceinline__ uint32_t warp_unit_hbm(const uint32_t* tl, const char* __restrict__ src,
-                                                  char* __restrict__ dst, int64_t len, int lane, bool tail,
-                                                  const kvsnap_span& sp, int valid) {
-    const int64_t seg = len >> 5;
-    const int64_t base = (int64_t)lane * seg;
+// One warp over one unit of `len` bytes (a multiple of 16), front-padded with
+// zeros to whole 2 KiB steps (a zero prefix leaves a zero-started raw CRC as is).
+// Returns the lane's register; the caller multiplies by x^(8*64*(31-lane)).
+template <bool STORE, bool CRC, bool TAIL>
+__device__ __forceinline__ uint32_t warp_unit_wide(const uint32_t* tl, const uint32_t* far,
+                                                   const char* __restrict__ src, char* __restrict__ dst, int64_t len,
+                                                   int lane, const kvsnap_span& sp, int valid) {
+    const int64_t steps = (len + kWideStep - 1) / kWideStep;
+    const int64_t first = (int64_t)lane * 64 - (steps * kWideStep - len);
     uint32_t r = 0;
-    int64_t at = 0;
-    for (; at + 64 <= seg; at += 64) {
+    for (int64_t t = 0; t < steps; ++t) {
         uint4 v[4];
 #pragma unroll
-        for (int k = 0; k < 4; ++k) v[k] = *reinterpret_cast<const uint4*>(src + base + at + 16 * k);
+        for (int k = 0; k < 4; ++k) {
+            const int64_t at = first + t * kWideStep + 16 * k;
+            v[k] = at >= 0 ? *reinterpret_cast<const uint4*>(src + at) : make_uint4(0, 0, 0, 0);
+        }
 #pragma unroll
         for (int k = 0; k < 4; ++k) {
-            if (tail) v[k] = mask_tail<16>(v[k], base + at + 16 * k, sp, valid);
-            if (STORE) *reinterpret_cast<uint4*>(dst + base + at + 16 * k) = v[k];
+            const int64_t at = first + t * kWideStep + 16 * k;
+            if (at >= 0) {
+                if (TAIL) v[k] = mask_tail<16>(v[k], at, sp, valid);
+                if (STORE) *reinterpret_cast<uint4*>(dst + at) = v[k];
+            }
         }
         if (CRC) {
+            r = crc_jump(far, r);
 #pragma unroll
-            for (int k = 0; k < 4; ++k) r = crc_vec(tl, r, v[k]);
+            for (int k = 0; k < 4; ++k) {
+                r = crc_word(tl, r, v[k].x);
+                r = crc_word(tl, r, v[k].y);
+                r = crc_word(tl, r, v[k].z);
+                r = crc_word(tl, r, v[k].w);
+            }
         }
     }
-    for (; at < seg; at += 16) {
-        uint4 v = *reinterpret_cast<const uint4*>(src + base + at);
-        if (tail) v = mask_tail<16>(v, base + at, sp, valid);
-        if (STORE) *reinterpret_cast<uint4*>(dst + base + at) = v;
-        if (CRC) r = crc_vec(tl, r, v);
-    }
     return r;
+}
+
+// The last block of a save, whose tail token slots are written as zeros: kept
+// out of line so the common path's registers stay free of the masking code.
+__device__ __noinline__ uint32_t wide_tail_unit(const uint32_t* tl, const uint32_t* far, const char* src, char* dst,
+                                                const kvsnap_span& sp, int lane, int valid) {
+    return warp_unit_wide<true, true, true>(tl, far, src, dst, sp.bytes, lane, sp, valid);
 }
 
 template <int MODE>
 __global__ void __launch_bounds__(1024, 1) span_kernel_hbm(SpanArgs a) {
     extern __shared__ uint32_t tb[];
     const bool crc = a.crc != nullptr;
-    if (crc) load_rep_tables(tb);
+    if (crc) load_wide_tables(tb);
     __syncthreads();
     if (MODE == kScatter && a.gate && *a.gate) return;
     const int lane = threadIdx.x & 31;
     const uint32_t* tl = tb + lane;
-    int64_t shift_for = -1;
-    uint32_t lane_shift = 0;
+    const uint32_t* far = tb + kRepWords;
+    const uint32_t lane_shift = crc ? dev_xpow8n(64 * (31 - lane)) : 0;
     const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
     const int64_t units = a.n * a.nspans;
     for (int64_t u = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); u < units; u += warps) {
@@ -385,7 +402,7 @@ __global__ void __launch_bounds__(1024, 1) span_kernel_hbm(SpanArgs a) {
         }
         const int64_t packed = a.packed[i] + sp.offset;
         const int64_t cache = sp.base + block * sp.pitch;
-        if (((packed | cache) & 15) || (sp.bytes & 511)) {
+        if ((packed | cache | sp.bytes) & 15) {
             if (lane == 0) flag(a.status, KVSNAP_DP_MISALIGNED);
             continue;
         }
@@ -393,40 +410,42 @@ __global__ void __launch_bounds__(1024, 1) span_kernel_hbm(SpanArgs a) {
         char* dst = reinterpret_cast<char*>(MODE == kGather ? packed : cache);
         const bool tail = MODE == kGather && a.valid > 0 && i == a.n - 1;
         if (crc) {
-            if (sp.bytes != shift_for) {
-                lane_shift = dev_xpow8n((uint64_t)(31 - lane) * uint64_t(sp.bytes >> 5));
-                shift_for = sp.bytes;
-            }
-            uint32_t r = warp_unit_hbm<true, true>(tl, src, dst, sp.bytes, lane, tail, sp, a.valid);
+            uint32_t r = tail ? wide_tail_unit(tl, far, src, dst, sp, lane, a.valid)
+                              : warp_unit_wide<true, true, false>(tl, far, src, dst, sp.bytes, lane, sp, 0);
             r = gf_mulmod(warp_xor(gf_mulmod(r, lane_shift)), sp.crc_shift);
             if (lane == 0) atomicXor(&a.crc[i], r);
+        } else if (tail) {
+            wide_tail_unit(tl, far, src, dst, sp, lane, a.valid);
         } else {
-            warp_unit_hbm<true, false>(tl, src, dst, sp.bytes, lane, tail, sp, a.valid);
+            warp_unit_wide<true, false, false>(tl, far, src, dst, sp.bytes, lane, sp, 0);
         }
     }
 }
 
 __global__ void __launch_bounds__(1024, 1) crc_kernel_hbm(const int64_t* addrs, int64_t n, int64_t block_bytes,
-                                                          int64_t piece, uint32_t* crc, uint32_t* status) {
+                                                          uint32_t* crc, uint32_t* status) {
     extern __shared__ uint32_t tb[];
-    load_rep_tables(tb);
+    load_wide_tables(tb);
     __syncthreads();
     const int lane = threadIdx.x & 31;
     const uint32_t* tl = tb + lane;
-    const uint32_t lane_shift = dev_xpow8n((uint64_t)(31 - lane) * uint64_t(piece >> 5));
-    const int64_t pieces = block_bytes / piece;
+    const uint32_t* far = tb + kRepWords;
+    const uint32_t lane_shift = dev_xpow8n(64 * (31 - lane));
+    constexpr int64_t piece = 64 << 10;
+    const int64_t pieces = (block_bytes + piece - 1) / piece;
     const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
     kvsnap_span none{};
     for (int64_t u = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); u < n * pieces; u += warps) {
         const int64_t i = u / pieces, p = u - i * pieces;
-        const int64_t base = addrs[i] + p * piece;
-        if (base & 15) {
+        const int64_t at = p * piece, len = min(piece, block_bytes - at);
+        const int64_t base = addrs[i] + at;
+        if ((base | len) & 15) {
             if (lane == 0) flag(status, KVSNAP_DP_MISALIGNED);
             continue;
         }
-        uint32_t r = warp_unit_hbm<false, true>(tl, reinterpret_cast<const char*>(base), nullptr, piece, lane, false,
-                                                none, 0);
-        r = gf_mulmod(warp_xor(gf_mulmod(r, lane_shift)), dev_xpow8n(uint64_t(block_bytes - (p + 1) * piece)));
+        uint32_t r = warp_unit_wide<false, true, false>(tl, far, reinterpret_cast<const char*>(base), nullptr, len,
+                                                        lane, none, 0);
+        r = gf_mulmod(warp_xor(gf_mulmod(r, lane_shift)), dev_xpow8n(uint64_t(block_bytes - at - len)));
         if (lane == 0) atomicXor(&crc[i], r);
     }
 }
@@ -544,8 +563,17 @@ constexpr int kShaSlotWords = 64 * 32;
 __device__ __forceinline__ void named_arrive(int id) { asm volatile("bar.arrive %0, 64;" ::"r"(id) : "memory"); }
 __device__ __forceinline__ void named_sync(int id) { asm volatile("bar.sync %0, 64;" ::"r"(id) : "memory"); }
 
+// a + c issued as a multiply-add (`one` is 1 at run time, so the compiler
+// cannot fold it into an add): it runs on the FMA pipe and leaves the integer
+// ALU, which the rotations and logic ops keep busy, to them.
+__device__ __forceinline__ uint32_t fadd(uint32_t a, uint32_t one, uint32_t c) {
+    uint32_t d;
+    asm("mad.lo.u32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(one), "r"(c));
+    return d;
+}
+
 __global__ void __launch_bounds__(64 * kShaPairs) sha256_kernel(const int64_t* addrs, int64_t n,
-                                                               int64_t block_bytes, uint8_t* out) {
+                                                               int64_t block_bytes, uint8_t* out, uint32_t one) {
     extern __shared__ uint32_t ring[];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int pair = warp >> 1;
@@ -567,10 +595,31 @@ __global__ void __launch_bounds__(64 * kShaPairs) sha256_kernel(const int64_t* a
         const unsigned char* p = reinterpret_cast<const unsigned char*>(addrs[live ? i : n - 1]);
         const bool aligned = (reinterpret_cast<uintptr_t>(p) & 15) == 0;
         const uint64_t bits = uint64_t(block_bytes) * 8;
+        const uint4* q = reinterpret_cast<const uint4*>(p);
+        uint4 next[4];
+        if (aligned && full > 0) {
+#pragma unroll
+            for (int k = 0; k < 4; ++k) next[k] = __ldcs(q + k);
+        }
         for (int64_t c = 0; c < chunks; ++c) {
             const int s = int(c % kShaSlots);
             uint32_t w[16];
-            sha256_words(p, aligned, c, full, rest, bits, w);
+            if (aligned && c < full) {
+                // This chunk's words, then the next chunk's loads in flight under the expansion.
+#pragma unroll
+                for (int k = 0; k < 4; ++k) {
+                    w[4 * k + 0] = be32(next[k].x);
+                    w[4 * k + 1] = be32(next[k].y);
+                    w[4 * k + 2] = be32(next[k].z);
+                    w[4 * k + 3] = be32(next[k].w);
+                }
+                if (c + 1 < full) {
+#pragma unroll
+                    for (int k = 0; k < 4; ++k) next[k] = __ldcs(q + 4 * (c + 1) + k);
+                }
+            } else {
+                sha256_words(p, aligned, c, full, rest, bits, w);
+            }
             if (c >= kShaSlots) named_sync(empty_id + s);
             uint32_t* slot = slots + s * kShaSlotWords + lane;
 #pragma unroll
@@ -597,16 +646,26 @@ __global__ void __launch_bounds__(64 * kShaPairs) sha256_kernel(const int64_t* a
         uint32_t a = h[0], b = h[1], cc = h[2], d = h[3], e = h[4], f = h[5], g = h[6], k = h[7];
 #pragma unroll
         for (int t = 0; t < 64; ++t) {
-            const uint32_t t1 = k + (rotr(e, 6) ^ rotr(e, 11) ^ rotr(e, 25)) + ((e & f) ^ (~e & g)) + slot[t * 32];
-            const uint32_t t2 = (rotr(a, 2) ^ rotr(a, 13) ^ rotr(a, 22)) + ((a & b) ^ (a & cc) ^ (b & cc));
+            // The round, reassociated so the new e is one add after Sigma1 and Ch:
+            // e' = (d + h + W + K) + Sigma1(e) + Ch(e,f,g), with d + h + W + K
+            // formed off the critical path from values known rounds earlier.
+            const uint32_t hk = fadd(k, one, slot[t * 32]);
+            const uint32_t dhk = fadd(d, one, hk);
+            const uint32_t ch = (e & f) ^ (~e & g);
+            const uint32_t s1 = rotr(e, 6) ^ rotr(e, 11) ^ rotr(e, 25);
+            const uint32_t e_new = fadd(s1, one, fadd(ch, one, dhk));
+            const uint32_t t1 = fadd(s1, one, fadd(ch, one, hk));
+            const uint32_t s0 = rotr(a, 2) ^ rotr(a, 13) ^ rotr(a, 22);
+            const uint32_t maj = (a & b) ^ (a & cc) ^ (b & cc);
+            const uint32_t a_new = t1 + s0 + maj;
             k = g;
             g = f;
             f = e;
-            e = d + t1;
+            e = e_new;
             d = cc;
             cc = b;
             b = a;
-            a = t1 + t2;
+            a = a_new;
         }
         named_arrive(empty_id + s);
         h[0] += a; h[1] += b; h[2] += cc; h[3] += d; h[4] += e; h[5] += f; h[6] += g; h[7] += k;
@@ -743,12 +802,12 @@ int launch_spans(const kvsnap_span* spans, int nspans, uint64_t block_bytes, con
             static bool configured = false;
             if (!configured) {
                 check(cudaFuncSetAttribute(span_kernel_hbm<MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                           kRepBytes));
+                                           kWideSmemBytes));
                 configured = true;
             }
             const int64_t want = (n * nspans + 31) / 32;
             const int grid = ctas > 0 ? ctas : int(want < sms ? want : sms);
-            span_kernel_hbm<MODE><<<grid, 1024, crc ? kRepBytes : 0, s>>>(a);
+            span_kernel_hbm<MODE><<<grid, 1024, crc ? kWideSmemBytes : 0, s>>>(a);
             check(cudaGetLastError());
             if (crc) finish(crc, expect, n, block_bytes, status, s);
             return;
@@ -795,19 +854,16 @@ extern "C" int kvsnap_dp_crc32c(const int64_t* addrs, int64_t n, uint64_t block_
         const int sms = enter_stream(stream);
         cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
         check(cudaMemsetAsync(crc_out, 0, sizeof(uint32_t) * size_t(n), s));
-        // Device-memory blocks: lane-contiguous pieces of the largest power of two
-        // up to 64 KiB dividing the block, when that is a multiple of 512 bytes.
-        int64_t piece = int64_t(block_bytes & (~block_bytes + 1));
-        if (piece > kPiece) piece = kPiece;
-        if (hbm && vec == 16 && piece >= 512) {
+        if (hbm && vec == 16) {
             static bool configured = false;
             if (!configured) {
-                check(cudaFuncSetAttribute(crc_kernel_hbm, cudaFuncAttributeMaxDynamicSharedMemorySize, kRepBytes));
+                check(cudaFuncSetAttribute(crc_kernel_hbm, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           kWideSmemBytes));
                 configured = true;
             }
-            const int64_t want = (n * (int64_t(block_bytes) / piece) + 31) / 32;
+            const int64_t want = (n * ((int64_t(block_bytes) + kPiece - 1) / kPiece) + 31) / 32;
             const int grid = ctas > 0 ? ctas : int(want < sms ? want : sms);
-            crc_kernel_hbm<<<grid, 1024, kRepBytes, s>>>(addrs, n, int64_t(block_bytes), piece, crc_out, status);
+            crc_kernel_hbm<<<grid, 1024, kWideSmemBytes, s>>>(addrs, n, int64_t(block_bytes), crc_out, status);
             check(cudaGetLastError());
             finish(crc_out, expect, n, block_bytes, status, s);
             return;
@@ -840,7 +896,7 @@ extern "C" int kvsnap_dp_sha256(const int64_t* addrs, int64_t n, uint64_t block_
         }
         const int64_t per_cta = 32 * kShaPairs;
         sha256_kernel<<<int((n + per_cta - 1) / per_cta), 64 * kShaPairs, smem, s>>>(addrs, n,
-                                                                                    int64_t(block_bytes), out);
+                                                                                    int64_t(block_bytes), out, 1u);
         check(cudaGetLastError());
     });
 }

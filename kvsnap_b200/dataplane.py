@@ -348,6 +348,10 @@ class TorchBlockDataPlane:
         if self.save_mode not in ("staged", "direct") or self.restore_mode not in ("staged", "direct"):
             raise ValueError("save_mode and restore_mode are 'staged' or 'direct'")
         self.ctas = ctas
+        # Kernels that read or write pinned memory in place are bound by the host
+        # link, which 16-32 CTAs already saturate; the rest of the GPU stays free
+        # for the engine and the SHA-256 kernel.
+        self.host_ctas = ctas or 32
         self.pool = CudaPool(capacity_bytes, device.index)
 
     # ---- registration-time tables ------------------------------------------------------------
@@ -381,7 +385,7 @@ class TorchBlockDataPlane:
             host = torch.frombuffer(bytearray(bytes(spans)), dtype=torch.uint8)
             self._span_vec = vec
             # Device-side copies may use the lane-contiguous HBM kernels.
-            self._hbm = _abi.HBM if vec == 16 and all(layer["bytes"] % 512 == 0 for layer in self.layers) else 0
+            self._hbm = _abi.HBM if vec == 16 else 0
             self._min_blocks = min(t.shape[0] for t in self.caches.values())
             self._span_table = host.to(self._device())
             self._sha_stream = torch.cuda.Stream(self._device())
@@ -576,11 +580,12 @@ class TorchBlockDataPlane:
                         self._verify(table, n, expected_crc32c, status, vec)
                     if progress is not None:
                         progress.append((None, n * size))
+                    ctas = self.ctas if staged else self.host_ctas
                     for first in range(0, n, per_launch):
                         last = min(n, first + per_launch)
                         self._check(lib.kvsnap_dp_scatter(
                             spans.data_ptr(), len(self.layers), size, table[first:].data_ptr(),
-                            table[n + first:].data_ptr(), last - first, 0, 0, 0, status.data_ptr(), vec, self.ctas,
+                            table[n + first:].data_ptr(), last - first, 0, 0, 0, status.data_ptr(), vec, ctas,
                             stream.cuda_stream))
                         launches += 1
                         done = torch.cuda.Event()
@@ -672,7 +677,7 @@ class TorchBlockDataPlane:
                         self._check(lib.kvsnap_dp_gather(
                             spans.data_ptr(), len(self.layers), size, table[first:].data_ptr(),
                             table[n + first:].data_ptr(), last - first, valid if last == n else 0, 0,
-                            status.data_ptr(), vec, self.ctas, stream.cuda_stream))
+                            status.data_ptr(), vec, self.host_ctas, stream.cuda_stream))
                         copies += 1
                     for allocation in {id(a): a for a, _ in targets}.values():
                         allocation.mark()
