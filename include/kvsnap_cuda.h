@@ -166,6 +166,31 @@ int kvsnap_dp_copy_host_blocks(const int64_t* sources, const int64_t* blocks, in
                                const int64_t* layer_pitches, const int64_t* layer_words, int64_t n_layers,
                                int ctas, uintptr_t stream);
 
+/*
+ * Tensor-parallel regroup (no reference counterpart: the reference treats a
+ * restore at another TP size as a miss, kvsnap/connector/vllm.py:9-14). This
+ * rank's cache holds H heads a layer; the snapshot was saved by `groups` times
+ * as many ranks, shard q holding heads [q*H/groups, (q+1)*H/groups). For each
+ * block i and span s, every (head, token) row of cache block blocks[i] is read
+ * from shard q's packed block at shards[i*groups + q] + src_spans[s].offset.
+ * src_spans describe one shard's packed layout (the same spans with H/groups
+ * heads; offsets from kvsnap_dp_plan). Shard addresses may be this GPU's
+ * memory or a peer's mapped with kvsnap_dp_ipc_open: the kernel reads them
+ * with plain loads over NVLink. The caller orders producer and consumer ranks.
+ */
+int kvsnap_dp_regroup(const kvsnap_span* dst_spans, const kvsnap_span* src_spans, int nspans, const int64_t* shards,
+                      int groups, const int64_t* blocks, int64_t n, uint32_t* status, int ctas, uintptr_t stream);
+
+/* Device memory from cudaMalloc, shareable with other processes through
+   kvsnap_dp_ipc_export (memory from torch's expandable segments is not). */
+int kvsnap_dp_device_alloc(size_t size, int device, void** ptr);
+int kvsnap_dp_device_free(void* ptr);
+/* A 64-byte CUDA IPC handle for an allocation made by kvsnap_dp_device_alloc. */
+int kvsnap_dp_ipc_export(void* ptr, void* handle);
+/* Map another process's allocation into this one on `device` (peer access enabled lazily). */
+int kvsnap_dp_ipc_open(const void* handle, int device, void** ptr);
+int kvsnap_dp_ipc_close(void* ptr);
+
 #ifdef __cplusplus
 }
 #endif

@@ -60,6 +60,12 @@ DP_API = {
     "kvsnap_dp_crc32c": ([_P, _I64, _U64, _P, _P, _P, C.c_int, C.c_int, _SZ], C.c_int),
     "kvsnap_dp_sha256": ([_P, _I64, _U64, _P, _SZ], C.c_int),
     "kvsnap_dp_copy_host_blocks": ([_P, _P, _I64, _P, _P, _P, _P, _I64, C.c_int, _SZ], C.c_int),
+    "kvsnap_dp_regroup": ([_P, _P, C.c_int, _P, C.c_int, _P, _I64, _P, C.c_int, _SZ], C.c_int),
+    "kvsnap_dp_device_alloc": ([_SZ, C.c_int, C.POINTER(C.c_void_p)], C.c_int),
+    "kvsnap_dp_device_free": ([_P], C.c_int),
+    "kvsnap_dp_ipc_export": ([_P, _P], C.c_int),
+    "kvsnap_dp_ipc_open": ([_P, C.c_int, C.POINTER(C.c_void_p)], C.c_int),
+    "kvsnap_dp_ipc_close": ([_P], C.c_int),
 }
 
 IO_API = {

@@ -28,6 +28,7 @@
 
 #include <cstdint>
 #include <cstdio>
+#include <cstring>
 
 #include "kvsnap_cuda.h"
 #include "kvsnap_internal.h"
@@ -701,6 +702,72 @@ __global__ void __launch_bounds__(256) copy_host_blocks_kernel(const int64_t* so
     }
 }
 
+// ---- tensor-parallel regroup ---------------------------------------------------------
+//
+// Restore at TP size T of a snapshot saved at TP size T*g: each of this rank's
+// cache blocks takes its heads from g source shards, shard q holding heads
+// [q*H/g, (q+1)*H/g) of every layer. The shards' packed blocks may sit in
+// this GPU's memory or a peer GPU's (mapped over NVLink with CUDA IPC); the
+// kernel reads them with plain loads, so the transfer over NVLink is fused with
+// the interleave into the cache rows. No multicast, no waits on other GPUs:
+// the host orders the ranks before and after the launch.
+
+// Byte offset of row (head, token) inside a dense [H, N, C] block span whose
+// token slots are `token_pitch` bytes apart: head-major when a token slot is
+// one row, token-major otherwise.
+__device__ __forceinline__ int64_t row_at(const kvsnap_span& sp, int64_t head, int64_t token) {
+    const int64_t heads = sp.bytes / (int64_t(sp.tokens) * sp.row_bytes);
+    const int64_t head_pitch = sp.token_pitch == sp.row_bytes ? int64_t(sp.tokens) * sp.row_bytes : sp.row_bytes;
+    (void)heads;
+    return head * head_pitch + token * sp.token_pitch;
+}
+
+struct RegroupArgs {
+    const kvsnap_span* dst;      // this rank's registered spans (the cache)
+    const kvsnap_span* src;      // one shard's packed layout: same spans, heads / groups
+    int nspans;
+    const int64_t* shards;       // shard q of block i at shards[i * groups + q]
+    int groups;
+    const int64_t* blocks;       // this rank's cache block ids
+    int64_t n;
+    uint32_t* status;
+};
+
+__global__ void __launch_bounds__(256) regroup_kernel(RegroupArgs a) {
+    const int lane = threadIdx.x & 31;
+    const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
+    const int64_t units = a.n * a.nspans;
+    for (int64_t u = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); u < units; u += warps) {
+        const int64_t i = u / a.nspans;
+        const int s = int(u - i * a.nspans);
+        const kvsnap_span d = a.dst[s], sp = a.src[s];
+        const int64_t block = a.blocks[i];
+        if (block < 0 || block >= d.nblocks) {
+            if (lane == 0) flag(a.status, KVSNAP_DP_BAD_BLOCK);
+            continue;
+        }
+        const int64_t rows_per_shard = sp.bytes / sp.row_bytes;   // heads/g x tokens
+        const int64_t shard_heads = rows_per_shard / sp.tokens;
+        const int64_t row = d.row_bytes;
+        char* cache = reinterpret_cast<char*>(d.base + block * d.pitch);
+        if ((row & 15) || (reinterpret_cast<uintptr_t>(cache) & 15) || sp.row_bytes != row) {
+            if (lane == 0) flag(a.status, KVSNAP_DP_MISALIGNED);
+            continue;
+        }
+        const int64_t vecs_per_row = row / 16;
+        const int64_t total = a.groups * rows_per_shard * vecs_per_row;
+        for (int64_t v = lane; v < total; v += 32) {
+            const int64_t q = v / (rows_per_shard * vecs_per_row);
+            const int64_t rest = v - q * rows_per_shard * vecs_per_row;
+            const int64_t r = rest / vecs_per_row, k = rest - r * vecs_per_row;
+            const int64_t h = r / sp.tokens, t = r - h * sp.tokens;     // head within the shard, token
+            const char* shard = reinterpret_cast<const char*>(a.shards[i * a.groups + q]);
+            const uint4 x = *reinterpret_cast<const uint4*>(shard + sp.offset + row_at(sp, h, t) + 16 * k);
+            *reinterpret_cast<uint4*>(cache + row_at(d, q * shard_heads + h, t) + 16 * k) = x;
+        }
+    }
+}
+
 // ---- host side ----------------------------------------------------------------------
 
 struct Fail {
@@ -915,4 +982,54 @@ extern "C" int kvsnap_dp_copy_host_blocks(const int64_t* sources, const int64_t*
                                                      layer_pitches, layer_words, n_layers);
         check(cudaGetLastError());
     });
+}
+
+extern "C" int kvsnap_dp_regroup(const kvsnap_span* dst_spans, const kvsnap_span* src_spans, int nspans,
+                                 const int64_t* shards, int groups, const int64_t* blocks, int64_t n,
+                                 uint32_t* status, int ctas, uintptr_t stream) {
+    return guarded([&] {
+        if (n < 0 || nspans <= 0 || groups <= 0 || !dst_spans || !src_spans) throw Fail{"invalid regroup request"};
+        if (n == 0) return;
+        if (!shards || !blocks) throw Fail{"regroup needs shard and block tables"};
+        const int sms = enter_stream(stream);
+        cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+        RegroupArgs a{dst_spans, src_spans, nspans, shards, groups, blocks, n, status};
+        regroup_kernel<<<grid_for(n * nspans, ctas, sms), 256, 0, s>>>(a);
+        check(cudaGetLastError());
+    });
+}
+
+extern "C" int kvsnap_dp_device_alloc(size_t size, int device, void** ptr) {
+    return guarded([&] {
+        if (!ptr || size == 0) throw Fail{"device allocation needs a size and an output"};
+        check(cudaSetDevice(device));
+        check(cudaMalloc(ptr, size));
+    });
+}
+
+extern "C" int kvsnap_dp_device_free(void* ptr) {
+    return guarded([&] { check(cudaFree(ptr)); });
+}
+
+extern "C" int kvsnap_dp_ipc_export(void* ptr, void* handle) {
+    return guarded([&] {
+        if (!ptr || !handle) throw Fail{"IPC export needs a device pointer and a 64-byte output"};
+        cudaIpcMemHandle_t h;
+        check(cudaIpcGetMemHandle(&h, ptr));
+        memcpy(handle, &h, sizeof(h));
+    });
+}
+
+extern "C" int kvsnap_dp_ipc_open(const void* handle, int device, void** ptr) {
+    return guarded([&] {
+        if (!handle || !ptr) throw Fail{"IPC open needs a handle and an output"};
+        cudaIpcMemHandle_t h;
+        memcpy(&h, handle, sizeof(h));
+        check(cudaSetDevice(device));
+        check(cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess));
+    });
+}
+
+extern "C" int kvsnap_dp_ipc_close(void* ptr) {
+    return guarded([&] { check(cudaIpcCloseMemHandle(ptr)); });
 }

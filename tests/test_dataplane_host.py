@@ -1,0 +1,188 @@
+"""Host-side logic of the data plane on a CPU: the C ABI's exports, registration, and the span plan.
+
+No kernel runs here. Registration runs on CPU tensors that report a CUDA
+device (as the reference's own layout tests do), with the pinned pool
+replaced by a mock. Its results must equal what the reference recorded
+(tests/golden/golden.json): accept/reject, the ``layers`` metadata that
+becomes the snapshot identity, and ``block_bytes``. The span plan and the way
+the CUDA kernels combine partial CRCs are checked against the oracle.
+"""
+import ctypes as C
+import re
+from pathlib import Path
+from types import SimpleNamespace
+from unittest.mock import patch
+
+import numpy as np
+import pytest
+import torch
+
+from cases import GOLDEN, golden_case
+from oracle import oracle
+
+ROOT = Path(__file__).resolve().parents[1]
+
+
+class OnCuda:
+    """A CPU tensor that reports a CUDA device, for registration's device check."""
+    device = SimpleNamespace(type="cuda", index=0)
+
+    def __init__(self, tensor):
+        self._tensor = tensor
+
+    def __getattr__(self, name):
+        return getattr(self._tensor, name)
+
+    def __getitem__(self, index):
+        item = self._tensor[index]
+        return OnCuda(item) if isinstance(item, torch.Tensor) and item.ndim >= 3 else item
+
+    def permute(self, *dims):
+        return OnCuda(self._tensor.permute(*dims))
+
+
+def register(caches, block_size=16):
+    from kvsnap_b200.dataplane import TorchBlockDataPlane
+    with patch("kvsnap_b200.dataplane.CudaPool"):
+        return TorchBlockDataPlane({k: OnCuda(v) for k, v in caches.items()}, block_size, 1 << 20)
+
+
+def declared(header):
+    text = (ROOT / "include" / header).read_text()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(kvsnap_\w+)\s*\(", text)))
+
+
+def test_every_declared_entry_point_is_exported():
+    from kvsnap_b200 import build
+    cuda = C.CDLL(str(build.build_cuda()))
+    io = C.CDLL(str(build.build_io()))
+    cuda_symbols = declared("kvsnap_cuda.h")
+    io_symbols = declared("kvsnap_io.h")
+    assert "kvsnap_pool_reserve" in cuda_symbols and "kvsnap_dp_gather" in cuda_symbols
+    assert "kvsnap_crc32c_extend" in io_symbols
+    for name in cuda_symbols:
+        assert hasattr(cuda, name), name
+    for name in io_symbols:
+        assert hasattr(io, name), name
+
+
+def test_abi_versions_and_span_layout_load_without_a_gpu():
+    from kvsnap_b200 import _abi
+    from kvsnap_b200.dataplane import _dp, _load
+    lib = _dp(_load())
+    assert lib.kvsnap_pool_abi_version() == _abi.POOL_ABI_VERSION == 2
+    assert lib.kvsnap_dp_abi_version() == _abi.DP_ABI_VERSION
+    assert C.sizeof(_abi.Span) == 64
+    for data in (b"", b"123456789", bytes(range(256)) * 9):
+        assert lib.kvsnap_dp_crc32c_host(data, len(data), 0) == oracle.crc32c(data)
+    assert lib.kvsnap_dp_crc32c_host(b"456789", 6, oracle.crc32c(b"123")) == 0xE3069283
+
+
+def test_missing_library_fails_loudly(tmp_path, monkeypatch):
+    from kvsnap_b200.dataplane import CudaPool
+    monkeypatch.setenv("KVSNAP_CUDA_LIBRARY", str(tmp_path / "absent.so"))
+    with pytest.raises(RuntimeError, match="not found"):
+        CudaPool(1 << 20)
+
+
+@pytest.mark.parametrize("row", GOLDEN["registration"], ids=lambda r: str(r["strides"]))
+def test_registration_matches_the_reference(row):
+    storage = torch.zeros(5 * max(row["strides"][0], 96) + 256, dtype=torch.bfloat16)
+    cache = storage.as_strided((5, 3, 4, 8), row["strides"])
+    if row["accepted"]:
+        plane = register({"layer.0": cache}, 4)
+        assert plane.block_bytes == row["block_bytes"]
+        assert plane.layers == row["layers"]
+    else:
+        with pytest.raises(ValueError):
+            register({"layer.0": cache}, 4)
+
+
+def test_registration_rejects_what_the_reference_rejects():
+    with pytest.raises(ValueError, match="empty"):
+        register({})
+    bad = torch.zeros((4, 8, 16, 128), dtype=torch.bfloat16).permute(0, 1, 3, 2)   # C not contiguous
+    with pytest.raises(ValueError, match="unsupported KV layout"):
+        register({"x": bad})
+    with pytest.raises(ValueError, match="unsupported KV layout"):
+        register({"x": torch.zeros((4, 8, 8, 128), dtype=torch.bfloat16)})           # N != block size
+
+
+def cpu_caches(key):
+    case, storages, _ = golden_case(key)
+    if case["kind"] == "5d":
+        return case, {name: torch.from_numpy(buf).view(torch.bfloat16).view(2, case["num_blocks"], 16, 8, 128)
+                      for name, buf in storages.items()}
+    view = torch.from_numpy(storages["backing"]).view(torch.bfloat16).view(case["num_layers"], case["num_blocks"],
+                                                                           16, 8, 256)
+    return case, {f"model.layers.{i}.self_attn.attn": view[i].permute(0, 2, 1, 3) for i in range(case["num_layers"])}
+
+
+@pytest.mark.parametrize("key", ["vllm031", "qwen3_1p7b_5d", "qwen3_8b_5d"])
+def test_layers_metadata_equals_the_reference_identity(key):
+    case, caches = cpu_caches(key)
+    plane = register(caches)
+    assert plane.layers == case["layers"]
+    assert plane.block_bytes == case["block_bytes"]
+    assert list(plane.caches) == [layer["name"] for layer in case["layers"]]
+
+
+@pytest.mark.parametrize("key", ["vllm031", "qwen3_8b_5d"])
+def test_span_plan_and_crc_combination_rule(key):
+    """kvsnap_dp_plan's offsets and shifts, and the kernels' rule: CRC32C(block) =
+    ~0 ^ ~0*x^(8L) ^ XOR_s raw(span_s) * x^(8 * bytes after span s)."""
+    from kvsnap_b200 import _abi
+    from kvsnap_b200.dataplane import _dp, _load
+    case, storages, layout = golden_case(key)
+    lib = _dp(_load())
+    spans = (_abi.Span * len(layout.spans))()
+    for dst, src in zip(spans, layout.spans):
+        dst.bytes = src.bytes
+    total = C.c_uint64()
+    assert lib.kvsnap_dp_plan(spans, len(spans), C.byref(total)) == 0
+    assert total.value == layout.block_bytes
+    for dst, src in zip(spans, layout.spans):
+        assert dst.offset == src.offset
+        assert dst.crc_shift == oracle.xpow8n(layout.block_bytes - src.offset - src.bytes)
+    packed = oracle.pack(storages, layout, case["saved"], case["num_kv_tokens"])
+    init = 0xFFFFFFFF ^ oracle.gf_mulmod(0xFFFFFFFF, oracle.xpow8n(layout.block_bytes))
+    for block, (_, expected) in zip(packed, case["digests"]):
+        acc = 0
+        for span, plan in zip(layout.spans, spans):
+            raw = ~oracle.crc32c(block[span.offset:span.offset + span.bytes].tobytes(), 0xFFFFFFFF) & 0xFFFFFFFF
+            acc ^= oracle.gf_mulmod(raw, plan.crc_shift)
+        assert acc ^ init == expected
+
+
+def test_lane_partials_recombine_like_the_kernels():
+    """A warp's lanes each CRC the 16-byte vectors they load (lane j: bytes 16j + 512t),
+    and recombine with x^(8*16*(31-j)): the coalesced kernels' arithmetic, checked on the CPU."""
+    data = np.frombuffer(bytes(range(256)) * 64, dtype=np.uint8)       # 16 KiB = 32 steps of 512 bytes
+    lane_regs = []
+    for j in range(32):
+        reg = 0
+        for t in range(len(data) // 512):
+            vec = data[512 * t + 16 * j:512 * t + 16 * j + 16].tobytes()
+            raw = ~oracle.crc32c(vec, 0xFFFFFFFF) & 0xFFFFFFFF
+            reg = oracle.gf_mulmod(reg, oracle.xpow8n(512)) ^ raw
+        lane_regs.append(reg)
+    total = 0
+    for j, reg in enumerate(lane_regs):
+        total ^= oracle.gf_mulmod(reg, oracle.xpow8n(16 * (31 - j)))
+    init = 0xFFFFFFFF ^ oracle.gf_mulmod(0xFFFFFFFF, oracle.xpow8n(len(data)))
+    assert total ^ init == oracle.crc32c(data.tobytes())
+
+
+def test_runs_coalesce_like_the_reference_copy_count():
+    from kvsnap_b200.dataplane import TorchBlockDataPlane
+    size = 100
+    a, b = object(), object()
+    for chunk_blocks in (1, 2, 3, 64):
+        targets = [(a, 0), (a, 100), (a, 200), (b, 0), (a, 300), (a, 400), (b, 100), (b, 200)]
+        ours = 0
+        per = max(1, min(len(targets), chunk_blocks))
+        for first in range(0, len(targets), per):
+            ours += len(list(TorchBlockDataPlane._runs(targets, first, min(len(targets), first + per), size)))
+        keyed = [(id(x), o) for x, o in targets]
+        assert ours == oracle.save_copy_count(keyed, size, chunk_blocks * size)
