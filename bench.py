@@ -185,11 +185,19 @@ def pinned_copy_peaks(nbytes, device, repeats=5):
 class Engine:
     """The data plane's kernels launched straight through the C ABI with resident tables.
 
-    One step: gather the session into device staging (+ CRC32C), then on the
-    pool's copy stream the copy engine moves it to pinned memory while the
-    SHA-256 kernel hashes the staging on a side stream, then the scatter kernel
-    restores the pinned blocks into the other block set (reading host memory
-    in place, or via device staging with --restore-mode staged).
+    A stream of sessions through one GPU, two deep. Step k saves session k and
+    restores session k-1 (the snapshot step k-1 saved) into other blocks, the way
+    the connector's save and load threads overlap on a serving worker:
+
+    * copy stream: gather session k into device staging (CRC32C fused), then the
+      copy engine moves it to pinned memory (device to host);
+    * SHA stream k%2: SHA-256 of the staged blocks (the store's content ids);
+    * load stream: the scatter kernel reads snapshot k-1 from pinned memory in
+      place (host to device) and writes it into the restore blocks, checking
+      every block's CRC32C against the one its save computed.
+
+    The host link is full duplex, so the two copy directions overlap; staging,
+    snapshots and CRCs are double-buffered and every reuse waits on an event.
     """
 
     def __init__(self, plane, save_ids, restore_ids, ctas, restore_mode):
@@ -200,95 +208,115 @@ class Engine:
         self.lib = _dp(plane.pool.lib)
         self.spans = plane._spans()
         self.copy = plane._scatter_targets()
-        self.side = plane._sha_stream
+        self.load = plane._load_stream
+        self.sides = plane._sha_streams
         self.n = len(save_ids)
         self.size = plane.block_bytes
         self.ctas = ctas
         self.restore_mode = restore_mode
         dev = plane._device()
         n, size = self.n, self.size
-        self.stage = torch.empty(n * size, dtype=torch.uint8, device=dev)
-        self.stage2 = torch.empty(n * size, dtype=torch.uint8, device=dev) if restore_mode == "staged" else None
-        self.snapshot = plane.pool.reserve(n * size)
         i64 = dict(dtype=torch.int64, device=dev)
+        self.stage = [torch.empty(n * size, dtype=torch.uint8, device=dev) for _ in range(2)]
+        self.snapshot = [plane.pool.reserve(n * size) for _ in range(2)]
+        self.stage_addrs = [torch.tensor([st.data_ptr() + i * size for i in range(n)], **i64) for st in self.stage]
+        self.pinned_addrs = [torch.tensor([sn.pointer + i * size for i in range(n)], **i64) for sn in self.snapshot]
+        if restore_mode == "staged":
+            self.stage_in = torch.empty(n * size, dtype=torch.uint8, device=dev)
+            self.stage_in_addrs = torch.tensor([self.stage_in.data_ptr() + i * size for i in range(n)], **i64)
         self.save_ids = torch.tensor(save_ids, **i64)
         self.restore_ids = torch.tensor(restore_ids, **i64)
-        self.stage_addrs = torch.tensor([self.stage.data_ptr() + i * size for i in range(n)], **i64)
-        self.pinned_addrs = torch.tensor([self.snapshot.pointer + i * size for i in range(n)], **i64)
-        if self.stage2 is not None:
-            self.stage2_addrs = torch.tensor([self.stage2.data_ptr() + i * size for i in range(n)], **i64)
-        self.crc = torch.empty(n, dtype=torch.int32, device=dev)
+        self.crc = [torch.empty(n, dtype=torch.int32, device=dev) for _ in range(2)]
         self.crc_restore = torch.empty(n, dtype=torch.int32, device=dev)
-        self.digest = torch.empty(n * 32, dtype=torch.uint8, device=dev)
+        self.digest = [torch.empty(n * 32, dtype=torch.uint8, device=dev) for _ in range(2)]
         self.status = torch.zeros(1, dtype=torch.int32, device=dev)
         self.handle = plane.pool.handle
-        self.copy_handle = self.copy.cuda_stream
+        self.k = 0
+        self.events = {}
         self.launches_per_step = 0
 
     def _ok(self, rc):
         if rc < 0:
             raise RuntimeError(self.plane.pool.lib.kvsnap_cuda_error().decode())
 
+    def _event(self, name, k, stream, timing=False):
+        e = self.torch.cuda.Event(enable_timing=timing)
+        e.record(stream)
+        self.events[(name, k)] = e
+        return e
+
+    def _wait(self, stream, name, k):
+        e = self.events.get((name, k))
+        if e is not None:
+            stream.wait_event(e)
+
     def step(self, marks=None):
         torch, lib, n, size = self.torch, self.lib, self.n, self.size
+        k, b = self.k, self.k % 2
         nspans = len(self.plane.layers)
-        ev = (lambda: torch.cuda.Event(enable_timing=True)) if marks is not None else None
-        e = {k: ev() for k in ("t0", "gather", "sha0", "sha1", "d2h", "restore")} if marks is not None else {}
+        timing = marks is not None
         launches = 0
-        if e:
-            e["t0"].record(self.copy)
+        side = self.sides[b]
+        # ---- save session k ----
+        self._wait(self.copy, "hashed", k - 2)          # staging[b] free
+        self._wait(self.copy, "restored", k - 1)        # snapshot[b] and crc[b] free
+        t0 = self._event("t0", k, self.copy, timing)
         self._ok(lib.kvsnap_dp_gather(self.spans.data_ptr(), nspans, size, self.save_ids.data_ptr(),
-                                      self.stage_addrs.data_ptr(), n, 0, self.crc.data_ptr(), self.status.data_ptr(),
-                                      16 | self.plane._hbm, self.ctas, self.copy_handle))
+                                      self.stage_addrs[b].data_ptr(), n, 0, self.crc[b].data_ptr(),
+                                      self.status.data_ptr(), 16 | self.plane._hbm, self.ctas, self.copy.cuda_stream))
         launches += 2   # gather + CRC finish
-        gathered = torch.cuda.Event()
-        gathered.record(self.copy)
-        if e:
-            e["gather"].record(self.copy)
-        self.side.wait_event(gathered)
-        if e:
-            e["sha0"].record(self.side)
-        self._ok(lib.kvsnap_dp_sha256(self.stage_addrs.data_ptr(), n, size, self.digest.data_ptr(),
-                                      self.side.cuda_stream))
+        gathered = self._event("gathered", k, self.copy, timing)
+        side.wait_event(gathered)
+        s0 = self._event("sha0", k, side, timing)
+        self._ok(lib.kvsnap_dp_sha256(self.stage_addrs[b].data_ptr(), n, size, self.digest[b].data_ptr(),
+                                      side.cuda_stream))
         launches += 1
-        hashed = torch.cuda.Event()
-        hashed.record(self.side)
-        if e:
-            e["sha1"].record(self.side)
-        self._ok(lib.kvsnap_pool_copy(self.handle, self.snapshot.ident, 0, self.stage.data_ptr(), n * size, 1,
-                                      self.copy_handle))
-        if e:
-            e["d2h"].record(self.copy)
-        if self.restore_mode == "staged":
-            self._ok(lib.kvsnap_pool_copy(self.handle, self.snapshot.ident, 0, self.stage2.data_ptr(), n * size,
-                                          0, 0))
-            sources = self.stage2_addrs
-        else:
-            sources = self.pinned_addrs
-        staged = self.restore_mode == "staged"
-        vec = 16 | (self.plane._hbm if staged else 0)
-        self._ok(lib.kvsnap_dp_scatter(self.spans.data_ptr(), nspans, size, sources.data_ptr(),
-                                       self.restore_ids.data_ptr(), n, self.crc_restore.data_ptr(),
-                                       self.crc.data_ptr(), 0, self.status.data_ptr(), vec,
-                                       self.ctas if staged else self.plane.host_ctas, self.copy_handle))
-        launches += 2   # scatter + CRC verify finish
-        self.copy.wait_event(hashed)
-        if e:
-            e["restore"].record(self.copy)
-            marks.append(e)
+        self._event("hashed", k, side, timing)
+        self._ok(lib.kvsnap_pool_copy(self.handle, self.snapshot[b].ident, 0, self.stage[b].data_ptr(), n * size, 1,
+                                      self.copy.cuda_stream))
+        self._event("saved", k, self.copy, timing)
+        # ---- restore session k-1 (its snapshot and CRCs), concurrently ----
+        r0 = None
+        if ("saved", k - 1) in self.events:
+            p = 1 - b
+            self._wait(self.load, "saved", k - 1)
+            r0 = self._event("r0", k, self.load, timing)
+            if self.restore_mode == "staged":
+                self._ok(lib.kvsnap_pool_copy(self.handle, self.snapshot[p].ident, 0, self.stage_in.data_ptr(),
+                                              n * size, 0, 0))
+                sources, vec, ctas, stream = self.stage_in_addrs, 16 | self.plane._hbm, self.ctas, self.copy
+            else:
+                sources, vec, ctas, stream = self.pinned_addrs[p], 16, self.plane.host_ctas, self.load
+            self._ok(lib.kvsnap_dp_scatter(self.spans.data_ptr(), nspans, size, sources.data_ptr(),
+                                           self.restore_ids.data_ptr(), n, self.crc_restore.data_ptr(),
+                                           self.crc[p].data_ptr(), 0, self.status.data_ptr(), vec, ctas,
+                                           stream.cuda_stream))
+            launches += 2   # scatter + CRC verify finish
+            self._event("restored", k, stream, timing)
+        if timing:
+            marks.append((k, r0 is not None))
         self.launches_per_step = launches
+        self.k += 1
 
+    def join(self):
+        """Make the copy stream wait for everything queued on the other streams."""
+        for stream in (self.load, *self.sides):
+            e = self.torch.cuda.Event()
+            e.record(stream)
+            self.copy.wait_event(e)
 
-def phase_ms(marks):
-    """Mean per-phase device time over the timed steps."""
-    out = {"gather": [], "sha256": [], "d2h": [], "restore": [], "step": []}
-    for e in marks:
-        out["gather"].append(e["t0"].elapsed_time(e["gather"]))
-        out["sha256"].append(e["sha0"].elapsed_time(e["sha1"]))
-        out["d2h"].append(e["gather"].elapsed_time(e["d2h"]))
-        out["restore"].append(e["d2h"].elapsed_time(e["restore"]))
-        out["step"].append(e["t0"].elapsed_time(e["restore"]))
-    return {k: statistics.mean(v) for k, v in out.items()}
+    def phases(self, marks):
+        """Mean device time of each phase over the timed steps."""
+        out = {"gather": [], "sha256": [], "d2h": [], "restore": [], "save_latency": []}
+        for k, restored in marks:
+            ev = lambda name: self.events[(name, k)]   # noqa: E731
+            out["gather"].append(ev("t0").elapsed_time(ev("gathered")))
+            out["sha256"].append(ev("sha0").elapsed_time(ev("hashed")))
+            out["d2h"].append(ev("gathered").elapsed_time(ev("saved")))
+            out["save_latency"].append(max(ev("t0").elapsed_time(ev("saved")), ev("t0").elapsed_time(ev("hashed"))))
+            if restored:
+                out["restore"].append(ev("r0").elapsed_time(ev("restored")))
+        return {key: statistics.mean(v) for key, v in out.items() if v}
 
 
 def check_session(plane, save_ids, restore_ids, tokens):
@@ -420,7 +448,7 @@ def main():
     caches = make_caches(args, device)
     save_ids, restore_ids = session_blocks(args, n)
     size_guess = args.layers * 2 * BLOCK * HEADS * HEAD_DIM * 2
-    plane = TorchBlockDataPlane(caches, BLOCK, 3 * n * size_guess + (64 << 20), restore_mode=args.restore_mode,
+    plane = TorchBlockDataPlane(caches, BLOCK, 5 * n * size_guess + (64 << 20), restore_mode=args.restore_mode,
                                 ctas=args.ctas)
     plane.warm_up()
     size = plane.block_bytes
@@ -431,8 +459,8 @@ def main():
     link = pinned_copy_peaks(session, device)
     engine = Engine(plane, save_ids, restore_ids, args.ctas, args.restore_mode)
 
-    # Device-timed steps.
-    for _ in range(args.warmup):
+    # Device-timed steps: a stream of sessions, each step saving one and restoring the previous.
+    for _ in range(max(1, args.warmup)):
         engine.step()
     torch.cuda.synchronize()
     if int(engine.status.item()) != 0:
@@ -444,55 +472,73 @@ def main():
     barrier(world)
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     start.record(engine.copy)
+    for stream in (engine.load, *engine.sides):
+        stream.wait_event(start)
     for _ in range(args.steps):
         engine.step(marks)
+    engine.join()
     end.record(engine.copy)
     torch.cuda.synchronize()
     barrier(world)
     clock_info = clocks.stop()
     ms = max_over_ranks(start.elapsed_time(end) / args.steps, world)
-    phases = phase_ms(marks)
+    phases = engine.phases(marks)
     if int(engine.status.item()) != 0:
         raise RuntimeError(f"kernel status {int(engine.status.item())} during the timed steps")
-    digests_ok = True
     if args.quick:
         if rank == 0:
             print(json.dumps({"quick": True, "ms_per_step": round(ms, 3),
                               "phases_ms": {k: round(v, 3) for k, v in phases.items()}}), flush=True)
-        engine.snapshot.close()
+        for snap in engine.snapshot:
+            snap.close()
         plane.close()
         return
 
-    # End to end through the public API, host tier (one pinned allocation per block).
-    targets = [plane.pool.reserve(size) for _ in range(n)]
-    places = [(a, 0) for a in targets]
-    for _ in range(args.warmup):
-        plane.save_gather(save_ids, places, args.tokens, digests=[])
-        plane.load_scatter(restore_ids, places)
+    # End to end through the public API, host tier (one pinned allocation per block): each step the
+    # connector's save thread saves a session while its load thread restores the one saved before.
+    sets = [[plane.pool.reserve(size) for _ in range(n)] for _ in range(2)]
+    places = [[(a, 0) for a in owned] for owned in sets]
+    pool = ThreadPoolExecutor(max_workers=2)
+
+    def e2e_step(k):
+        saving = pool.submit(plane.save_gather, save_ids, places[k % 2], args.tokens, digests=[])
+        if k > 0:
+            restoring = pool.submit(plane.load_scatter, restore_ids, places[(k - 1) % 2])
+            restoring.result()
+        return saving.result()
+
+    k = 0
+    for _ in range(max(1, args.warmup)):
+        e2e_step(k)
+        k += 1
     torch.cuda.synchronize()
     barrier(world)
     t0 = time.perf_counter()
     for _ in range(args.steps):
-        out = []
-        plane.save_gather(save_ids, places, args.tokens, digests=out)
-        plane.load_scatter(restore_ids, places)
+        e2e_step(k)
+        k += 1
     torch.cuda.synchronize()
     e2e_ms = max_over_ranks((time.perf_counter() - t0) / args.steps * 1e3, world)
-    for a in targets:
-        a.close()
+    pool.shutdown()
+    for owned in sets:
+        for a in owned:
+            a.close()
     check_session(plane, save_ids, restore_ids, args.tokens)
 
-    # Restore alone through the API (the north star's per-session restore latency).
+    # One session at a time through the API: restore latency, and save latency with digests.
     with plane.staging(n) as snap:
         places = [(snap, i * size) for i in range(n)]
-        plane.save_gather(save_ids, places, args.tokens)
-        restore_times = []
+        save_times, restore_times = [], []
         for _ in range(max(3, args.steps // 2)):
             torch.cuda.synchronize()
+            t0 = time.perf_counter()
+            plane.save_gather(save_ids, places, args.tokens, digests=[])
+            save_times.append((time.perf_counter() - t0) * 1e3)
             t0 = time.perf_counter()
             plane.load_scatter(restore_ids, places)
             restore_times.append((time.perf_counter() - t0) * 1e3)
     restore_ms = max_over_ranks(statistics.median(restore_times), world)
+    save_ms = max_over_ranks(statistics.median(save_times), world)
 
     explore = {}
     if args.explore and rank == 0:
@@ -510,6 +556,7 @@ def main():
     e2e = world * 2 * session / (e2e_ms / 1e3) / 1e9
     restore_gbs = session / (phases["restore"] / 1e3) / 1e9
     gather_gbs = 2 * session / (phases["gather"] / 1e3) / 1e9
+    d2h_gbs = session / (phases["d2h"] / 1e3) / 1e9
     line = {
         "metric": METRIC, "value": round(value, 3), "unit": UNIT, "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(ms, 3), "higher_is_better": True, "scaling": "weak",
@@ -521,10 +568,11 @@ def main():
                    "kv": "bf16 N(0,1), seeded"},
         "phases_ms": {k: round(v, 3) for k, v in phases.items()},
         "restore_ms": round(restore_ms, 3),
+        "save_ms": round(save_ms, 3),
         "host_link": {"h2d_memcpy_gbs": round(link["h2d"], 2), "d2h_memcpy_gbs": round(link["d2h"], 2),
                       "restore_gbs": round(restore_gbs, 2), "restore_frac": round(restore_gbs / link["h2d"], 3),
-                      "save_d2h_gbs": round(session / (phases["d2h"] / 1e3) / 1e9, 2),
-                      "save_frac": round(session / (phases["d2h"] / 1e3) / 1e9 / link["d2h"], 3)},
+                      "save_d2h_gbs": round(d2h_gbs, 2), "save_frac": round(d2h_gbs / link["d2h"], 3),
+                      "note": "per-phase rates measured while the other direction runs concurrently"},
         "roofline": {"bound": "hbm", "kernel": "span_kernel<16,gather> (KV -> HBM staging, CRC32C)",
                      "achieved": round(gather_gbs, 1), "peak": hbm_peak, "unit": "GB/s",
                      "frac": round(gather_gbs / hbm_peak, 3), "traffic": None,
@@ -540,7 +588,8 @@ def main():
         line["cpu_baseline"] = cpu
     if rank == 0:
         print(json.dumps(line), flush=True)
-    engine.snapshot.close()
+    for snap in engine.snapshot:
+        snap.close()
     plane.close()
     if world > 1:
         import torch.distributed as dist
@@ -567,49 +616,49 @@ def explore_phases(plane, engine, save_ids, restore_ids, link):
 
     for ctas in (0, 16, 32, 64, 148, 296, 592):
         def restore():
-            lib.kvsnap_dp_scatter(engine.spans.data_ptr(), nspans, size, engine.pinned_addrs.data_ptr(),
+            lib.kvsnap_dp_scatter(engine.spans.data_ptr(), nspans, size, engine.pinned_addrs[0].data_ptr(),
                                   engine.restore_ids.data_ptr(), n, 0, 0, 0, engine.status.data_ptr(), 16, ctas,
-                                  engine.copy_handle)
+                                  engine.copy.cuda_stream)
 
         def restore_crc():
-            lib.kvsnap_dp_scatter(engine.spans.data_ptr(), nspans, size, engine.pinned_addrs.data_ptr(),
+            lib.kvsnap_dp_scatter(engine.spans.data_ptr(), nspans, size, engine.pinned_addrs[0].data_ptr(),
                                   engine.restore_ids.data_ptr(), n, engine.crc_restore.data_ptr(), 0, 0,
-                                  engine.status.data_ptr(), 16, ctas, engine.copy_handle)
+                                  engine.status.data_ptr(), 16, ctas, engine.copy.cuda_stream)
 
         def gather():
             lib.kvsnap_dp_gather(engine.spans.data_ptr(), nspans, size, engine.save_ids.data_ptr(),
-                                 engine.stage_addrs.data_ptr(), n, 0, engine.crc.data_ptr(), engine.status.data_ptr(),
-                                 16, ctas, engine.copy_handle)
+                                 engine.stage_addrs[0].data_ptr(), n, 0, engine.crc[0].data_ptr(), engine.status.data_ptr(),
+                                 16, ctas, engine.copy.cuda_stream)
 
         def gather_nocrc():
             lib.kvsnap_dp_gather(engine.spans.data_ptr(), nspans, size, engine.save_ids.data_ptr(),
-                                 engine.stage_addrs.data_ptr(), n, 0, 0, engine.status.data_ptr(), 16, ctas,
-                                 engine.copy_handle)
+                                 engine.stage_addrs[0].data_ptr(), n, 0, 0, engine.status.data_ptr(), 16, ctas,
+                                 engine.copy.cuda_stream)
 
         def scatter_hbm():
-            lib.kvsnap_dp_scatter(engine.spans.data_ptr(), nspans, size, engine.stage_addrs.data_ptr(),
+            lib.kvsnap_dp_scatter(engine.spans.data_ptr(), nspans, size, engine.stage_addrs[0].data_ptr(),
                                   engine.restore_ids.data_ptr(), n, engine.crc_restore.data_ptr(), 0, 0,
-                                  engine.status.data_ptr(), 16, ctas, engine.copy_handle)
+                                  engine.status.data_ptr(), 16, ctas, engine.copy.cuda_stream)
 
         def scatter_lc():
-            lib.kvsnap_dp_scatter(engine.spans.data_ptr(), nspans, size, engine.stage_addrs.data_ptr(),
+            lib.kvsnap_dp_scatter(engine.spans.data_ptr(), nspans, size, engine.stage_addrs[0].data_ptr(),
                                   engine.restore_ids.data_ptr(), n, engine.crc_restore.data_ptr(), 0, 0,
-                                  engine.status.data_ptr(), 16 | plane._hbm, ctas, engine.copy_handle)
+                                  engine.status.data_ptr(), 16 | plane._hbm, ctas, engine.copy.cuda_stream)
 
         def gather_lc():
             lib.kvsnap_dp_gather(engine.spans.data_ptr(), nspans, size, engine.save_ids.data_ptr(),
-                                 engine.stage_addrs.data_ptr(), n, 0, engine.crc.data_ptr(), engine.status.data_ptr(),
-                                 16 | plane._hbm, ctas, engine.copy_handle)
+                                 engine.stage_addrs[0].data_ptr(), n, 0, engine.crc[0].data_ptr(), engine.status.data_ptr(),
+                                 16 | plane._hbm, ctas, engine.copy.cuda_stream)
 
         def gather_lc_nocrc():
             lib.kvsnap_dp_gather(engine.spans.data_ptr(), nspans, size, engine.save_ids.data_ptr(),
-                                 engine.stage_addrs.data_ptr(), n, 0, 0, engine.status.data_ptr(),
-                                 16 | plane._hbm, ctas, engine.copy_handle)
+                                 engine.stage_addrs[0].data_ptr(), n, 0, 0, engine.status.data_ptr(),
+                                 16 | plane._hbm, ctas, engine.copy.cuda_stream)
 
         def gather_direct():
             lib.kvsnap_dp_gather(engine.spans.data_ptr(), nspans, size, engine.save_ids.data_ptr(),
-                                 engine.pinned_addrs.data_ptr(), n, 0, engine.crc.data_ptr(),
-                                 engine.status.data_ptr(), 16, ctas, engine.copy_handle)
+                                 engine.pinned_addrs[0].data_ptr(), n, 0, engine.crc[0].data_ptr(),
+                                 engine.status.data_ptr(), 16, ctas, engine.copy.cuda_stream)
 
         row = {}
         for name, fn, nbytes in (("restore_direct", restore, size * n), ("restore_direct_crc", restore_crc, size * n),
@@ -623,14 +672,14 @@ def explore_phases(plane, engine, save_ids, restore_ids, link):
         out[f"ctas={ctas}"] = row
 
     def sha():
-        lib.kvsnap_dp_sha256(engine.stage_addrs.data_ptr(), n, size, engine.digest.data_ptr(), engine.copy_handle)
+        lib.kvsnap_dp_sha256(engine.stage_addrs[0].data_ptr(), n, size, engine.digest[0].data_ptr(), engine.copy.cuda_stream)
 
     def d2h():
-        lib.kvsnap_pool_copy(engine.handle, engine.snapshot.ident, 0, engine.stage.data_ptr(), n * size, 1,
-                             engine.copy_handle)
+        lib.kvsnap_pool_copy(engine.handle, engine.snapshot[0].ident, 0, engine.stage[0].data_ptr(), n * size, 1,
+                             engine.copy.cuda_stream)
 
     def h2d():
-        lib.kvsnap_pool_copy(engine.handle, engine.snapshot.ident, 0, engine.stage.data_ptr(), n * size, 0, 0)
+        lib.kvsnap_pool_copy(engine.handle, engine.snapshot[0].ident, 0, engine.stage[0].data_ptr(), n * size, 0, 0)
 
     for name, fn in (("sha256", sha), ("d2h_pool", d2h), ("h2d_pool", h2d)):
         ms = timed(fn, reps=3)

@@ -67,9 +67,9 @@ int kvsnap_pool_ready(void* pool, uint64_t id);
 /* Wait, then return the bytes to the arena (reference cuda_pool.cpp:190-199). */
 int kvsnap_pool_release(void* pool, uint64_t id);
 /* Extension (no reference counterpart): record the allocation's completion
-   event on the copy stream now, so wait/ready/release also fence kernels that
-   read or write the allocation in place on that stream. */
-int kvsnap_pool_mark(void* pool, uint64_t id);
+   event on `stream` (0: the pool's copy stream) now, so wait/ready/release
+   also fence kernels queued there that read or write the allocation in place. */
+int kvsnap_pool_mark(void* pool, uint64_t id, uintptr_t stream);
 
 /* ---- 2. data-plane kernels --------------------------------------------------- */
 

@@ -43,6 +43,7 @@ struct Slot {
     cudaEvent_t done = nullptr;   // completion of the last work queued on this slot
     bool queued = false;          // some copy or kernel was queued on it
     bool done_valid = false;      // `done` was recorded after that work
+    bool foreign = false;         // that work ran on a stream other than the pool's
 };
 
 struct Arena {
@@ -72,10 +73,14 @@ struct Arena {
         return it->second;
     }
 
-    // Wait until nothing queued on `s` can still touch its bytes.
+    // Wait until nothing queued on `s` can still touch its bytes. Without a valid
+    // event the work's stream must drain; work on a foreign stream drains the device.
     void settle(Slot& s) {
         if (!s.queued) return;
-        cuda(s.done_valid ? cudaEventSynchronize(s.done) : cudaStreamSynchronize(stream));
+        if (s.done_valid)
+            cuda(cudaEventSynchronize(s.done));
+        else
+            cuda(s.foreign ? cudaDeviceSynchronize() : cudaStreamSynchronize(stream));
     }
 
     // Make the copy stream wait for everything queued on `producer` so far.
@@ -93,6 +98,7 @@ struct Arena {
     void begin(Slot& s) {
         s.queued = true;
         s.done_valid = false;
+        s.foreign = false;
     }
 
     void end(Slot& s) {
@@ -243,14 +249,17 @@ extern "C" int kvsnap_pool_copy_2d(void* pool, uint64_t id, size_t host_offset, 
     });
 }
 
-extern "C" int kvsnap_pool_mark(void* pool, uint64_t id) {
+extern "C" int kvsnap_pool_mark(void* pool, uint64_t id, uintptr_t stream) {
     return guarded([&] {
         Arena* a = live(pool);
         std::lock_guard<std::mutex> lock(a->mutex);
         Slot& s = a->slot(id);
         cuda(cudaSetDevice(a->device));
+        cudaStream_t on = stream ? reinterpret_cast<cudaStream_t>(stream) : a->stream;
         a->begin(s);
-        a->end(s);
+        s.foreign = on != a->stream;
+        cuda(cudaEventRecord(s.done, on));
+        s.done_valid = true;
     });
 }
 

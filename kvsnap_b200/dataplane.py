@@ -216,14 +216,12 @@ class PinnedAllocation:
                 self.pool.handle, self.ident, host_offset, host_pitch, device_ptr, device_pitch,
                 width, height, int(bool(to_host)), producer_stream))
 
-    def mark(self):
-        """Fence work queued on the pool's copy stream so far under this allocation's wait/ready/release.
-
-        Kernels that read or write the allocation in place run on that stream;
-        marking after them makes the allocation's lifetime cover them.
-        """
+    def mark(self, stream=0):
+        """Fence work queued so far on ``stream`` (0: the pool's copy stream) under this allocation's
+        wait/ready/release: kernels that read or write the allocation in place run there, and
+        marking after them makes the allocation's lifetime cover them."""
         with self.operation():
-            self.pool.check(self.pool.lib.kvsnap_pool_mark(self.pool.handle, self.ident))
+            self.pool.check(self.pool.lib.kvsnap_pool_mark(self.pool.handle, self.ident, stream))
 
     def wait(self):
         with self.operation():
@@ -388,7 +386,14 @@ class TorchBlockDataPlane:
             self._hbm = _abi.HBM if vec == 16 else 0
             self._min_blocks = min(t.shape[0] for t in self.caches.values())
             self._span_table = host.to(self._device())
-            self._sha_stream = torch.cuda.Stream(self._device())
+            # Side streams: restores that read pinned memory in place run on their
+            # own stream, so one can overlap a save's copies (the host link is full
+            # duplex); digests run on streams of their own, so concurrent saves'
+            # SHA-256 kernels overlap each other and the copies.
+            self._load_stream = torch.cuda.Stream(self._device())
+            self._sha_streams = [torch.cuda.Stream(self._device()) for _ in range(2)]
+            self._sha_next = 0
+            self._sha_lock = threading.Lock()
         return self._span_table
 
     def _scatter_targets(self):
@@ -549,6 +554,8 @@ class TorchBlockDataPlane:
         n, size = len(block_ids), self.block_bytes
         per_launch = max(1, chunk_bytes // size)
         staged = expected_crc32c is not None or self.restore_mode == "staged"
+        if not staged:
+            stream = self._load_stream
         launches = 0
         done = None
         with self.pool.operation():
@@ -594,10 +601,10 @@ class TorchBlockDataPlane:
                             progress.append((done, (n - last) * size))
                     if not staged:
                         for allocation in {id(a): a for a, _ in sources}.values():
-                            allocation.mark()
+                            allocation.mark(stream.cuda_stream)
                 except BaseException:
                     # A launch that failed part way may still be queued: nothing
-                    # may release the sources before the copy stream drains.
+                    # may release the sources before its stream drains.
                     stream.synchronize()
                     raise
         done.synchronize()
@@ -687,7 +694,8 @@ class TorchBlockDataPlane:
                         crc.data_ptr() if crc is not None else 0, status.data_ptr(), vec, self.ctas,
                         stream.cuda_stream))
                     if digests is not None:
-                        digest = self._sha256_after(stage, table[n:], n, stream)
+                        side = self._sha_stream()
+                        digest = self._sha256_after(stage, table[n:], n, stream, side)
                     for first in range(0, n, per_chunk):
                         for i, j in self._runs(targets, first, min(n, first + per_chunk), size):
                             allocation, offset = targets[i]
@@ -703,19 +711,24 @@ class TorchBlockDataPlane:
             allocation.wait()
         self._status_error(status)
         if digests is not None:
-            self._sha_stream.synchronize()
+            side.synchronize()
             crcs = [v & 0xFFFFFFFF for v in crc.cpu().tolist()]
             raw = digest.cpu().numpy().tobytes()
             digests.extend((raw[32 * i:32 * i + 32].hex(), crcs[i]) for i in range(n))
         return copies
 
-    def _sha256_after(self, stage, addresses, n, stream):
-        """SHA-256 of the staged blocks on a side stream, after the work queued on ``stream`` so far."""
+    def _sha_stream(self):
+        with self._sha_lock:
+            side = self._sha_streams[self._sha_next % len(self._sha_streams)]
+            self._sha_next += 1
+        return side
+
+    def _sha256_after(self, stage, addresses, n, stream, side):
+        """SHA-256 of the staged blocks on ``side``, after the work queued on ``stream`` so far."""
         torch = self.torch
         lib = _dp(self.pool.lib)
         ready = torch.cuda.Event()
         ready.record(stream)
-        side = self._sha_stream
         side.wait_event(ready)
         with torch.cuda.stream(side):
             out = torch.empty(n * 32, dtype=torch.uint8, device=addresses.device)

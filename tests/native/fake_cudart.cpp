@@ -84,6 +84,11 @@ cudaError_t cudaStreamSynchronize(cudaStream_t) {
     apply_until(enqueued);
     return cudaSuccess;
 }
+cudaError_t cudaDeviceSynchronize(void) {
+    if (fail("cudaDeviceSynchronize")) return cudaErrorInjected;
+    apply_until(enqueued);
+    return cudaSuccess;
+}
 cudaError_t cudaStreamQuery(cudaStream_t) { return queue.empty() ? cudaSuccess : cudaErrorNotReady; }
 cudaError_t cudaStreamDestroy(cudaStream_t s) {
     delete s;

@@ -22,6 +22,7 @@ cudaError_t cudaHostAlloc(void**, size_t, unsigned);
 cudaError_t cudaFreeHost(void*);
 cudaError_t cudaStreamCreateWithFlags(cudaStream_t*, unsigned);
 cudaError_t cudaStreamSynchronize(cudaStream_t);
+cudaError_t cudaDeviceSynchronize(void);
 cudaError_t cudaStreamQuery(cudaStream_t);
 cudaError_t cudaStreamDestroy(cudaStream_t);
 cudaError_t cudaStreamWaitEvent(cudaStream_t, cudaEvent_t, unsigned);

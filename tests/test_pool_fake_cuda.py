@@ -192,7 +192,7 @@ def test_mark_fences_in_place_work_under_the_allocation(lib):
         device = C.create_string_buffer(16)
         assert lib.kvsnap_pool_copy(pool, b, 0, C.addressof(device), 16, 0, 0) == 0   # other slot's copy
         assert lib.kvsnap_pool_ready(pool, a) == 1        # a has nothing queued
-        assert lib.kvsnap_pool_mark(pool, a) == 0         # e.g. a kernel read a in place after that copy
+        assert lib.kvsnap_pool_mark(pool, a, 0) == 0      # e.g. a kernel read a in place after that copy
         assert lib.kvsnap_pool_ready(pool, a) == 0
         assert lib.kvsnap_pool_wait(pool, a) == 0
         assert lib.kvsnap_pool_ready(pool, a) == 1 and lib.fake_cuda_pending() == 0
@@ -225,3 +225,19 @@ def test_destroy_quarantines_memory_it_cannot_prove_idle(lib):
     assert lib.fake_cuda_live_host_allocations() == before + 1      # leaked on purpose, never reused
     assert lib.fake_cuda_pending() == 1
     lib.fake_cuda_discard_pending()      # its target buffer is about to go away
+
+
+def test_mark_on_a_foreign_stream_drains_the_device_when_its_event_fails(lib):
+    pool = lib.kvsnap_pool_create(32, 0)
+    try:
+        rc, a, _ = reserve(lib, pool, 16)
+        rc, b, _ = reserve(lib, pool, 16)
+        device = C.create_string_buffer(16)
+        assert lib.kvsnap_pool_copy(pool, b, 0, C.addressof(device), 16, 0, 0) == 0
+        lib.fake_cuda_fail_next(b"cudaEventRecord")
+        assert lib.kvsnap_pool_mark(pool, a, 12345) == -1      # a kernel on another stream, unrecorded
+        assert lib.kvsnap_pool_ready(pool, a) == 0              # the pool cannot vouch for it
+        assert lib.kvsnap_pool_release(pool, a) == 0            # so release drains the whole device
+        assert lib.fake_cuda_pending() == 0
+    finally:
+        lib.kvsnap_pool_destroy(pool)
