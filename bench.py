@@ -523,7 +523,7 @@ def main():
     for owned in sets:
         for a in owned:
             a.close()
-    check_session(plane, save_ids, restore_ids, args.tokens)
+    digests_ok = check_session(plane, save_ids, restore_ids, args.tokens)
 
     # One session at a time through the API: restore latency, and save latency with digests.
     with plane.staging(n) as snap:

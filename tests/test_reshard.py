@@ -95,7 +95,7 @@ def _exchange_worker(rank, world, port, results):
 def test_a_failed_shard_reaches_every_rank_over_gloo():
     import torch.multiprocessing as mp
     port = 29500 + os.getpid() % 1000
-    with mp.Manager() as manager:
+    with mp.get_context("spawn").Manager() as manager:
         results = manager.dict()
         mp.start_processes(_exchange_worker, args=(2, port, results), nprocs=2, start_method="spawn")
         for rank in range(2):
