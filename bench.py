@@ -684,6 +684,36 @@ def explore_phases(plane, engine, save_ids, restore_ids, link):
     for name, fn in (("sha256", sha), ("d2h_pool", d2h), ("h2d_pool", h2d)):
         ms = timed(fn, reps=3)
         out[name] = {"ms": round(ms, 3), "gbs": round(n * size / (ms / 1e3) / 1e9, 2)}
+
+    # Both directions of the host link at once: device-to-host by the copy engine on the copy stream,
+    # host-to-device either by a second copy engine or by the scatter kernel on the load stream.
+    dev_in = torch.empty(n * size, dtype=torch.uint8, device=engine.stage[0].device)
+    pinned_in = torch.empty(n * size, dtype=torch.uint8, pin_memory=True)
+
+    def duplex(kernel):
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        start.record(engine.copy)
+        engine.load.wait_event(start)
+        for _ in range(3):
+            d2h()
+            if kernel:
+                lib.kvsnap_dp_scatter(engine.spans.data_ptr(), nspans, size, engine.pinned_addrs[1].data_ptr(),
+                                      engine.restore_ids.data_ptr(), n, 0, 0, 0, engine.status.data_ptr(), 16,
+                                      plane.host_ctas, engine.load.cuda_stream)
+            else:
+                with torch.cuda.stream(engine.load):
+                    dev_in.copy_(pinned_in, non_blocking=True)
+        done = torch.cuda.Event()
+        done.record(engine.load)
+        engine.copy.wait_event(done)
+        end.record(engine.copy)
+        torch.cuda.synchronize()
+        ms = start.elapsed_time(end) / 3
+        return {"ms_per_pair": round(ms, 3), "gbs_both": round(2 * n * size / (ms / 1e3) / 1e9, 2)}
+
+    out["duplex_dma"] = duplex(False)
+    out["duplex_dma_kernel"] = duplex(True)
     return out
 
 
