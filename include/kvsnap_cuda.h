@@ -191,6 +191,27 @@ int kvsnap_dp_ipc_export(void* ptr, void* handle);
 int kvsnap_dp_ipc_open(const void* handle, int device, void** ptr);
 int kvsnap_dp_ipc_close(void* ptr);
 
+/*
+ * Restore scatter with CRC32C verification that allocates nothing. No
+ * counterpart in the reference. For callers that cannot allocate device
+ * memory: a serving worker whose KV cache was sized to fill the GPU, or host
+ * code that must not enter an allocator that may synchronise the device. The
+ * same copy and check as kvsnap_dp_scatter with crc_out and expect, except that
+ * the per-block CRC accumulators live in one fixed scratch array inside this
+ * library (KVSNAP_DP_STATIC_MAX_BLOCKS × 4 bytes, held on every GPU that loads
+ * the library until the process exits). The caller passes inputs and outputs;
+ * the result is the cache write and the KVSNAP_DP_CRC_MISMATCH bit in *status.
+ * n above the maximum is rejected with an error and nothing is launched. The
+ * first call on a device looks up the scratch's device address; make that
+ * first call before any stream capture. Every call shares the scratch (it is
+ * cleared at the start of each call): calls whose work overlaps on the GPU race
+ * and must not be issued concurrently.
+ */
+#define KVSNAP_DP_STATIC_MAX_BLOCKS 65536
+int kvsnap_dp_scatter_verify_static(const kvsnap_span* spans, int nspans, uint64_t block_bytes,
+                                    const int64_t* sources, const int64_t* blocks, int64_t n,
+                                    const uint32_t* expect, uint32_t* status, int vec, int ctas, uintptr_t stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -66,7 +66,11 @@ DP_API = {
     "kvsnap_dp_ipc_export": ([_P, _P], C.c_int),
     "kvsnap_dp_ipc_open": ([_P, C.c_int, C.POINTER(C.c_void_p)], C.c_int),
     "kvsnap_dp_ipc_close": ([_P], C.c_int),
+    "kvsnap_dp_scatter_verify_static": ([_P, C.c_int, _U64, _P, _P, _I64, _P, _P, C.c_int, C.c_int, _SZ], C.c_int),
 }
+
+# Blocks the no-allocation verified scatter handles in one call (include/kvsnap_cuda.h).
+STATIC_MAX_BLOCKS = 65536
 
 IO_API = {
     "kvsnap_io_abi_version": ([], C.c_int),

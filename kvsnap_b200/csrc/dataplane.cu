@@ -29,6 +29,7 @@
 #include <cstdint>
 #include <cstdio>
 #include <cstring>
+#include <mutex>
 
 #include "kvsnap_cuda.h"
 #include "kvsnap_internal.h"
@@ -1032,4 +1033,51 @@ extern "C" int kvsnap_dp_ipc_open(const void* handle, int device, void** ptr) {
 
 extern "C" int kvsnap_dp_ipc_close(void* ptr) {
     return guarded([&] { check(cudaIpcCloseMemHandle(ptr)); });
+}
+
+// ---- restore scatter with CRC verification into a fixed scratch -------------------------
+//
+// For callers that cannot allocate device memory: the per-block CRC32C
+// accumulators live in this file-scope array instead of a caller buffer.
+// `g_static_crc` is a host-side stand-in in host code: its device address is
+// obtained once per device with cudaGetSymbolAddress (with that device current)
+// and passed to the kernels.
+constexpr int64_t kStaticMaxBlocks = KVSNAP_DP_STATIC_MAX_BLOCKS;
+__device__ __align__(256) uint32_t g_static_crc[kStaticMaxBlocks];
+
+namespace {
+std::mutex g_static_mutex;
+uint32_t* g_static_ptr[256];   // per device ordinal, set up on first use
+}  // namespace
+
+extern "C" int kvsnap_dp_scatter_verify_static(const kvsnap_span* spans, int nspans, uint64_t block_bytes,
+                                               const int64_t* sources, const int64_t* blocks, int64_t n,
+                                               const uint32_t* expect, uint32_t* status, int vec, int ctas,
+                                               uintptr_t stream) {
+    return guarded([&] {
+        if (n < 0 || n > kStaticMaxBlocks) throw Fail{"kvsnap_dp_scatter_verify_static: more blocks than its fixed "
+                                                      "scratch holds (KVSNAP_DP_STATIC_MAX_BLOCKS)"};
+        if (!expect || !status) throw Fail{"kvsnap_dp_scatter_verify_static needs expected CRCs and a status word"};
+        if (n == 0) return;
+        int device = 0;
+        if (stream)
+            check(cudaStreamGetDevice(reinterpret_cast<cudaStream_t>(stream), &device));
+        else
+            check(cudaGetDevice(&device));
+        if (device < 0 || device >= 256) throw Fail{"device ordinal out of range"};
+        uint32_t* scratch = nullptr;
+        {
+            std::lock_guard<std::mutex> lock(g_static_mutex);
+            if (!g_static_ptr[device]) {
+                check(cudaSetDevice(device));
+                void* ptr = nullptr;
+                check(cudaGetSymbolAddress(&ptr, g_static_crc));
+                g_static_ptr[device] = static_cast<uint32_t*>(ptr);
+            }
+            scratch = g_static_ptr[device];
+        }
+        if (launch_spans<kScatter>(spans, nspans, block_bytes, blocks, sources, n, 0, scratch, expect, nullptr,
+                                   status, vec, ctas, stream) < 0)
+            throw Fail{kvsnap_cuda_error()};
+    });
 }
