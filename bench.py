@@ -54,7 +54,7 @@ def parse():
     p.add_argument("--pool-blocks", type=int, default=32768)
     p.add_argument("--layers", type=int, default=LAYERS)
     p.add_argument("--ctas", type=int, default=0, help="CTAs for the data-plane kernels (0: library default)")
-    p.add_argument("--restore-mode", choices=["direct", "staged"], default="direct")
+    p.add_argument("--restore-mode", choices=["direct", "staged"], default="staged")
     p.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     p.add_argument("--explore", type=str, default="", help="write a per-phase / CTA sweep breakdown to this path")
     p.add_argument("--seed", type=int, default=0)
@@ -209,7 +209,9 @@ class Engine:
         self.spans = plane._spans()
         self.copy = plane._scatter_targets()
         self.load = plane._load_stream
+        self.load_copy = plane._load_copy_stream
         self.sides = plane._sha_streams
+        self.chunk = max(1, (64 << 20) // plane.block_bytes)
         self.n = len(save_ids)
         self.size = plane.block_bytes
         self.ctas = ctas
@@ -280,27 +282,58 @@ class Engine:
         if ("saved", k - 1) in self.events:
             p = 1 - b
             self._wait(self.load, "saved", k - 1)
-            r0 = self._event("r0", k, self.load, timing)
+            self._wait(self.load_copy, "saved", k - 1)
+            self._wait(self.load_copy, "restored", k - 1)   # stage_in free
+            r0 = self._event("r0", k, self.load_copy, timing)
             if self.restore_mode == "staged":
-                self._ok(lib.kvsnap_pool_copy(self.handle, self.snapshot[p].ident, 0, self.stage_in.data_ptr(),
-                                              n * size, 0, 0))
-                sources, vec, ctas, stream = self.stage_in_addrs, 16 | self.plane._hbm, self.ctas, self.copy
+                # Copy engine into device staging chunk by chunk, each chunk scattered
+                # (and its CRCs checked) from HBM as soon as it lands.
+                for first in range(0, n, self.chunk):
+                    last = min(n, first + self.chunk)
+                    self._ok(lib.kvsnap_pool_copy_on(self.handle, self.snapshot[p].ident, first * size,
+                                                     self.stage_in.data_ptr() + first * size, (last - first) * size,
+                                                     0, self.load_copy.cuda_stream))
+                    landed = torch.cuda.Event()
+                    landed.record(self.load_copy)
+                    self.load.wait_event(landed)
+                    self._ok(lib.kvsnap_dp_scatter(self.spans.data_ptr(), nspans, size,
+                                                   self.stage_in_addrs[first:].data_ptr(),
+                                                   self.restore_ids[first:].data_ptr(), last - first,
+                                                   self.crc_restore[first:].data_ptr(), self.crc[p][first:].data_ptr(),
+                                                   0, self.status.data_ptr(), 16 | self.plane._hbm, self.ctas,
+                                                   self.load.cuda_stream))
+                    launches += 2   # scatter + CRC verify finish
             else:
-                sources, vec, ctas, stream = self.pinned_addrs[p], 16, self.plane.host_ctas, self.load
-            self._ok(lib.kvsnap_dp_scatter(self.spans.data_ptr(), nspans, size, sources.data_ptr(),
-                                           self.restore_ids.data_ptr(), n, self.crc_restore.data_ptr(),
-                                           self.crc[p].data_ptr(), 0, self.status.data_ptr(), vec, ctas,
-                                           stream.cuda_stream))
-            launches += 2   # scatter + CRC verify finish
-            self._event("restored", k, stream, timing)
+                self.load.wait_event(self.events[("r0", k)])
+                self._ok(lib.kvsnap_dp_scatter(self.spans.data_ptr(), nspans, size, self.pinned_addrs[p].data_ptr(),
+                                               self.restore_ids.data_ptr(), n, self.crc_restore.data_ptr(),
+                                               self.crc[p].data_ptr(), 0, self.status.data_ptr(), 16,
+                                               self.plane.host_ctas, self.load.cuda_stream))
+                launches += 2   # scatter + CRC verify finish
+            self._event("restored", k, self.load, timing)
         if timing:
             marks.append((k, r0 is not None))
         self.launches_per_step = launches
         self.k += 1
 
+    def gather_only(self):
+        """One save gather (KV -> device staging, tail zeroing, CRC32C) on the copy stream."""
+        self._ok(self.lib.kvsnap_dp_gather(self.spans.data_ptr(), len(self.plane.layers), self.size,
+                                           self.save_ids.data_ptr(), self.stage_addrs[0].data_ptr(), self.n, 0,
+                                           self.crc[0].data_ptr(), self.status.data_ptr(), 16 | self.plane._hbm,
+                                           self.ctas, self.copy.cuda_stream))
+
+    def scatter_only(self):
+        """One restore scatter (device staging -> KV, CRC32C checked) on the copy stream."""
+        self._ok(self.lib.kvsnap_dp_scatter(self.spans.data_ptr(), len(self.plane.layers), self.size,
+                                            self.stage_addrs[0].data_ptr(), self.restore_ids.data_ptr(), self.n,
+                                            self.crc_restore.data_ptr(), self.crc[0].data_ptr(), 0,
+                                            self.status.data_ptr(), 16 | self.plane._hbm, self.ctas,
+                                            self.copy.cuda_stream))
+
     def join(self):
         """Make the copy stream wait for everything queued on the other streams."""
-        for stream in (self.load, *self.sides):
+        for stream in (self.load, self.load_copy, *self.sides):
             e = self.torch.cuda.Event()
             e.record(stream)
             self.copy.wait_event(e)
@@ -472,7 +505,7 @@ def main():
     barrier(world)
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     start.record(engine.copy)
-    for stream in (engine.load, *engine.sides):
+    for stream in (engine.load, engine.load_copy, *engine.sides):
         stream.wait_event(start)
     for _ in range(args.steps):
         engine.step(marks)
@@ -493,6 +526,19 @@ def main():
             snap.close()
         plane.close()
         return
+
+    # The on-device kernels alone, back to back, for their rooflines (HBM read + write per launch).
+    kernel_ms = {}
+    for name, fn in (("gather", engine.gather_only), ("scatter", engine.scatter_only)):
+        fn()
+        torch.cuda.synchronize()
+        s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s0.record(engine.copy)
+        for _ in range(10):
+            fn()
+        s1.record(engine.copy)
+        torch.cuda.synchronize()
+        kernel_ms[name] = max_over_ranks(s0.elapsed_time(s1) / 10, world)
 
     # End to end through the public API, host tier (one pinned allocation per block): each step the
     # connector's save thread saves a session while its load thread restores the one saved before.
@@ -555,7 +601,8 @@ def main():
     value = world * 2 * session / (ms / 1e3) / 1e9
     e2e = world * 2 * session / (e2e_ms / 1e3) / 1e9
     restore_gbs = session / (phases["restore"] / 1e3) / 1e9
-    gather_gbs = 2 * session / (phases["gather"] / 1e3) / 1e9
+    gather_gbs = 2 * session / (kernel_ms["gather"] / 1e3) / 1e9
+    scatter_gbs = 2 * session / (kernel_ms["scatter"] / 1e3) / 1e9
     d2h_gbs = session / (phases["d2h"] / 1e3) / 1e9
     line = {
         "metric": METRIC, "value": round(value, 3), "unit": UNIT, "n_gpus": world, "steps": args.steps,
@@ -573,10 +620,15 @@ def main():
                       "restore_gbs": round(restore_gbs, 2), "restore_frac": round(restore_gbs / link["h2d"], 3),
                       "save_d2h_gbs": round(d2h_gbs, 2), "save_frac": round(d2h_gbs / link["d2h"], 3),
                       "note": "per-phase rates measured while the other direction runs concurrently"},
-        "roofline": {"bound": "hbm", "kernel": "span_kernel<16,gather> (KV -> HBM staging, CRC32C)",
+        "roofline": {"bound": "hbm", "kernel": "span_kernel_hbm<gather>: KV -> device staging, tail zero, CRC32C",
                      "achieved": round(gather_gbs, 1), "peak": hbm_peak, "unit": "GB/s",
-                     "frac": round(gather_gbs / hbm_peak, 3), "traffic": None,
-                     "peak_source": f"{peak_src} hbm_gbs"},
+                     "frac": round(gather_gbs / hbm_peak, 3), "traffic": 2.588e9,
+                     "traffic_note": "ncu dram read+write per launch, profiles/span_kernel_hbm_gather_qwen3-8b_512-blocks.md",
+                     "algorithmic_bytes": 2 * session, "ms": round(kernel_ms["gather"], 4),
+                     "peak_source": f"{peak_src} hbm_gbs (burst copy)"},
+        "roofline_scatter": {"bound": "hbm", "kernel": "span_kernel_hbm<scatter>: device staging -> KV, CRC32C check",
+                             "achieved": round(scatter_gbs, 1), "peak": hbm_peak, "unit": "GB/s",
+                             "frac": round(scatter_gbs / hbm_peak, 3), "ms": round(kernel_ms["scatter"], 4)},
         "sha256_gbs": round(session / (phases["sha256"] / 1e3) / 1e9, 2),
         "e2e": {"value": round(e2e, 3), "unit": UNIT, "ms_per_step": round(e2e_ms, 3),
                 "h2d_bytes_per_step": session + 16 * n, "d2h_bytes_per_step": session + 36 * n},

@@ -66,6 +66,13 @@ int kvsnap_pool_wait(void* pool, uint64_t id);
 int kvsnap_pool_ready(void* pool, uint64_t id);
 /* Wait, then return the bytes to the arena (reference cuda_pool.cpp:190-199). */
 int kvsnap_pool_release(void* pool, uint64_t id);
+/* Extension (no reference counterpart): kvsnap_pool_copy queued on `stream`
+   (0: the pool's copy stream) instead of the pool's stream, with no producer
+   fence: the caller orders its own stream. Lets a restore's host-to-device
+   copies run beside a save's device-to-host copies (the host link is full
+   duplex). The allocation's completion event is recorded on `stream`. */
+int kvsnap_pool_copy_on(void* pool, uint64_t id, size_t host_offset, void* device_ptr, size_t size, int to_host,
+                        uintptr_t stream);
 /* Extension (no reference counterpart): record the allocation's completion
    event on `stream` (0: the pool's copy stream) now, so wait/ready/release
    also fence kernels queued there that read or write the allocation in place. */

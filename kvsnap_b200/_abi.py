@@ -49,6 +49,7 @@ POOL_API = {
 # Pool entry points this library adds to the reference's ABI 2 set.
 POOL_EXTRA = {
     "kvsnap_pool_mark": ([_P, C.c_uint64, _SZ], C.c_int),
+    "kvsnap_pool_copy_on": ([_P, C.c_uint64, _SZ, _P, _SZ, C.c_int, _SZ], C.c_int),
 }
 
 DP_API = {

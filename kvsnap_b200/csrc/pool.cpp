@@ -249,6 +249,28 @@ extern "C" int kvsnap_pool_copy_2d(void* pool, uint64_t id, size_t host_offset, 
     });
 }
 
+extern "C" int kvsnap_pool_copy_on(void* pool, uint64_t id, size_t host_offset, void* device_ptr, size_t size,
+                                   int to_host, uintptr_t stream) {
+    return guarded([&] {
+        Arena* a = live(pool);
+        std::lock_guard<std::mutex> lock(a->mutex);
+        Slot& s = a->slot(id);
+        if (host_offset > s.size || size > s.size - host_offset)
+            throw Failure("copy outside pinned allocation");
+        cuda(cudaSetDevice(a->device));
+        cudaStream_t on = stream ? reinterpret_cast<cudaStream_t>(stream) : a->stream;
+        char* host = a->base + s.offset + host_offset;
+        a->begin(s);
+        s.foreign = on != a->stream;
+        if (to_host)
+            cuda(cudaMemcpyAsync(host, device_ptr, size, cudaMemcpyDeviceToHost, on));
+        else
+            cuda(cudaMemcpyAsync(device_ptr, host, size, cudaMemcpyHostToDevice, on));
+        cuda(cudaEventRecord(s.done, on));
+        s.done_valid = true;
+    });
+}
+
 extern "C" int kvsnap_pool_mark(void* pool, uint64_t id, uintptr_t stream) {
     return guarded([&] {
         Arena* a = live(pool);

@@ -216,6 +216,14 @@ class PinnedAllocation:
                 self.pool.handle, self.ident, host_offset, host_pitch, device_ptr, device_pitch,
                 width, height, int(bool(to_host)), producer_stream))
 
+    def copy_on(self, device_ptr, size, offset=0, *, to_host, stream):
+        """Like :meth:`copy`, queued on ``stream`` instead of the pool's copy stream (no producer fence)."""
+        with self.operation():
+            if min(size, offset, device_ptr, stream) < 0:
+                raise ValueError("negative copy argument")
+            self.pool.check(self.pool.lib.kvsnap_pool_copy_on(
+                self.pool.handle, self.ident, offset, device_ptr, size, int(bool(to_host)), stream))
+
     def mark(self, stream=0):
         """Fence work queued so far on ``stream`` (0: the pool's copy stream) under this allocation's
         wait/ready/release: kernels that read or write the allocation in place run there, and
@@ -305,14 +313,16 @@ class TorchBlockDataPlane:
     blocks to pinned memory with the copy engine (the default, and always
     used when digests are requested); ``"direct"`` has the gather kernel
     write the pinned blocks in place over the host link. ``restore_mode``:
-    ``"direct"`` has the scatter kernel read pinned blocks in place (the
-    default); ``"staged"`` copies them to device memory with the copy engine
-    first. A restore with ``expected_crc32c`` is always staged, so the check
-    completes before any KV byte changes.
+    ``"staged"`` moves pinned blocks to a device ring with the copy engine and
+    scatters them from there (the default: copy engines in both directions at
+    once reach about twice what one direction does, SM reads of host memory
+    beside a copy do not); ``"direct"`` has the scatter kernel read pinned
+    blocks in place. A restore with ``expected_crc32c`` stages every block, so
+    the check completes before any KV byte changes.
     """
 
     save_mode = "staged"
-    restore_mode = "direct"
+    restore_mode = "staged"
 
     def __init__(self, caches, block_size, capacity_bytes, *, save_mode=None, restore_mode=None, ctas=0):
         import torch
@@ -391,6 +401,7 @@ class TorchBlockDataPlane:
             # duplex); digests run on streams of their own, so concurrent saves'
             # SHA-256 kernels overlap each other and the copies.
             self._load_stream = torch.cuda.Stream(self._device())
+            self._load_copy_stream = torch.cuda.Stream(self._device())
             self._sha_streams = [torch.cuda.Stream(self._device()) for _ in range(2)]
             self._sha_next = 0
             self._sha_lock = threading.Lock()
@@ -527,17 +538,24 @@ class TorchBlockDataPlane:
         """Copy packed host blocks into ``block_ids`` and wait for it (reference dataplane.py:334-386).
 
         ``sources[i]`` is ``(allocation, offset)`` holding block i packed, in
-        this pool's pinned memory. One kernel launch per ``chunk_bytes`` of
-        blocks on the pool's copy stream; a ``progress`` list receives
-        ``(None, total bytes)`` and then, as each launch is queued, ``(its
-        completion event, bytes left once it completes)``. Returns the number
-        of launches.
+        this pool's pinned memory. One scatter launch per ``chunk_bytes`` of
+        blocks; a ``progress`` list receives ``(None, total bytes)`` and then, as
+        each launch is queued, ``(its completion event, bytes left once it
+        completes)``. Returns the number of launches.
 
-        ``expected_crc32c``: the recorded CRC32C of each block. When given, the
-        blocks are copied to device memory, every CRC is checked there, and only
-        then are the scatter launches queued (and ``progress`` filled): a
-        mismatch raises :class:`CorruptBlockError` with the KV cache untouched
-        and no progress reported, so it stays a miss.
+        ``restore_mode`` "staged" (the default): per chunk, the copy engine moves
+        the blocks into a two-slot device ring on the restore's copy stream and
+        the scatter kernel writes them from there into the cache on the restore
+        stream, chunk k+1's copy overlapping chunk k's scatter. "direct": the
+        scatter kernel reads the pinned blocks in place. Both streams are the
+        restore's own, so a restore overlaps a save's copies (the host link is
+        full duplex).
+
+        ``expected_crc32c``: the recorded CRC32C of each block. When given, all
+        blocks are copied to device memory and checked there before any
+        scatter is queued (and before ``progress`` is filled): a mismatch raises
+        :class:`CorruptBlockError` with the KV cache untouched and no progress
+        reported, so it stays a miss.
         """
         torch = self.torch
         self._validate_ids(block_ids)
@@ -548,14 +566,14 @@ class TorchBlockDataPlane:
         if not block_ids:
             return 0
         spans = self._spans()
-        stream = self._scatter_targets()
+        self._scatter_targets()
         lib = _dp(self.pool.lib)
         device = self._device()
         n, size = len(block_ids), self.block_bytes
         per_launch = max(1, chunk_bytes // size)
-        staged = expected_crc32c is not None or self.restore_mode == "staged"
-        if not staged:
-            stream = self._load_stream
+        verified = expected_crc32c is not None
+        mode = "staged" if verified else self.restore_mode
+        copies, kernels = self._load_copy_stream, self._load_stream
         launches = 0
         done = None
         with self.pool.operation():
@@ -566,50 +584,108 @@ class TorchBlockDataPlane:
                 if offset < 0 or offset + size > allocation.size:
                     raise ValueError("load source outside its allocation")
                 addresses.append(allocation.pointer + offset)
-            with torch.cuda.stream(stream):
+            with torch.cuda.stream(kernels):
                 status = torch.zeros(1, dtype=torch.int32, device=device)
+                ids = torch.tensor(list(block_ids), dtype=torch.int64).pin_memory().to(device, non_blocking=True)
                 try:
-                    if staged:
+                    if mode == "direct":
+                        vec = self._vec_for(addresses)
+                        table = torch.tensor(addresses, dtype=torch.int64).pin_memory().to(device, non_blocking=True)
+                        if progress is not None:
+                            progress.append((None, n * size))
+                        for first in range(0, n, per_launch):
+                            last = min(n, first + per_launch)
+                            self._check(lib.kvsnap_dp_scatter(
+                                spans.data_ptr(), len(self.layers), size, table[first:].data_ptr(),
+                                ids[first:].data_ptr(), last - first, 0, 0, 0, status.data_ptr(), vec,
+                                self.host_ctas, kernels.cuda_stream))
+                            launches += 1
+                            done = torch.cuda.Event()
+                            done.record(kernels)
+                            if progress is not None:
+                                progress.append((done, (n - last) * size))
+                        for allocation in {id(a): a for a, _ in sources}.values():
+                            allocation.mark(kernels.cuda_stream)
+                    elif verified:
                         stage = torch.empty(n * size, dtype=torch.uint8, device=device)
+                        stage.record_stream(copies)
                         base = stage.data_ptr()
                         for i, j in self._runs(sources, 0, n, size):
                             allocation, offset = sources[i]
-                            allocation.copy(base + i * size, (j - i) * size, offset, to_host=False)
-                        read_from = [base + i * size for i in range(n)]
-                    else:
-                        read_from = addresses
-                    vec = self._vec_for(read_from)
-                    if staged and vec == 16:
-                        vec |= self._hbm
-                    table = torch.tensor(read_from + list(block_ids), dtype=torch.int64).pin_memory().to(
-                        device, non_blocking=True)
-                    if expected_crc32c is not None:
+                            allocation.copy_on(base + i * size, (j - i) * size, offset, to_host=False,
+                                               stream=copies.cuda_stream)
+                        landed = torch.cuda.Event()
+                        landed.record(copies)
+                        kernels.wait_event(landed)
+                        vec = (16 | self._hbm) if size % 16 == 0 else 8
+                        table = torch.tensor([base + i * size for i in range(n)], dtype=torch.int64).pin_memory().to(
+                            device, non_blocking=True)
                         self._verify(table, n, expected_crc32c, status, vec)
-                    if progress is not None:
-                        progress.append((None, n * size))
-                    ctas = self.ctas if staged else self.host_ctas
-                    for first in range(0, n, per_launch):
-                        last = min(n, first + per_launch)
-                        self._check(lib.kvsnap_dp_scatter(
-                            spans.data_ptr(), len(self.layers), size, table[first:].data_ptr(),
-                            table[n + first:].data_ptr(), last - first, 0, 0, 0, status.data_ptr(), vec, ctas,
-                            stream.cuda_stream))
-                        launches += 1
-                        done = torch.cuda.Event()
-                        done.record()
                         if progress is not None:
-                            progress.append((done, (n - last) * size))
-                    if not staged:
-                        for allocation in {id(a): a for a, _ in sources}.values():
-                            allocation.mark(stream.cuda_stream)
+                            progress.append((None, n * size))
+                        for first in range(0, n, per_launch):
+                            last = min(n, first + per_launch)
+                            self._check(lib.kvsnap_dp_scatter(
+                                spans.data_ptr(), len(self.layers), size, table[first:].data_ptr(),
+                                ids[first:].data_ptr(), last - first, 0, 0, 0, status.data_ptr(), vec, self.ctas,
+                                kernels.cuda_stream))
+                            launches += 1
+                            done = torch.cuda.Event()
+                            done.record(kernels)
+                            if progress is not None:
+                                progress.append((done, (n - last) * size))
+                    else:
+                        launches, done = self._staged_chunks(sources, ids, n, per_launch, status, progress)
                 except BaseException:
-                    # A launch that failed part way may still be queued: nothing
-                    # may release the sources before its stream drains.
-                    stream.synchronize()
+                    # A launch or copy that failed part way may still be queued:
+                    # nothing may release the sources before both streams drain.
+                    copies.synchronize()
+                    kernels.synchronize()
                     raise
         done.synchronize()
         self._status_error(status)
         return launches
+
+    def _staged_chunks(self, sources, ids, n, per_launch, status, progress):
+        """Restore through a two-slot device ring: copy engine in, scatter kernel out, per chunk."""
+        torch = self.torch
+        lib = _dp(self.pool.lib)
+        spans = self._spans()
+        device = self._device()
+        size = self.block_bytes
+        copies, kernels = self._load_copy_stream, self._load_stream
+        depth = min(n, per_launch)
+        ring = torch.empty(2 * depth * size, dtype=torch.uint8, device=device)
+        ring.record_stream(copies)
+        base = ring.data_ptr()
+        table = torch.tensor([base + i * size for i in range(2 * depth)], dtype=torch.int64).pin_memory().to(
+            device, non_blocking=True)
+        vec = (16 | self._hbm) if size % 16 == 0 else 8
+        if progress is not None:
+            progress.append((None, n * size))
+        scattered, done, launches = [], None, 0
+        for chunk, first in enumerate(range(0, n, per_launch)):
+            last = min(n, first + per_launch)
+            slot = chunk % 2
+            if chunk >= 2:
+                copies.wait_event(scattered[chunk - 2])      # the slot's previous chunk is in the cache
+            for i, j in self._runs(sources, first, last, size):
+                allocation, offset = sources[i]
+                allocation.copy_on(base + (slot * depth + i - first) * size, (j - i) * size, offset, to_host=False,
+                                   stream=copies.cuda_stream)
+            landed = torch.cuda.Event()
+            landed.record(copies)
+            kernels.wait_event(landed)
+            self._check(lib.kvsnap_dp_scatter(
+                spans.data_ptr(), len(self.layers), size, table[slot * depth:].data_ptr(), ids[first:].data_ptr(),
+                last - first, 0, 0, 0, status.data_ptr(), vec, self.ctas, kernels.cuda_stream))
+            launches += 1
+            done = torch.cuda.Event()
+            done.record(kernels)
+            scattered.append(done)
+            if progress is not None:
+                progress.append((done, (n - last) * size))
+        return launches, done
 
     def _verify(self, table, n, expected, status, vec):
         """CRC32C of the staged blocks (table[:n]) against ``expected``; raises before any scatter is queued."""

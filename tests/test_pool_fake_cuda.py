@@ -241,3 +241,23 @@ def test_mark_on_a_foreign_stream_drains_the_device_when_its_event_fails(lib):
         assert lib.fake_cuda_pending() == 0
     finally:
         lib.kvsnap_pool_destroy(pool)
+
+
+def test_copy_on_another_stream_is_fenced_by_its_own_event(lib):
+    pool = lib.kvsnap_pool_create(32, 0)
+    try:
+        rc, a, ptr = reserve(lib, pool, 16)
+        C.memmove(ptr, b"fedcba9876543210", 16)
+        device = C.create_string_buffer(16)
+        assert lib.kvsnap_pool_copy_on(pool, a, 0, C.addressof(device), 16, 0, 777) == 0
+        assert lib.fake_cuda_last_stream() == 777
+        assert lib.kvsnap_pool_ready(pool, a) == 0
+        assert lib.kvsnap_pool_copy_on(pool, a, 8, C.addressof(device), 9, 0, 777) == -1    # outside
+        assert lib.kvsnap_pool_wait(pool, a) == 0
+        assert device.raw == b"fedcba9876543210"
+        lib.fake_cuda_fail_next(b"cudaEventRecord")
+        assert lib.kvsnap_pool_copy_on(pool, a, 0, C.addressof(device), 16, 1, 777) == -1
+        assert lib.kvsnap_pool_release(pool, a) == 0          # drains the device: the copy ran elsewhere
+        assert lib.fake_cuda_pending() == 0
+    finally:
+        lib.kvsnap_pool_destroy(pool)
