@@ -58,6 +58,9 @@ def parse():
     p.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     p.add_argument("--explore", type=str, default="", help="write a per-phase / CTA sweep breakdown to this path")
     p.add_argument("--seed", type=int, default=0)
+    p.add_argument("--workload", choices=["session", "disk"], default="session",
+                   help="session: BASELINE config 2 (the default line); disk: config 3, verified restores of "
+                        "8k and 32k-token snapshots from one pinned staging buffer with seeded corruption")
     p.add_argument("--quick", action="store_true",
                    help="only the device-timed steps (a short run for profiling captures)")
     return p.parse_args()
@@ -185,7 +188,7 @@ def pinned_copy_peaks(nbytes, device, repeats=5):
 class Engine:
     """The data plane's kernels launched straight through the C ABI with resident tables.
 
-    A stream of sessions through one GPU, two deep. Step k saves session k and
+    A stream of sessions through one GPU, three deep. Step k saves session k and
     restores session k-1 (the snapshot step k-1 saved) into other blocks, the way
     the connector's save and load threads overlap on a serving worker:
 
@@ -197,7 +200,7 @@ class Engine:
       every block's CRC32C against the one its save computed.
 
     The host link is full duplex, so the two copy directions overlap; staging,
-    snapshots and CRCs are double-buffered and every reuse waits on an event.
+    snapshots and CRCs rotate through three buffers and every reuse waits on an event.
     """
 
     def __init__(self, plane, save_ids, restore_ids, ctas, restore_mode):
@@ -219,8 +222,9 @@ class Engine:
         dev = plane._device()
         n, size = self.n, self.size
         i64 = dict(dtype=torch.int64, device=dev)
-        self.stage = [torch.empty(n * size, dtype=torch.uint8, device=dev) for _ in range(2)]
-        self.snapshot = [plane.pool.reserve(n * size) for _ in range(2)]
+        self.depth = 3
+        self.stage = [torch.empty(n * size, dtype=torch.uint8, device=dev) for _ in range(self.depth)]
+        self.snapshot = [plane.pool.reserve(n * size) for _ in range(self.depth)]
         self.stage_addrs = [torch.tensor([st.data_ptr() + i * size for i in range(n)], **i64) for st in self.stage]
         self.pinned_addrs = [torch.tensor([sn.pointer + i * size for i in range(n)], **i64) for sn in self.snapshot]
         if restore_mode == "staged":
@@ -228,9 +232,9 @@ class Engine:
             self.stage_in_addrs = torch.tensor([self.stage_in.data_ptr() + i * size for i in range(n)], **i64)
         self.save_ids = torch.tensor(save_ids, **i64)
         self.restore_ids = torch.tensor(restore_ids, **i64)
-        self.crc = [torch.empty(n, dtype=torch.int32, device=dev) for _ in range(2)]
+        self.crc = [torch.empty(n, dtype=torch.int32, device=dev) for _ in range(self.depth)]
         self.crc_restore = torch.empty(n, dtype=torch.int32, device=dev)
-        self.digest = [torch.empty(n * 32, dtype=torch.uint8, device=dev) for _ in range(2)]
+        self.digest = [torch.empty(n * 32, dtype=torch.uint8, device=dev) for _ in range(self.depth)]
         self.status = torch.zeros(1, dtype=torch.int32, device=dev)
         self.handle = plane.pool.handle
         self.k = 0
@@ -254,14 +258,14 @@ class Engine:
 
     def step(self, marks=None):
         torch, lib, n, size = self.torch, self.lib, self.n, self.size
-        k, b = self.k, self.k % 2
+        k, b, depth = self.k, self.k % self.depth, self.depth
         nspans = len(self.plane.layers)
         timing = marks is not None
         launches = 0
-        side = self.sides[b]
+        side = self.sides[k % len(self.sides)]
         # ---- save session k ----
-        self._wait(self.copy, "hashed", k - 2)          # staging[b] free
-        self._wait(self.copy, "restored", k - 1)        # snapshot[b] and crc[b] free
+        self._wait(self.copy, "hashed", k - depth)          # staging[b] free
+        self._wait(self.copy, "restored", k - depth + 1)    # snapshot[b] and crc[b] read by restore(k-depth+1)
         t0 = self._event("t0", k, self.copy, timing)
         self._ok(lib.kvsnap_dp_gather(self.spans.data_ptr(), nspans, size, self.save_ids.data_ptr(),
                                       self.stage_addrs[b].data_ptr(), n, 0, self.crc[b].data_ptr(),
@@ -280,7 +284,7 @@ class Engine:
         # ---- restore session k-1 (its snapshot and CRCs), concurrently ----
         r0 = None
         if ("saved", k - 1) in self.events:
-            p = 1 - b
+            p = (k - 1) % depth
             self._wait(self.load, "saved", k - 1)
             self._wait(self.load_copy, "saved", k - 1)
             self._wait(self.load_copy, "restored", k - 1)   # stage_in free
@@ -476,12 +480,15 @@ def main():
 
     device = torch.device("cuda", local)
     torch.cuda.set_device(device)
+    if args.workload == "disk":
+        run_disk(args, world, rank, device)
+        return
     n = (args.tokens + BLOCK - 1) // BLOCK
     t_setup = time.perf_counter()
     caches = make_caches(args, device)
     save_ids, restore_ids = session_blocks(args, n)
     size_guess = args.layers * 2 * BLOCK * HEADS * HEAD_DIM * 2
-    plane = TorchBlockDataPlane(caches, BLOCK, 5 * n * size_guess + (64 << 20), restore_mode=args.restore_mode,
+    plane = TorchBlockDataPlane(caches, BLOCK, 7 * n * size_guess + (64 << 20), restore_mode=args.restore_mode,
                                 ctas=args.ctas)
     plane.warm_up()
     size = plane.block_bytes
@@ -540,32 +547,41 @@ def main():
         torch.cuda.synchronize()
         kernel_ms[name] = max_over_ranks(s0.elapsed_time(s1) / 10, world)
 
-    # End to end through the public API, host tier (one pinned allocation per block): each step the
-    # connector's save thread saves a session while its load thread restores the one saved before.
-    sets = [[plane.pool.reserve(size) for _ in range(n)] for _ in range(2)]
+    # End to end through the public API, host tier (one pinned allocation per block), with the
+    # connector's threads: two save workers (vllm.py:202) and one load worker (vllm.py:203). Session k
+    # is saved into snapshot k % 3 (with its digests) and restored once its save has returned.
+    sets = [[plane.pool.reserve(size) for _ in range(n)] for _ in range(3)]
     places = [[(a, 0) for a in owned] for owned in sets]
-    pool = ThreadPoolExecutor(max_workers=2)
+    savers, loader = ThreadPoolExecutor(max_workers=2), ThreadPoolExecutor(max_workers=1)
 
-    def e2e_step(k):
-        saving = pool.submit(plane.save_gather, save_ids, places[k % 2], args.tokens, digests=[])
-        if k > 0:
-            restoring = pool.submit(plane.load_scatter, restore_ids, places[(k - 1) % 2])
-            restoring.result()
-        return saving.result()
+    def run_sessions(first, count):
+        saves, restores = {}, []
+        for k in range(first, first + count):
+            if k - 3 in saves:                       # snapshot k % 3 is free once its restore is done
+                saves.pop(k - 3).result()
+                while restores and restores[0][0] <= k - 3:
+                    restores.pop(0)[1].result()
+            saves[k] = savers.submit(plane.save_gather, save_ids, places[k % 3], args.tokens, digests=[])
+            if k - 1 >= first:
+                saves[k - 1].result()
+                restores.append((k - 1, loader.submit(plane.load_scatter, restore_ids, places[(k - 1) % 3])))
+        last = first + count - 1
+        saves[last].result()
+        restores.append((last, loader.submit(plane.load_scatter, restore_ids, places[last % 3])))
+        for _, f in restores:
+            f.result()
+        for f in saves.values():
+            f.result()
 
-    k = 0
-    for _ in range(max(1, args.warmup)):
-        e2e_step(k)
-        k += 1
+    run_sessions(0, max(2, args.warmup))
     torch.cuda.synchronize()
     barrier(world)
     t0 = time.perf_counter()
-    for _ in range(args.steps):
-        e2e_step(k)
-        k += 1
+    run_sessions(0, args.steps)
     torch.cuda.synchronize()
     e2e_ms = max_over_ranks((time.perf_counter() - t0) / args.steps * 1e3, world)
-    pool.shutdown()
+    savers.shutdown()
+    loader.shutdown()
     for owned in sets:
         for a in owned:
             a.close()
@@ -646,6 +662,78 @@ def main():
     if world > 1:
         import torch.distributed as dist
         dist.destroy_process_group()
+
+
+def run_disk(args, world, rank, device):
+    """the disk tier's restore from one pinned staging buffer, CRC32C checked on the GPU.
+
+    For 8192- and 32768-token Qwen3-8B snapshots: save the session into one
+    staging buffer (its CRCs recorded, as the store's manifest does), flip one
+    byte in a seeded 1-in-1000 of the blocks (at least one), and require the
+    verified restore to name exactly those blocks and leave the cache untouched.
+    Then time the verified restore of the repaired snapshot into fragmented
+    (seeded random) block tables.
+    """
+    import ctypes
+    import numpy as np
+    import torch
+    from kvsnap_b200.dataplane import CorruptBlockError, TorchBlockDataPlane
+    caches = make_caches(args, device)
+    rows = []
+    size_guess = args.layers * 2 * BLOCK * HEADS * HEAD_DIM * 2
+    plane = TorchBlockDataPlane(caches, BLOCK, 2048 * size_guess + (256 << 20), ctas=args.ctas)
+    plane.warm_up()
+    size = plane.block_bytes
+    rng = np.random.Generator(np.random.PCG64(args.seed + 33))
+    for tokens in (8192, 32768):
+        n = tokens // BLOCK
+        order = rng.permutation(args.pool_blocks - 1) + 1
+        saved, restored = [int(b) for b in order[:n]], [int(b) for b in order[n:2 * n]]
+        with plane.staging(n) as staged:
+            sources = [(staged, i * size) for i in range(n)]
+            digests = []
+            plane.save_gather(saved, sources, tokens, digests=digests)
+            crcs = [c for _, c in digests]
+            corrupt = sorted(set(int(i) for i in rng.choice(n, max(1, n // 1000), replace=False)))
+            flips = []
+            for i in corrupt:
+                at = staged.pointer + i * size + int(rng.integers(size))
+                flips.append(at)
+                ctypes.memset(at, ctypes.string_at(at, 1)[0] ^ 0x5A, 1)
+            before = []
+            check_ids = restored[:8]
+            with plane.staging(len(check_ids)) as probe:
+                plane.save_gather(check_ids, [(probe, i * size) for i in range(len(check_ids))],
+                                  len(check_ids) * BLOCK, digests=before)
+            detected = None
+            try:
+                plane.load_scatter(restored, sources, expected_crc32c=crcs)
+            except CorruptBlockError as exc:
+                detected = exc.blocks
+            after = []
+            with plane.staging(len(check_ids)) as probe:
+                plane.save_gather(check_ids, [(probe, i * size) for i in range(len(check_ids))],
+                                  len(check_ids) * BLOCK, digests=after)
+            for at in flips:
+                ctypes.memset(at, ctypes.string_at(at, 1)[0] ^ 0x5A, 1)
+            plane.load_scatter(restored, sources, expected_crc32c=crcs)       # warm
+            torch.cuda.synchronize()
+            times = []
+            for _ in range(max(3, args.steps // 2)):
+                t0 = time.perf_counter()
+                plane.load_scatter(restored, sources, expected_crc32c=crcs)
+                times.append((time.perf_counter() - t0) * 1e3)
+            ms = statistics.median(times)
+            restored_digests = []      # re-save the restored blocks over the snapshot and compare ids
+            plane.save_gather(restored, sources, tokens, digests=restored_digests)
+            rows.append({"tokens": tokens, "blocks": n, "bytes": n * size, "corrupted": corrupt,
+                         "detected": detected, "detected_exactly": detected == corrupt,
+                         "cache_untouched_on_failure": before == after,
+                         "restore_bit_exact": restored_digests == digests,
+                         "verified_restore_ms": round(ms, 3), "gbs": round(n * size / (ms / 1e3) / 1e9, 2)})
+    if rank == 0:
+        print(json.dumps({"workload": "disk-tier verified restore (BASELINE config 3)", "rows": rows}), flush=True)
+    plane.close()
 
 
 def explore_phases(plane, engine, save_ids, restore_ids, link):

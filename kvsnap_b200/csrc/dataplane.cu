@@ -374,6 +374,54 @@ __device__ __forceinline__ uint32_t warp_unit_wide(const uint32_t* tl, const uin
     return r;
 }
 
+// The common path (no tail masking), software-pipelined: the next step's four
+// 16-byte loads are in flight while this step's vectors are stored and CRC'd,
+// so each lane keeps 128 bytes of reads outstanding across the lookup chain.
+template <bool STORE, bool CRC>
+__device__ __forceinline__ uint32_t warp_unit_wide_piped(const uint32_t* tl, const uint32_t* far,
+                                                         const char* __restrict__ src, char* __restrict__ dst,
+                                                         int64_t len, int lane) {
+    const int64_t steps = (len + kWideStep - 1) / kWideStep;
+    const int64_t first = (int64_t)lane * 64 - (steps * kWideStep - len);
+    uint32_t r = 0;
+    uint4 cur[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        const int64_t at = first + 16 * k;
+        cur[k] = at >= 0 ? *reinterpret_cast<const uint4*>(src + at) : make_uint4(0, 0, 0, 0);
+    }
+    for (int64_t t = 0; t < steps; ++t) {
+        uint4 nxt[4];
+        const int64_t base = first + (t + 1) * kWideStep;   // >= 0 from the second step on
+        if (t + 1 < steps) {
+#pragma unroll
+            for (int k = 0; k < 4; ++k) nxt[k] = *reinterpret_cast<const uint4*>(src + base + 16 * k);
+        }
+        if (STORE) {
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                const int64_t at = first + t * kWideStep + 16 * k;
+                if (at >= 0) *reinterpret_cast<uint4*>(dst + at) = cur[k];
+            }
+        }
+        if (CRC) {
+            r = crc_jump(far, r);
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                r = crc_word(tl, r, cur[k].x);
+                r = crc_word(tl, r, cur[k].y);
+                r = crc_word(tl, r, cur[k].z);
+                r = crc_word(tl, r, cur[k].w);
+            }
+        }
+        if (t + 1 < steps) {
+#pragma unroll
+            for (int k = 0; k < 4; ++k) cur[k] = nxt[k];
+        }
+    }
+    return r;
+}
+
 // The last block of a save, whose tail token slots are written as zeros: kept
 // out of line so the common path's registers stay free of the masking code.
 __device__ __noinline__ uint32_t wide_tail_unit(const uint32_t* tl, const uint32_t* far, const char* src, char* dst,
@@ -381,8 +429,13 @@ __device__ __noinline__ uint32_t wide_tail_unit(const uint32_t* tl, const uint32
     return warp_unit_wide<true, true, true>(tl, far, src, dst, sp.bytes, lane, sp, valid);
 }
 
+// Threads a CTA of the HBM kernels (one CTA an SM). The gather's out-of-line
+// tail call spills at this size; its common path does not.
 template <int MODE>
-__global__ void __launch_bounds__(1024, 1) span_kernel_hbm(SpanArgs a) {
+constexpr int kHbmThreads = 1024;
+
+template <int MODE>
+__global__ void __launch_bounds__(kHbmThreads<MODE>, 1) span_kernel_hbm(SpanArgs a) {
     extern __shared__ uint32_t tb[];
     const bool crc = a.crc != nullptr;
     if (crc) load_wide_tables(tb);
@@ -413,13 +466,13 @@ __global__ void __launch_bounds__(1024, 1) span_kernel_hbm(SpanArgs a) {
         const bool tail = MODE == kGather && a.valid > 0 && i == a.n - 1;
         if (crc) {
             uint32_t r = tail ? wide_tail_unit(tl, far, src, dst, sp, lane, a.valid)
-                              : warp_unit_wide<true, true, false>(tl, far, src, dst, sp.bytes, lane, sp, 0);
+                              : warp_unit_wide_piped<true, true>(tl, far, src, dst, sp.bytes, lane);
             r = gf_mulmod(warp_xor(gf_mulmod(r, lane_shift)), sp.crc_shift);
             if (lane == 0) atomicXor(&a.crc[i], r);
         } else if (tail) {
             wide_tail_unit(tl, far, src, dst, sp, lane, a.valid);
         } else {
-            warp_unit_wide<true, false, false>(tl, far, src, dst, sp.bytes, lane, sp, 0);
+            warp_unit_wide_piped<true, false>(tl, far, src, dst, sp.bytes, lane);
         }
     }
 }
@@ -445,8 +498,8 @@ __global__ void __launch_bounds__(1024, 1) crc_kernel_hbm(const int64_t* addrs, 
             if (lane == 0) flag(status, KVSNAP_DP_MISALIGNED);
             continue;
         }
-        uint32_t r = warp_unit_wide<false, true, false>(tl, far, reinterpret_cast<const char*>(base), nullptr, len,
-                                                        lane, none, 0);
+        uint32_t r = warp_unit_wide_piped<false, true>(tl, far, reinterpret_cast<const char*>(base), nullptr, len,
+                                                       lane);
         r = gf_mulmod(warp_xor(gf_mulmod(r, lane_shift)), dev_xpow8n(uint64_t(block_bytes - at - len)));
         if (lane == 0) atomicXor(&crc[i], r);
     }
@@ -873,9 +926,9 @@ int launch_spans(const kvsnap_span* spans, int nspans, uint64_t block_bytes, con
                                            kWideSmemBytes));
                 configured = true;
             }
-            const int64_t want = (n * nspans + 31) / 32;
+            const int64_t want = (n * nspans + kHbmThreads<MODE> / 32 - 1) / (kHbmThreads<MODE> / 32);
             const int grid = ctas > 0 ? ctas : int(want < sms ? want : sms);
-            span_kernel_hbm<MODE><<<grid, 1024, crc ? kWideSmemBytes : 0, s>>>(a);
+            span_kernel_hbm<MODE><<<grid, kHbmThreads<MODE>, crc ? kWideSmemBytes : 0, s>>>(a);
             check(cudaGetLastError());
             if (crc) finish(crc, expect, n, block_bytes, status, s);
             return;
