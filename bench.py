@@ -58,7 +58,7 @@ def parse():
     p.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     p.add_argument("--explore", type=str, default="", help="write a per-phase / CTA sweep breakdown to this path")
     p.add_argument("--seed", type=int, default=0)
-    p.add_argument("--workload", choices=["session", "disk"], default="session",
+    p.add_argument("--workload", choices=["session", "disk", "reshard", "rotation"], default="session",
                    help="session: BASELINE config 2 (the default line); disk: config 3, verified restores of "
                         "8k and 32k-token snapshots from one pinned staging buffer with seeded corruption")
     p.add_argument("--quick", action="store_true",
@@ -483,6 +483,12 @@ def main():
     if args.workload == "disk":
         run_disk(args, world, rank, device)
         return
+    if args.workload == "reshard":
+        run_reshard(args, world, rank, device)
+        return
+    if args.workload == "rotation":
+        run_rotation(args, world, rank, device)
+        return
     n = (args.tokens + BLOCK - 1) // BLOCK
     t_setup = time.perf_counter()
     caches = make_caches(args, device)
@@ -733,6 +739,226 @@ def run_disk(args, world, rank, device):
                          "verified_restore_ms": round(ms, 3), "gbs": round(n * size / (ms / 1e3) / 1e9, 2)})
     if rank == 0:
         print(json.dumps({"workload": "disk-tier verified restore (BASELINE config 3)", "rows": rows}), flush=True)
+    plane.close()
+
+
+def run_reshard(args, world, rank, device):
+    """BASELINE config 5's regroup: a TP-(2T) Qwen3-32B snapshot restored at TP-T over NVLink.
+
+    World size W (torchrun, one GPU a rank): the snapshot was saved at TP=W (one
+    shard a rank, 64 layers × 8/W heads, 2048 blocks = 32768 tokens), the cache
+    it is restored into runs at TP=W/2 on ranks 0..W/2-1. Every rank copies its
+    own shard from pinned memory into device memory it shares over CUDA IPC;
+    each destination rank's regroup kernel reads its two shards (one its own,
+    one a peer's over NVLink) and interleaves them into its cache blocks.
+    Checked: sample blocks of every destination rank re-save to the interleave
+    of the two shards' bytes (gathered from their ranks with NCCL).
+    """
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+    from kvsnap_b200.dataplane import TorchBlockDataPlane
+    from kvsnap_b200.reshard import RegroupPlan, regroup_restore
+    if world < 2 or world % 2:
+        raise SystemExit("the regroup workload needs an even number of ranks (torchrun --nproc-per-node 2|4|8)")
+    plan = RegroupPlan(world, world // 2)
+    layers, heads, n, pool = 64, 8, 2048, 4096
+    dst_heads = heads // plan.dst_tp
+    caches = {f"model.layers.{i}": torch.zeros((2, pool, BLOCK, dst_heads, HEAD_DIM), dtype=torch.bfloat16,
+                                               device=device) for i in range(layers)}
+    size = layers * 2 * BLOCK * dst_heads * HEAD_DIM * 2
+    shard = size // plan.groups
+    plane = TorchBlockDataPlane(caches, BLOCK, n * shard + size * 8 + (256 << 20), ctas=args.ctas)
+    plane.warm_up()
+    gen = torch.Generator(device=device).manual_seed(args.seed * 97 + rank)
+    noise = torch.randint(0, 256, (n * shard,), dtype=torch.uint8, device=device, generator=gen)
+    snapshot = plane.pool.reserve(n * shard)
+    snapshot.copy(noise.data_ptr(), n * shard, 0, to_host=True)
+    snapshot.wait()
+    sources = [(snapshot, i * shard) for i in range(n)]
+    order = np.random.Generator(np.random.PCG64(args.seed + 5)).permutation(pool - 1) + 1
+    restored = [int(b) for b in order[:n]]
+    regroup_restore(plane, plan, rank, restored, sources)                 # warm: maps, loads kernels
+    runs = []
+    for _ in range(max(3, args.steps // 2)):
+        torch.cuda.synchronize()
+        dist.barrier()
+        timings = {}
+        t0 = time.perf_counter()
+        regroup_restore(plane, plan, rank, restored, sources, timings=timings)
+        timings["total_s"] = time.perf_counter() - t0
+        runs.append(timings)
+    # Parity on sample blocks: destination rank r's packed block i = interleave of shards 2r, 2r+1.
+    samples = [0, n // 2, n - 1]
+    mine = torch.stack([noise[i * shard:(i + 1) * shard] for i in samples])
+    gathered = [torch.empty_like(mine) for _ in range(world)]
+    dist.all_gather(gathered, mine)
+    ok = True
+    if rank < plan.dst_tp:
+        with plane.staging(len(samples)) as probe:
+            plane.save_gather([restored[i] for i in samples], [(probe, j * size) for j in range(len(samples))],
+                              len(samples) * BLOCK)
+            for j in range(len(samples)):
+                got = np.frombuffer(probe.read_range(j * size, size), dtype=np.uint8)
+                parts = [gathered[src][j].cpu().numpy() for src in plan.sources(rank)]
+                span = BLOCK * HEAD_DIM * 2                      # one head's bytes in a K or V span
+                want = []
+                for s_idx in range(2 * layers):                  # spans in layer-name order: k, v per layer
+                    rows = [p[s_idx * span * (dst_heads // plan.groups):(s_idx + 1) * span * (dst_heads // plan.groups)]
+                            .reshape(BLOCK, dst_heads // plan.groups, HEAD_DIM * 2) for p in parts]
+                    want.append(np.concatenate(rows, axis=1).reshape(-1))
+                ok &= bool(np.array_equal(got, np.concatenate(want)))
+    flags = torch.tensor([1.0 if ok else 0.0], device=device)
+    dist.all_reduce(flags, op=dist.ReduceOp.MIN)
+    med = {key: statistics.median(r[key] for r in runs if key in r) for key in runs[-1]}
+    worst = torch.tensor([med["total_s"], med.get("kernel_ms", 0.0), med["stage_s"]], dtype=torch.float64,
+                         device=device)
+    dist.all_reduce(worst, op=dist.ReduceOp.MAX)
+    if rank == 0:
+        moved = plan.dst_tp * n * size
+        print(json.dumps({
+            "workload": f"TP-{plan.src_tp} -> TP-{plan.dst_tp} regroup restore, qwen3-32b shape, 32768 tokens",
+            "n_gpus": world, "blocks": n, "shard_bytes_per_rank": n * shard, "dest_bytes_per_rank": n * size,
+            "total_ms": round(worst[0].item() * 1e3, 3), "regroup_kernel_ms": round(worst[1].item(), 3),
+            "stage_ms": round(worst[2].item() * 1e3, 3),
+            "regroup_kernel_gbs_per_dest_rank": round(n * size / (worst[1].item() / 1e3) / 1e9, 1),
+            "box_restored_gbs": round(moved / worst[0].item() / 1e9, 2),
+            "bit_exact_samples": bool(flags.item() == 1.0)}), flush=True)
+    snapshot.close()
+    plane.close()
+    dist.destroy_process_group()
+
+
+def run_rotation(args, world, rank, device):
+    """64 Qwen3-1.7B sessions saved and restored beside synthetic decode traffic.
+
+    Session lengths are log-uniform in [512, 8192] tokens (seeded); blocks come
+    from a shuffled free list (fragmented tables). Sessions 32..63 fork sessions
+    0..31: their first 75% of blocks are copies of the parent's, so those blocks
+    pack to the same bytes and the same content ids. All 64 are saved through the
+    API (two save threads, digests on the GPU) and then restored into fresh blocks
+    (one load thread), while a side stream keeps copying a 4 GiB buffer (HBM
+    traffic standing in for decode). Reported: save/restore GB/s with and without
+    the traffic, the traffic's GB/s with and without the data plane, and the dedup
+    rate from the GPU digests beside the one from hashlib over the saved bytes.
+    """
+    import hashlib
+    import threading
+    import numpy as np
+    import torch
+    from kvsnap_b200.dataplane import TorchBlockDataPlane
+    layers, pool_blocks = 28, 32768
+    rng = np.random.Generator(np.random.PCG64(args.seed + 44))
+    lengths = np.exp(rng.uniform(np.log(512), np.log(8192), 64)).astype(int)
+    for child in range(32, 64):                        # a fork is at least as long as 75% of its parent
+        lengths[child] = max(lengths[child], int(lengths[child - 32]))
+    free = [int(b) for b in rng.permutation(pool_blocks - 1) + 1]
+    sessions = []
+    for tokens in lengths:
+        n = (int(tokens) + BLOCK - 1) // BLOCK
+        sessions.append((int(tokens), [free.pop() for _ in range(n)]))
+    caches = {}
+    gen = torch.Generator(device=device)
+    for i in range(layers):
+        gen.manual_seed(args.seed * 1000 + 500 + i)
+        t = torch.empty((2, pool_blocks, BLOCK, HEADS, HEAD_DIM), dtype=torch.bfloat16, device=device)
+        t.normal_(generator=gen)
+        caches[f"model.layers.{i}.self_attn.attn"] = t
+    for child in range(32, 64):                        # forks copy 75% of the parent's full blocks
+        parent_blocks = sessions[child - 32][1]
+        shared = (len(parent_blocks) - 1) * 3 // 4
+        src = torch.tensor(parent_blocks[:shared], device=device)
+        dst = torch.tensor(sessions[child][1][:shared], device=device)
+        for t in caches.values():
+            t[:, dst] = t[:, src]
+    total_blocks = sum(len(b) for _, b in sessions)
+    size_guess = layers * 2 * BLOCK * HEADS * HEAD_DIM * 2
+    plane = TorchBlockDataPlane(caches, BLOCK, total_blocks * size_guess + (512 << 20), ctas=args.ctas)
+    plane.warm_up()
+    size = plane.block_bytes
+    snapshots = [[plane.pool.reserve(size) for _ in blocks] for _, blocks in sessions]
+    restore_tables = [[free.pop() for _ in blocks] for _, blocks in sessions]
+
+    decode_src = torch.empty(4 << 30, dtype=torch.uint8, device=device)
+    decode_dst = torch.empty_like(decode_src)
+    decode_stream = torch.cuda.Stream(device)
+    stop = threading.Event()
+    decoded = [0]
+
+    def decode_loop():
+        with torch.cuda.stream(decode_stream):
+            while not stop.is_set():
+                decode_dst.copy_(decode_src, non_blocking=True)
+                decoded[0] += 1
+                decode_stream.synchronize()
+
+    def decode_rate(seconds):
+        decoded[0] = 0
+        stop.clear()
+        thread = threading.Thread(target=decode_loop)
+        t0 = time.perf_counter()
+        thread.start()
+        time.sleep(seconds)
+        stop.set()
+        thread.join()
+        return 2 * decoded[0] * decode_src.numel() / (time.perf_counter() - t0) / 1e9
+
+    def rotate(with_decode):
+        digests = [None] * len(sessions)
+        savers, loader = ThreadPoolExecutor(max_workers=2), ThreadPoolExecutor(max_workers=1)
+        thread = None
+        if with_decode:
+            decoded[0] = 0
+            stop.clear()
+            thread = threading.Thread(target=decode_loop)
+            thread.start()
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+
+        def save(i):
+            out = []
+            tokens, blocks = sessions[i]
+            plane.save_gather(blocks, [(a, 0) for a in snapshots[i]], tokens, digests=out)
+            digests[i] = out
+
+        list(savers.map(save, range(len(sessions))))
+        t_saved = time.perf_counter()
+        list(loader.map(lambda i: plane.load_scatter(restore_tables[i], [(a, 0) for a in snapshots[i]]),
+                        range(len(sessions))))
+        t1 = time.perf_counter()
+        decode_gbs = None
+        if thread is not None:
+            stop.set()
+            thread.join()
+            decode_gbs = 2 * decoded[0] * decode_src.numel() / (time.perf_counter() - t0) / 1e9
+        savers.shutdown()
+        loader.shutdown()
+        return digests, t_saved - t0, t1 - t_saved, decode_gbs
+
+    rotate(False)                                        # warm
+    digests, save_s, restore_s, _ = rotate(False)
+    _, save_s_busy, restore_s_busy, decode_busy = rotate(True)
+    decode_alone = decode_rate(2.0)
+    ids = [d[0] for ds in digests for d in ds]
+    gpu_dedup = 1 - len(set(ids)) / len(ids)
+    with ThreadPoolExecutor(max_workers=os.cpu_count() or 1) as hashers:
+        host_ids = list(hashers.map(lambda a: hashlib.sha256(a.read()).hexdigest(),
+                                    [a for owned in snapshots for a in owned]))
+    host_dedup = 1 - len(set(host_ids)) / len(host_ids)
+    moved = total_blocks * size
+    if rank == 0:
+        print(json.dumps({
+            "workload": "64-session rotation, qwen3-1.7b shape (BASELINE config 4)",
+            "sessions": len(sessions), "blocks": total_blocks, "bytes_each_way": moved,
+            "save_gbs": round(moved / save_s / 1e9, 2), "restore_gbs": round(moved / restore_s / 1e9, 2),
+            "save_gbs_beside_decode": round(moved / save_s_busy / 1e9, 2),
+            "restore_gbs_beside_decode": round(moved / restore_s_busy / 1e9, 2),
+            "decode_gbs_alone": round(decode_alone, 1), "decode_gbs_beside_data_plane": round(decode_busy, 1),
+            "dedup_rate_gpu": round(gpu_dedup, 6), "dedup_rate_hashlib": round(host_dedup, 6),
+            "dedup_match": gpu_dedup == host_dedup and ids == host_ids}), flush=True)
+    for owned in snapshots:
+        for a in owned:
+            a.close()
     plane.close()
 
 

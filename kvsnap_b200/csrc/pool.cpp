@@ -52,6 +52,7 @@ struct Arena {
     int device = 0;
     cudaStream_t stream = nullptr;
     std::map<uint64_t, Slot> slots;
+    std::map<size_t, size_t> used;   // live ranges, offset -> size, in address order
     uint64_t next_id = 1;
     bool drained = false;
     std::mutex mutex;
@@ -180,10 +181,8 @@ extern "C" int kvsnap_pool_reserve(void* pool, size_t size, uint64_t* id, void**
         std::lock_guard<std::mutex> lock(a->mutex);
         if (size == 0 || size > a->capacity) throw Failure("pinned capacity exhausted");
         // First fit over the live ranges in address order (ids are not ordered by address).
-        std::map<size_t, size_t> used;
-        for (const auto& kv : a->slots) used.emplace(kv.second.offset, kv.second.size);
         size_t at = 0;
-        for (const auto& range : used) {
+        for (const auto& range : a->used) {
             if (range.first >= at && range.first - at >= size) break;
             size_t end = range.first + range.second;
             at = (end + kAlign - 1) / kAlign * kAlign;
@@ -197,6 +196,7 @@ extern "C" int kvsnap_pool_reserve(void* pool, size_t size, uint64_t* id, void**
         *id = a->next_id++;
         *ptr = a->base + at;
         a->slots.emplace(*id, s);
+        a->used.emplace(at, size);
     });
 }
 
@@ -323,6 +323,7 @@ extern "C" int kvsnap_pool_release(void* pool, uint64_t id) {
         cuda(cudaSetDevice(a->device));
         a->settle(s);   // blocking: the bytes are idle before they go back to the arena
         cuda(cudaEventDestroy(s.done));
+        a->used.erase(s.offset);
         a->slots.erase(id);
     });
 }

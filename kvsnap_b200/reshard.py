@@ -117,7 +117,7 @@ def close_peer(lib, ptr: int) -> None:
 
 
 def regroup_restore(plane, plan: RegroupPlan, rank: int, block_ids, shard_sources, *, group=None,
-                    expected_crc32c=None, is_destination=None):
+                    expected_crc32c=None, is_destination=None, timings=None):
     """Collective TP regroup restore; every rank of ``group`` calls it.
 
     ``plane``: this rank's TorchBlockDataPlane, registered at the destination TP
@@ -128,8 +128,11 @@ def regroup_restore(plane, plan: RegroupPlan, rank: int, block_ids, shard_source
     not a destination). ``expected_crc32c``: this rank's shard CRCs, checked on
     the GPU before anyone reads the shard. Source rank s of the plan runs on
     torch.distributed rank s; destination rank r on rank r. Returns the number
-    of regroup launches on this rank.
+    of regroup launches on this rank. ``timings``: a dict that receives the
+    host-side seconds of the stage, exchange and regroup phases and the regroup
+    kernel's device milliseconds.
     """
+    import time
     import torch
     import torch.distributed as dist
     from .dataplane import CorruptBlockError, _dp
@@ -149,6 +152,7 @@ def regroup_restore(plane, plan: RegroupPlan, rank: int, block_ids, shard_source
     #    A failure here is carried into the exchange, so every rank still takes
     #    the same collective steps and all of them raise it afterwards.
     buffer, failure = None, None
+    t0 = time.perf_counter()
     try:
         if is_source and n:
             buffer = _stage_shard(lib, plane, stream, rank, n, shard_bytes, shard_sources, expected_crc32c)
@@ -158,8 +162,10 @@ def regroup_restore(plane, plan: RegroupPlan, rank: int, block_ids, shard_source
         failure = f"rank {rank}: {type(exc).__name__}: {exc}"
 
     # 2. Exchange handles and verdicts; every rank takes the same collective steps.
+    t1 = time.perf_counter()
     mine = (buffer.handle() if buffer is not None else None, failure)
     failures, everyone = exchange(mine, group)
+    t2 = time.perf_counter()
     launches = 0
     peers = []
     try:
@@ -177,17 +183,24 @@ def regroup_restore(plane, plan: RegroupPlan, rank: int, block_ids, shard_source
             with torch.cuda.stream(stream):
                 table = torch.tensor(rows + list(block_ids), dtype=torch.int64, device=device)
                 status = torch.zeros(1, dtype=torch.int32, device=device)
+                begin, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                begin.record(stream)
                 if lib.kvsnap_dp_regroup(plane._span_table.data_ptr(), src_table.data_ptr(), len(plane.layers),
                                          table.data_ptr(), plan.groups, table[len(rows):].data_ptr(), n,
                                          status.data_ptr(), 0, stream.cuda_stream) < 0:
                     raise RuntimeError(lib.kvsnap_cuda_error().decode())
+                end.record(stream)
                 launches = 1
             stream.synchronize()
+            if timings is not None:
+                timings["kernel_ms"] = begin.elapsed_time(end)
             if int(status.item()):
                 raise RuntimeError(f"regroup kernel reported status {int(status.item())}")
     finally:
         # 3. Nobody frees a shard another rank may still be reading.
         dist.barrier(group=group)
+        if timings is not None:
+            timings.update(stage_s=t1 - t0, exchange_s=t2 - t1, regroup_s=time.perf_counter() - t2)
         for ptr in peers:
             close_peer(lib, ptr)
         if buffer is not None:
