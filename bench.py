@@ -53,6 +53,10 @@ def parse():
     p.add_argument("--tokens", type=int, default=8192)
     p.add_argument("--pool-blocks", type=int, default=32768)
     p.add_argument("--layers", type=int, default=LAYERS)
+    p.add_argument("--heads", type=int, default=HEADS, help="KV heads a rank holds")
+    p.add_argument("--model", choices=["qwen3-8b", "qwen3-32b-tp"], default="qwen3-8b",
+                   help="qwen3-32b-tp: BASELINE config 5, each of N ranks saves and restores its 8/N-head shard "
+                        "of a 32768-token Qwen3-32B session (64 layers)")
     p.add_argument("--ctas", type=int, default=0, help="CTAs for the data-plane kernels (0: library default)")
     p.add_argument("--restore-mode", choices=["direct", "staged"], default="staged")
     p.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
@@ -151,7 +155,7 @@ def make_caches(args, device):
     caches = {}
     for i in range(args.layers):
         gen.manual_seed(args.seed * 1000 + i)
-        t = torch.empty((2, args.pool_blocks, BLOCK, HEADS, HEAD_DIM), dtype=torch.bfloat16, device=device)
+        t = torch.empty((2, args.pool_blocks, BLOCK, args.heads, HEAD_DIM), dtype=torch.bfloat16, device=device)
         t.normal_(generator=gen)
         caches[f"model.layers.{i}.self_attn.attn"] = t
     return caches
@@ -480,6 +484,11 @@ def main():
 
     device = torch.device("cuda", local)
     torch.cuda.set_device(device)
+    if args.model == "qwen3-32b-tp":
+        if 8 % world:
+            raise SystemExit("qwen3-32b-tp needs 1, 2, 4 or 8 ranks")
+        args.layers, args.heads, args.tokens = 64, 8 // world, 32768
+        args.pool_blocks = max(args.pool_blocks if args.pool_blocks != 32768 else 0, 2 * 2048 + 64)
     if args.workload == "disk":
         run_disk(args, world, rank, device)
         return
@@ -493,7 +502,7 @@ def main():
     t_setup = time.perf_counter()
     caches = make_caches(args, device)
     save_ids, restore_ids = session_blocks(args, n)
-    size_guess = args.layers * 2 * BLOCK * HEADS * HEAD_DIM * 2
+    size_guess = args.layers * 2 * BLOCK * args.heads * HEAD_DIM * 2
     plane = TorchBlockDataPlane(caches, BLOCK, 7 * n * size_guess + (64 << 20), restore_mode=args.restore_mode,
                                 ctas=args.ctas)
     plane.warm_up()
@@ -630,8 +639,9 @@ def main():
         "metric": METRIC, "value": round(value, 3), "unit": UNIT, "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(ms, 3), "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "u8", "data": "synthetic",
-        "config": {"workload": "qwen3-8b 8k-token session save+restore (BASELINE config 2)",
-                   "layers": args.layers, "kv_heads": HEADS, "head_dim": HEAD_DIM, "block_size": BLOCK,
+        "config": {"workload": ("qwen3-8b 8k-token session save+restore (BASELINE config 2)" if args.model == "qwen3-8b"
+                                else f"qwen3-32b 32k-token session, TP-{world} shard a rank (BASELINE config 5)"),
+                   "layers": args.layers, "kv_heads": args.heads, "head_dim": HEAD_DIM, "block_size": BLOCK,
                    "pool_blocks": args.pool_blocks, "session_blocks": n, "session_bytes": session,
                    "restore_mode": args.restore_mode, "l2": "inputs (1.2 GB a step) larger than L2; no flush",
                    "kv": "bf16 N(0,1), seeded"},

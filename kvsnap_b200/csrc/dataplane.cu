@@ -60,10 +60,9 @@ __host__ __device__ constexpr uint32_t gf_xpow8n(uint64_t n) {
 
 // Tables: slots 0..15 hold T_0..T_15, slots 16..19 T_492..T_495 (moving a lane's
 // register 496 bytes ahead), slots 20..23 T_244..T_247 (the same for 8-byte
-// vectors), slots 24..27 T_1980..T_1983 (1984 bytes ahead, for the HBM kernels),
-// slots 28..31 T_28..T_31 (32 bytes ahead, joining the HBM kernels' two chains).
+// vectors), slots 24..27 T_1980..T_1983 (1984 bytes ahead, for the HBM kernels).
 struct CrcTables {
-    uint32_t t[32][256];
+    uint32_t t[28][256];
 };
 
 constexpr CrcTables make_tables() {
@@ -75,10 +74,6 @@ constexpr CrcTables make_tables() {
     }
     for (int k = 1; k < 16; ++k)
         for (int v = 0; v < 256; ++v) r.t[k][v] = (r.t[k - 1][v] >> 8) ^ r.t[0][r.t[k - 1][v] & 0xFFu];
-    for (int j = 0; j < 4; ++j) {
-        const uint32_t near32 = gf_xpow8n(28 + j);
-        for (int v = 0; v < 256; ++v) r.t[28 + j][v] = gf_mulmod(r.t[0][v], near32);
-    }
     for (int j = 0; j < 4; ++j) {
         const uint32_t far16 = gf_xpow8n(492 + j), far8 = gf_xpow8n(244 + j), far64 = gf_xpow8n(1980 + j);
         for (int v = 0; v < 256; ++v) {
@@ -319,18 +314,14 @@ __global__ void __launch_bounds__(256) span_kernel(SpanArgs a) {
 // lane l lies in bank l, so those lookups never conflict; only the four jump
 // lookups per 64 bytes use shared, conflicting tables. One 1024-thread CTA per SM.
 constexpr int kRepWords = 4 * 256 * 32;                 // replicated T_0..T_3
-constexpr int kWideSmemBytes = (kRepWords + 8 * 256) * 4;
+constexpr int kWideSmemBytes = (kRepWords + 4 * 256) * 4;
 constexpr int kWideStep = 2048;
 
-// Replicated T_0..T_3, then T_1980..T_1983 (the step jump), then T_28..T_31
-// (the 32-byte join of a lane's two chains).
+// Replicated T_0..T_3, then T_1980..T_1983 (the step jump).
 __device__ __forceinline__ void load_wide_tables(uint32_t* tb) {
     const uint32_t* g = &g_tables.t[0][0];
     for (int i = threadIdx.x; i < kRepWords; i += blockDim.x) tb[i] = g[i >> 5];
-    for (int i = threadIdx.x; i < 4 * 256; i += blockDim.x) {
-        tb[kRepWords + i] = g[24 * 256 + i];
-        tb[kRepWords + 4 * 256 + i] = g[28 * 256 + i];
-    }
+    for (int i = threadIdx.x; i < 4 * 256; i += blockDim.x) tb[kRepWords + i] = g[24 * 256 + i];
 }
 
 // r <- raw(r, 4 bytes of w), little-endian byte order; tl = replicated tables + lane.
@@ -415,22 +406,14 @@ __device__ __forceinline__ uint32_t warp_unit_wide_piped(const uint32_t* tl, con
             }
         }
         if (CRC) {
-            // Two independent chains: the first 32 bytes continue the lane's
-            // register (jumped over the rest of the warp's step), the second 32
-            // start from zero; the first is then moved 32 bytes on and joined.
-            uint32_t a = crc_jump(far, r), b = 0;
+            r = crc_jump(far, r);
 #pragma unroll
-            for (int k = 0; k < 2; ++k) {
-                a = crc_word(tl, a, cur[k].x);
-                b = crc_word(tl, b, cur[k + 2].x);
-                a = crc_word(tl, a, cur[k].y);
-                b = crc_word(tl, b, cur[k + 2].y);
-                a = crc_word(tl, a, cur[k].z);
-                b = crc_word(tl, b, cur[k + 2].z);
-                a = crc_word(tl, a, cur[k].w);
-                b = crc_word(tl, b, cur[k + 2].w);
+            for (int k = 0; k < 4; ++k) {
+                r = crc_word(tl, r, cur[k].x);
+                r = crc_word(tl, r, cur[k].y);
+                r = crc_word(tl, r, cur[k].z);
+                r = crc_word(tl, r, cur[k].w);
             }
-            r = crc_jump(far + 4 * 256, a) ^ b;
         }
         if (t + 1 < steps) {
 #pragma unroll
@@ -781,7 +764,7 @@ __global__ void __launch_bounds__(256) copy_host_blocks_kernel(const int64_t* so
 // [q*H/g, (q+1)*H/g) of every layer. The shards' packed blocks may sit in
 // this GPU's memory or a peer GPU's (mapped over NVLink with CUDA IPC); the
 // kernel reads them with plain loads, so the transfer over NVLink is fused with
-// the interleave into the cache rows. No multicast, no waits on other GPUs:
+// the interleave into the cache rows. Plain loads only, no waits on other GPUs:
 // the host orders the ranks before and after the launch.
 
 // Byte offset of row (head, token) inside a dense [H, N, C] block span whose
