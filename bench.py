@@ -856,7 +856,7 @@ def run_rotation(args, world, rank, device):
     import threading
     import numpy as np
     import torch
-    from kvsnap_b200.dataplane import TorchBlockDataPlane
+    from kvsnap_b200.dataplane import PendingDigests, TorchBlockDataPlane
     layers, pool_blocks = 28, 32768
     rng = np.random.Generator(np.random.PCG64(args.seed + 44))
     lengths = np.exp(rng.uniform(np.log(512), np.log(8192), 64)).astype(int)
@@ -926,12 +926,14 @@ def run_rotation(args, world, rank, device):
         t0 = time.perf_counter()
 
         def save(i):
-            out = []
+            # The save returns once its blocks are in pinned memory; its digests follow.
+            pending = PendingDigests()
             tokens, blocks = sessions[i]
-            plane.save_gather(blocks, [(a, 0) for a in snapshots[i]], tokens, digests=out)
-            digests[i] = out
+            plane.save_gather(blocks, [(a, 0) for a in snapshots[i]], tokens, digests=pending)
+            digests[i] = pending
 
         list(savers.map(save, range(len(sessions))))
+        digests = [d.result() for d in digests]
         t_saved = time.perf_counter()
         list(loader.map(lambda i: plane.load_scatter(restore_tables[i], [(a, 0) for a in snapshots[i]]),
                         range(len(sessions))))

@@ -106,6 +106,37 @@ class CorruptBlockError(ValueError):
         self.blocks = list(blocks)
 
 
+class PendingDigests:
+    """Content ids and CRC32Cs of a save whose SHA-256 kernel may still be running.
+
+    Pass one as ``save_gather(..., digests=PendingDigests())``: the call returns
+    once the packed blocks are in pinned memory, and ``result()`` later waits for
+    the digest kernel and returns ``[(sha256 hex, crc32c), ...]`` in block order.
+    """
+
+    def __init__(self):
+        self._event = None
+        self._value = None
+
+    def _bind(self, event, crc, digest, stage, n):
+        # The staging buffer is kept referenced until the kernel reading it is done.
+        self._event, self._crc, self._digest, self._stage, self._n = event, crc, digest, stage, n
+
+    def done(self) -> bool:
+        return self._value is not None or (self._event is not None and self._event.query())
+
+    def result(self):
+        if self._value is None:
+            if self._event is None:
+                raise RuntimeError("no save has been bound to these digests")
+            self._event.synchronize()
+            crcs = [v & 0xFFFFFFFF for v in self._crc.cpu().tolist()]
+            raw = self._digest.cpu().numpy().tobytes()
+            self._value = [(raw[32 * i:32 * i + 32].hex(), crcs[i]) for i in range(self._n)]
+            self._crc = self._digest = self._stage = None
+        return self._value
+
+
 class CudaPool:
     """A pinned host arena with one copy stream, over the C ABI v2 (reference dataplane.py:38-131)."""
 
@@ -402,7 +433,7 @@ class TorchBlockDataPlane:
             # SHA-256 kernels overlap each other and the copies.
             self._load_stream = torch.cuda.Stream(self._device())
             self._load_copy_stream = torch.cuda.Stream(self._device())
-            self._sha_streams = [torch.cuda.Stream(self._device()) for _ in range(2)]
+            self._sha_streams = [torch.cuda.Stream(self._device()) for _ in range(4)]
             self._sha_next = 0
             self._sha_lock = threading.Lock()
         return self._span_table
@@ -718,7 +749,10 @@ class TorchBlockDataPlane:
 
         ``digests``: a list that receives ``(sha256 hex, crc32c)`` for each
         packed block, the store's content id and checksum, computed on the GPU
-        from the same bytes the targets receive.
+        from the same bytes the targets receive. A :class:`PendingDigests`
+        instead returns as soon as the targets are written (the point at which
+        the connector may free the GPU blocks) while the SHA-256 kernel still
+        runs; its ``result()`` waits for it and returns the list.
         """
         torch = self.torch
         self._validate_ids(block_ids)
@@ -787,10 +821,12 @@ class TorchBlockDataPlane:
             allocation.wait()
         self._status_error(status)
         if digests is not None:
-            side.synchronize()
-            crcs = [v & 0xFFFFFFFF for v in crc.cpu().tolist()]
-            raw = digest.cpu().numpy().tobytes()
-            digests.extend((raw[32 * i:32 * i + 32].hex(), crcs[i]) for i in range(n))
+            finished = torch.cuda.Event()
+            finished.record(side)
+            pending = digests if isinstance(digests, PendingDigests) else PendingDigests()
+            pending._bind(finished, crc, digest, stage, n)
+            if not isinstance(digests, PendingDigests):
+                digests.extend(pending.result())
         return copies
 
     def _sha_stream(self):

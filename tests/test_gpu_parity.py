@@ -239,6 +239,25 @@ def test_unaligned_sha256_source_takes_the_byte_path():
     assert out.cpu().numpy().tobytes().hex() == hashlib.sha256(data.tobytes()).hexdigest()
 
 
+def test_pending_digests_arrive_after_the_save_returns():
+    from kvsnap_b200.dataplane import PendingDigests
+    case, storages, layout, tensors, caches = cuda_case("qwen3_1p7b_5d")
+    plane = plane_for(caches)
+    try:
+        owned, targets = targets_for(plane, "per-block", len(case["saved"]))
+        pending = PendingDigests()
+        plane.save_gather(case["saved"], targets, case["num_kv_tokens"], digests=pending)
+        expected = oracle.pack(storages, layout, case["saved"], case["num_kv_tokens"])
+        for i, (allocation, offset) in enumerate(targets):     # the bytes are there already
+            assert allocation.read_range(offset, plane.block_bytes) == expected[i].tobytes()
+        assert [list(d) for d in pending.result()] == case["digests"]
+        assert pending.done() and pending.result() is pending.result()
+        with pytest.raises(RuntimeError):
+            PendingDigests().result()
+    finally:
+        plane.close()
+
+
 def test_digest_of_pinned_blocks_matches_host_digest():
     case, storages, layout, tensors, caches = cuda_case("qwen3_1p7b_5d")
     plane = plane_for(caches)
