@@ -30,6 +30,8 @@
 #include <cstdio>
 #include <cstring>
 #include <mutex>
+#include <set>
+#include <utility>
 
 #include "kvsnap_cuda.h"
 #include "kvsnap_internal.h"
@@ -49,6 +51,15 @@ __host__ __device__ constexpr uint32_t gf_mulmod(uint32_t a, uint32_t b) {
     return p;
 }
 
+// x^(-8n) mod P: n bytes of division by x (x is a unit: P has a constant term).
+// In the reflected form bit 31 of a product by x is set exactly when P was
+// added, which makes each step invertible.
+__host__ __device__ constexpr uint32_t gf_xpow_neg8n(int n) {
+    uint32_t r = 1u << 31;
+    for (int k = 0; k < 8 * n; ++k) r = (r >> 31) ? ((r ^ kPoly) << 1) | 1u : r << 1;
+    return r;
+}
+
 __host__ __device__ constexpr uint32_t gf_xpow8n(uint64_t n) {
     uint32_t result = 1u << 31, square = 1u << 23;   // x^0, x^8
     for (; n; n >>= 1) {
@@ -60,9 +71,9 @@ __host__ __device__ constexpr uint32_t gf_xpow8n(uint64_t n) {
 
 // Tables: slots 0..15 hold T_0..T_15, slots 16..19 T_492..T_495 (moving a lane's
 // register 496 bytes ahead), slots 20..23 T_244..T_247 (the same for 8-byte
-// vectors), slots 24..27 T_1980..T_1983 (1984 bytes ahead, for the HBM kernels).
+// vectors).
 struct CrcTables {
-    uint32_t t[28][256];
+    uint32_t t[24][256];
 };
 
 constexpr CrcTables make_tables() {
@@ -75,11 +86,10 @@ constexpr CrcTables make_tables() {
     for (int k = 1; k < 16; ++k)
         for (int v = 0; v < 256; ++v) r.t[k][v] = (r.t[k - 1][v] >> 8) ^ r.t[0][r.t[k - 1][v] & 0xFFu];
     for (int j = 0; j < 4; ++j) {
-        const uint32_t far16 = gf_xpow8n(492 + j), far8 = gf_xpow8n(244 + j), far64 = gf_xpow8n(1980 + j);
+        const uint32_t far16 = gf_xpow8n(492 + j), far8 = gf_xpow8n(244 + j);
         for (int v = 0; v < 256; ++v) {
             r.t[16 + j][v] = gf_mulmod(r.t[0][v], far16);
             r.t[20 + j][v] = gf_mulmod(r.t[0][v], far8);
-            r.t[24 + j][v] = gf_mulmod(r.t[0][v], far64);
         }
     }
     return r;
@@ -302,153 +312,229 @@ __global__ void __launch_bounds__(256) span_kernel(SpanArgs a) {
     }
 }
 
-// ---- wide-lane kernels, for packed blocks in device memory ------------------------
+// ---- segment-lane kernels, for packed blocks in device memory -------------------
 //
-// When both sides of a copy are HBM the CRC lookups, not the bytes, limit the
-// coalesced kernels: slicing-by-16 lookups of 32 random bytes hit a 256-word
-// table with ~3.5-way bank conflicts. Here lane j takes the 64 contiguous bytes
-// [64j, 64j+64) of every 2 KiB warp step (four 16-byte loads; a warp still
-// reads 2 KiB contiguous per step), runs its register straight through them
-// with slicing-by-4, and jumps it 1984 bytes ahead between steps. The four
-// slicing-by-4 tables are replicated once per lane (128 KiB): entry (k, v) of
-// lane l lies in bank l, so those lookups never conflict; only the four jump
-// lookups per 64 bytes use shared, conflicting tables. One 1024-thread CTA per SM.
-constexpr int kRepWords = 4 * 256 * 32;                 // replicated T_0..T_3
-constexpr int kWideSmemBytes = (kRepWords + 4 * 256) * 4;
-constexpr int kWideStep = 2048;
+// When both sides of a copy are HBM, the L1 data pipe (global and shared
+// wavefronts together), not DRAM, bounds a CRC'ing copy. Two things keep its
+// wavefront count per byte near the minimum here:
+//   * every global load and store moves whole 128-byte lines, 8 lanes a line
+//     (fully coalesced);
+//   * each lane owns one contiguous segment of the unit, so its register runs
+//     straight through its bytes with no jump between steps.
+// A unit of `len` bytes is front-padded with zeros to 32 equal segments of S
+// bytes, S a multiple of 128 (a zero prefix leaves a zero-started raw CRC as
+// is). Step t moves line t of every segment: the warp loads the 32 lines
+// coalesced, stores them to the destination, and writes them to a 4 KiB
+// per-warp buffer in shared memory; then lane l reads its own line back and
+// folds it in. The buffer is XOR-swizzled (16-byte slot s of line L lives at
+// slot s ^ (L & 7)), so the coalesced writes and the line-per-lane reads are
+// both free of bank conflicts.
+// A lane keeps four independent CRC chains, one per 32-bit word of each
+// 16-byte vector: chain k folds word k and then 12 zero bytes (the other
+// chains' words), which is slicing-by-4 with T_12..T_15. Four chains give the
+// lookup latency four times the work to hide behind. At the end of a unit the
+// lane's segment satisfies raw(seg) * x^96 = c0 x^96 + c1 x^64 + c2 x^32 + c3,
+// so every accumulated block CRC carries one factor x^96, which the finish
+// step divides out. The four tables are replicated once per lane (entry (k, v)
+// of lane l lies in bank l), so the lookups never conflict. One CTA per SM:
+// 128 KiB of tables and a 4 KiB line buffer per warp.
+constexpr int kRepWords = 4 * 256 * 32;                 // replicated T_12..T_15
+constexpr int kSegLine = 128;                           // bytes of a segment per step
+constexpr int kSegStep = 32 * kSegLine;                 // bytes a warp moves per step
+// Warps a CTA and steps of loads in flight a warp: build-time tuning knobs. On
+// B200 eight warps with two steps in flight measured fastest (more warps leave
+// each thread too few registers to keep its loads in flight).
+#ifndef KVSNAP_SEG_WARPS
+#define KVSNAP_SEG_WARPS 8
+#endif
+#ifndef KVSNAP_SEG_DEPTH
+#define KVSNAP_SEG_DEPTH 2
+#endif
+constexpr int kSegWarps = KVSNAP_SEG_WARPS;
+constexpr int kSegDepth = KVSNAP_SEG_DEPTH;
+constexpr int kSegThreads = 32 * kSegWarps;
+constexpr int kSegSmemBytes = kRepWords * 4 + kSegWarps * kSegStep;
+static_assert(kSegSmemBytes <= 227 * 1024, "segment kernels exceed the shared memory of a CTA");
 
-// Replicated T_0..T_3, then T_1980..T_1983 (the step jump).
-__device__ __forceinline__ void load_wide_tables(uint32_t* tb) {
-    const uint32_t* g = &g_tables.t[0][0];
-    for (int i = threadIdx.x; i < kRepWords; i += blockDim.x) tb[i] = g[i >> 5];
-    for (int i = threadIdx.x; i < 4 * 256; i += blockDim.x) tb[kRepWords + i] = g[24 * 256 + i];
+// Replicated layout, 256 bytes an entry so one byte permute forms an address:
+// entry v of T_{15-(2h+p)} for lane l lies at byte h*65536 + v*256 + p*128 + 4l,
+// which puts every lane in its own bank whatever v is.
+__device__ __forceinline__ void load_rep_tables(uint32_t* tb) {
+    for (int i = threadIdx.x; i < kRepWords; i += blockDim.x) {
+        const int h = i >> 14, v = (i >> 6) & 255, p = (i >> 5) & 1;
+        tb[i] = g_tables.t[15 - (2 * h + p)][v];
+    }
 }
 
-// r <- raw(r, 4 bytes of w), little-endian byte order; tl = replicated tables + lane.
-__device__ __forceinline__ uint32_t crc_word(const uint32_t* tl, uint32_t r, uint32_t w) {
+// The factor the segment kernels leave on every block's raw CRC, inverted.
+constexpr uint32_t kSegUnscale = gf_xpow_neg8n(12);
+
+// The replicated tables as a lane sees them: the shared base and 4 * lane.
+struct RepTables {
+    const char* t;
+    uint32_t l4;
+    __device__ __forceinline__ uint32_t at(int offset, uint32_t x, uint32_t sel) const {
+        // __byte_perm(x, l4, 0x55b4) = (byte b of x) << 8 | 4 * lane
+        return *reinterpret_cast<const uint32_t*>(t + offset + __byte_perm(x, l4, sel));
+    }
+};
+
+// r <- raw(r, the 4 bytes of w then 12 zero bytes), little-endian byte order:
+// T_15[x0] ^ T_14[x1] ^ T_13[x2] ^ T_12[x3] for x = r ^ w.
+__device__ __forceinline__ uint32_t crc_word(const RepTables& tl, uint32_t r, uint32_t w) {
     const uint32_t x = r ^ w;
-    return tl[(768 + (x & 255)) << 5] ^ tl[(512 + ((x >> 8) & 255)) << 5] ^ tl[(256 + ((x >> 16) & 255)) << 5] ^
-           tl[(x >> 24) << 5];
+    return tl.at(0, x, 0x5504) ^ tl.at(128, x, 0x5514) ^ tl.at(65536, x, 0x5524) ^ tl.at(65536 + 128, x, 0x5534);
 }
 
-// r * x^(8*1984) mod P: four lookups in T_1980..T_1983.
-__device__ __forceinline__ uint32_t crc_jump(const uint32_t* far, uint32_t r) {
-    return far[3 * 256 + (r & 255)] ^ far[2 * 256 + ((r >> 8) & 255)] ^ far[256 + ((r >> 16) & 255)] ^ far[r >> 24];
+struct Chains {
+    uint32_t c[4] = {0, 0, 0, 0};
+    __device__ __forceinline__ void fold(const RepTables& tl, uint4 v) {
+        c[0] = crc_word(tl, c[0], v.x);
+        c[1] = crc_word(tl, c[1], v.y);
+        c[2] = crc_word(tl, c[2], v.z);
+        c[3] = crc_word(tl, c[3], v.w);
+    }
+};
+
+// Segment bytes S for a unit of `len` bytes.
+__device__ __forceinline__ int64_t seg_bytes(int64_t len) { return (len + kSegStep - 1) / kSegStep * kSegLine; }
+
+// Token-slot test of the save's last block: the bytes at span offset `at` belong
+// to token slot (at / token_pitch) % tokens, which is >= valid exactly when
+// at mod (token_pitch * tokens) >= valid * token_pitch. A 16-byte vector lies in
+// one (head, token) row when row_bytes is a multiple of 16; otherwise the
+// general byte-wise mask applies.
+struct TailMask {
+    uint32_t group = 0, keep = 0;
+    bool rows = false;
+    TailMask() = default;
+    __device__ TailMask(const kvsnap_span& sp, int valid) {
+        const int64_t g = sp.token_pitch * sp.tokens;
+        rows = sp.row_bytes % 16 == 0 && g > 0 && g <= INT32_MAX && sp.bytes <= INT32_MAX;
+        if (rows) {
+            group = uint32_t(g);
+            keep = uint32_t(valid) * uint32_t(sp.token_pitch);
+        }
+    }
+    __device__ __forceinline__ uint4 apply(uint4 v, int64_t at, const kvsnap_span& sp, int valid) const {
+        if (rows) return uint32_t(at) % group >= keep ? make_uint4(0, 0, 0, 0) : v;
+        return mask_tail<16>(v, at, sp, valid);
+    }
+};
+
+// One warp over one unit of `len` bytes (a multiple of 16). Lane l issues, in
+// every step, the 16-byte slot (l & 7) of lines 4j + (l >> 3), j = 0..7.
+// Returns the lane's four chains over its segment; LaneShift places them.
+// `buf` is the warp's line buffer (used only when CRC).
+__device__ __forceinline__ uint4 seg_load(const char* src, int64_t at) {
+    return at >= 0 ? __ldcs(reinterpret_cast<const uint4*>(src + at)) : make_uint4(0, 0, 0, 0);
 }
 
-// One warp over one unit of `len` bytes (a multiple of 16), front-padded with
-// zeros to whole 2 KiB steps (a zero prefix leaves a zero-started raw CRC as is).
-// Returns the lane's register; the caller multiplies by x^(8*64*(31-lane)).
+// Both sides are streamed: a session is far larger than L2, so nothing a
+// gather or scatter touches is read again from L2.
+__device__ __forceinline__ void seg_store(char* dst, int64_t at, uint4 v) {
+    __stcs(reinterpret_cast<uint4*>(dst + at), v);
+}
+
 template <bool STORE, bool CRC, bool TAIL>
-__device__ __forceinline__ uint32_t warp_unit_wide(const uint32_t* tl, const uint32_t* far,
-                                                   const char* __restrict__ src, char* __restrict__ dst, int64_t len,
-                                                   int lane, const kvsnap_span& sp, int valid) {
-    const int64_t steps = (len + kWideStep - 1) / kWideStep;
-    const int64_t first = (int64_t)lane * 64 - (steps * kWideStep - len);
-    uint32_t r = 0;
-    for (int64_t t = 0; t < steps; ++t) {
-        uint4 v[4];
+__device__ __forceinline__ Chains warp_unit_seg(const RepTables& tl, uint4* buf, const char* __restrict__ src,
+                                                  char* __restrict__ dst, int64_t len, int lane,
+                                                  const kvsnap_span& sp, int valid) {
+    const int64_t seg = seg_bytes(len);
+    const int64_t steps = seg / kSegLine;
+    const int row = lane >> 3, slot = lane & 7;
+    const int64_t first = row * seg + 16 * slot - (32 * seg - len);   // + 4*j*seg + t*kSegLine
+    const TailMask mask = TAIL ? TailMask(sp, valid) : TailMask{};
+    Chains r;
+    // Step t: store and buffer the vectors in v, refill v with step t + kSegDepth
+    // (kSegDepth steps of loads stay in flight), then fold the lane's line.
+    auto step = [&](uint4(&v)[8], int64_t t) {
+        const int64_t here = first + t * kSegLine;
 #pragma unroll
-        for (int k = 0; k < 4; ++k) {
-            const int64_t at = first + t * kWideStep + 16 * k;
-            v[k] = at >= 0 ? *reinterpret_cast<const uint4*>(src + at) : make_uint4(0, 0, 0, 0);
-        }
-#pragma unroll
-        for (int k = 0; k < 4; ++k) {
-            const int64_t at = first + t * kWideStep + 16 * k;
-            if (at >= 0) {
-                if (TAIL) v[k] = mask_tail<16>(v[k], at, sp, valid);
-                if (STORE) *reinterpret_cast<uint4*>(dst + at) = v[k];
+        for (int j = 0; j < 8; ++j) {
+            const int64_t at = here + 4 * j * seg;
+            if (TAIL && at >= 0) v[j] = mask.apply(v[j], at, sp, valid);
+            if (STORE && at >= 0) seg_store(dst, at, v[j]);
+            if (CRC) {
+                const int line = 4 * j + row;
+                buf[line * 8 + (slot ^ (line & 7))] = v[j];
             }
+        }
+        if (t + kSegDepth < steps) {
+            // The front padding can cover whole segments, so every step checks.
+#pragma unroll
+            for (int j = 0; j < 8; ++j) v[j] = seg_load(src, here + kSegDepth * kSegLine + 4 * j * seg);
         }
         if (CRC) {
-            r = crc_jump(far, r);
-#pragma unroll
-            for (int k = 0; k < 4; ++k) {
-                r = crc_word(tl, r, v[k].x);
-                r = crc_word(tl, r, v[k].y);
-                r = crc_word(tl, r, v[k].z);
-                r = crc_word(tl, r, v[k].w);
+            __syncwarp();
+            const uint4* mine = buf + lane * 8;
+            uint4 w = mine[slot];
+#pragma unroll 1
+            for (int k = 1; k < 8; ++k) {   // one slot read ahead of the fold
+                const uint4 now = w;
+                w = mine[k ^ slot];
+                r.fold(tl, now);
             }
+            r.fold(tl, w);
+            __syncwarp();
         }
+    };
+    uint4 v[kSegDepth][8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) v[0][j] = seg_load(src, first + 4 * j * seg);
+#pragma unroll
+    for (int d = 1; d < kSegDepth; ++d) {
+        if (d < steps) {
+#pragma unroll
+            for (int j = 0; j < 8; ++j) v[d][j] = seg_load(src, first + d * kSegLine + 4 * j * seg);
+        }
+    }
+    for (int64_t t = 0; t < steps; t += kSegDepth) {
+        step(v[0], t);
+#pragma unroll
+        for (int d = 1; d < kSegDepth; ++d)
+            if (t + d < steps) step(v[d], t + d);
     }
     return r;
 }
 
-// The common path (no tail masking), software-pipelined: the next step's four
-// 16-byte loads are in flight while this step's vectors are stored and CRC'd,
-// so each lane keeps 128 bytes of reads outstanding across the lookup chain.
-template <bool STORE, bool CRC>
-__device__ __forceinline__ uint32_t warp_unit_wide_piped(const uint32_t* tl, const uint32_t* far,
-                                                         const char* __restrict__ src, char* __restrict__ dst,
-                                                         int64_t len, int lane) {
-    const int64_t steps = (len + kWideStep - 1) / kWideStep;
-    const int64_t first = (int64_t)lane * 64 - (steps * kWideStep - len);
-    uint32_t r = 0;
-    uint4 cur[4];
-#pragma unroll
-    for (int k = 0; k < 4; ++k) {
-        const int64_t at = first + 16 * k;
-        cur[k] = at >= 0 ? *reinterpret_cast<const uint4*>(src + at) : make_uint4(0, 0, 0, 0);
+// Places a lane's chains in its unit: sum_k c_k * x^(32*(3-k)) * x^(8*S*(31-lane))
+// = raw(segment) * x^96 moved to the segment's place. The four factors are
+// recomputed only when the segment size S changes.
+struct LaneShift {
+    int64_t seg = -1;
+    uint32_t k[4] = {0, 0, 0, 0};
+    __device__ __forceinline__ uint32_t place(const Chains& r, int64_t s, int lane) {
+        if (s != seg) {
+            seg = s;
+            k[3] = dev_xpow8n(uint64_t(s) * uint64_t(31 - lane));
+            k[2] = gf_mulmod(k[3], g_pow8.p[2]);             // * x^32
+            k[1] = gf_mulmod(k[3], g_pow8.p[3]);             // * x^64
+            k[0] = gf_mulmod(k[2], g_pow8.p[3]);             // * x^96
+        }
+        return gf_mulmod(r.c[0], k[0]) ^ gf_mulmod(r.c[1], k[1]) ^ gf_mulmod(r.c[2], k[2]) ^
+               gf_mulmod(r.c[3], k[3]);
     }
-    for (int64_t t = 0; t < steps; ++t) {
-        uint4 nxt[4];
-        const int64_t base = first + (t + 1) * kWideStep;   // >= 0 from the second step on
-        if (t + 1 < steps) {
-#pragma unroll
-            for (int k = 0; k < 4; ++k) nxt[k] = *reinterpret_cast<const uint4*>(src + base + 16 * k);
-        }
-        if (STORE) {
-#pragma unroll
-            for (int k = 0; k < 4; ++k) {
-                const int64_t at = first + t * kWideStep + 16 * k;
-                if (at >= 0) *reinterpret_cast<uint4*>(dst + at) = cur[k];
-            }
-        }
-        if (CRC) {
-            r = crc_jump(far, r);
-#pragma unroll
-            for (int k = 0; k < 4; ++k) {
-                r = crc_word(tl, r, cur[k].x);
-                r = crc_word(tl, r, cur[k].y);
-                r = crc_word(tl, r, cur[k].z);
-                r = crc_word(tl, r, cur[k].w);
-            }
-        }
-        if (t + 1 < steps) {
-#pragma unroll
-            for (int k = 0; k < 4; ++k) cur[k] = nxt[k];
-        }
-    }
-    return r;
-}
+};
 
-// The last block of a save, whose tail token slots are written as zeros: kept
-// out of line so the common path's registers stay free of the masking code.
-__device__ __noinline__ uint32_t wide_tail_unit(const uint32_t* tl, const uint32_t* far, const char* src, char* dst,
-                                                const kvsnap_span& sp, int lane, int valid) {
-    return warp_unit_wide<true, true, true>(tl, far, src, dst, sp.bytes, lane, sp, valid);
-}
-
-// Threads a CTA of the HBM kernels (one CTA an SM). The gather's out-of-line
-// tail call spills at this size; its common path does not.
-template <int MODE>
-constexpr int kHbmThreads = 1024;
-
-template <int MODE>
-__global__ void __launch_bounds__(kHbmThreads<MODE>, 1) span_kernel_hbm(SpanArgs a) {
-    extern __shared__ uint32_t tb[];
+// TAIL: every unit belongs to the save's last block, whose token slots from
+// `valid` on are written as zeros. The launcher gives that block a launch of
+// its own, so the common kernel carries none of the masking code.
+template <int MODE, bool TAIL>
+__global__ void __launch_bounds__(kSegThreads, 1) span_kernel_hbm(SpanArgs a) {
+    extern __shared__ uint4 smem[];
+    uint32_t* tb = reinterpret_cast<uint32_t*>(smem);
     const bool crc = a.crc != nullptr;
-    if (crc) load_wide_tables(tb);
+    if (crc) load_rep_tables(tb);
     __syncthreads();
     if (MODE == kScatter && a.gate && *a.gate) return;
     const int lane = threadIdx.x & 31;
-    const uint32_t* tl = tb + lane;
-    const uint32_t* far = tb + kRepWords;
-    const uint32_t lane_shift = crc ? dev_xpow8n(64 * (31 - lane)) : 0;
-    const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
+    const RepTables tl{reinterpret_cast<const char*>(tb), 4u * lane};
+    uint4* buf = smem + kRepWords / 4 + (threadIdx.x >> 5) * (kSegStep / 16);
+    LaneShift lane_shift;
+    const int64_t warps = (int64_t)gridDim.x * kSegWarps;
     const int64_t units = a.n * a.nspans;
-    for (int64_t u = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); u < units; u += warps) {
+    for (int64_t u = (int64_t)blockIdx.x * kSegWarps + (threadIdx.x >> 5); u < units; u += warps) {
         const int64_t i = u / a.nspans;
         const kvsnap_span sp = a.spans[u - i * a.nspans];
         const int64_t block = a.blocks[i];
@@ -464,34 +550,32 @@ __global__ void __launch_bounds__(kHbmThreads<MODE>, 1) span_kernel_hbm(SpanArgs
         }
         const char* src = reinterpret_cast<const char*>(MODE == kGather ? cache : packed);
         char* dst = reinterpret_cast<char*>(MODE == kGather ? packed : cache);
-        const bool tail = MODE == kGather && a.valid > 0 && i == a.n - 1;
         if (crc) {
-            uint32_t r = tail ? wide_tail_unit(tl, far, src, dst, sp, lane, a.valid)
-                              : warp_unit_wide_piped<true, true>(tl, far, src, dst, sp.bytes, lane);
-            r = gf_mulmod(warp_xor(gf_mulmod(r, lane_shift)), sp.crc_shift);
+            const Chains c = warp_unit_seg<true, true, TAIL>(tl, buf, src, dst, sp.bytes, lane, sp, a.valid);
+            const uint32_t r = gf_mulmod(warp_xor(lane_shift.place(c, seg_bytes(sp.bytes), lane)), sp.crc_shift);
             if (lane == 0) atomicXor(&a.crc[i], r);
-        } else if (tail) {
-            wide_tail_unit(tl, far, src, dst, sp, lane, a.valid);
         } else {
-            warp_unit_wide_piped<true, false>(tl, far, src, dst, sp.bytes, lane);
+            warp_unit_seg<true, false, TAIL>(tl, buf, src, dst, sp.bytes, lane, sp, a.valid);
         }
     }
 }
 
-__global__ void __launch_bounds__(1024, 1) crc_kernel_hbm(const int64_t* addrs, int64_t n, int64_t block_bytes,
-                                                          uint32_t* crc, uint32_t* status) {
-    extern __shared__ uint32_t tb[];
-    load_wide_tables(tb);
+__global__ void __launch_bounds__(kSegThreads, 1) crc_kernel_hbm(const int64_t* addrs, int64_t n,
+                                                                 int64_t block_bytes, uint32_t* crc,
+                                                                 uint32_t* status) {
+    extern __shared__ uint4 smem[];
+    uint32_t* tb = reinterpret_cast<uint32_t*>(smem);
+    load_rep_tables(tb);
     __syncthreads();
     const int lane = threadIdx.x & 31;
-    const uint32_t* tl = tb + lane;
-    const uint32_t* far = tb + kRepWords;
-    const uint32_t lane_shift = dev_xpow8n(64 * (31 - lane));
+    const RepTables tl{reinterpret_cast<const char*>(tb), 4u * lane};
+    uint4* buf = smem + kRepWords / 4 + (threadIdx.x >> 5) * (kSegStep / 16);
+    LaneShift lane_shift;
     constexpr int64_t piece = 64 << 10;
     const int64_t pieces = (block_bytes + piece - 1) / piece;
-    const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
+    const int64_t warps = (int64_t)gridDim.x * kSegWarps;
     kvsnap_span none{};
-    for (int64_t u = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); u < n * pieces; u += warps) {
+    for (int64_t u = (int64_t)blockIdx.x * kSegWarps + (threadIdx.x >> 5); u < n * pieces; u += warps) {
         const int64_t i = u / pieces, p = u - i * pieces;
         const int64_t at = p * piece, len = min(piece, block_bytes - at);
         const int64_t base = addrs[i] + at;
@@ -499,9 +583,10 @@ __global__ void __launch_bounds__(1024, 1) crc_kernel_hbm(const int64_t* addrs, 
             if (lane == 0) flag(status, KVSNAP_DP_MISALIGNED);
             continue;
         }
-        uint32_t r = warp_unit_wide_piped<false, true>(tl, far, reinterpret_cast<const char*>(base), nullptr, len,
-                                                       lane);
-        r = gf_mulmod(warp_xor(gf_mulmod(r, lane_shift)), dev_xpow8n(uint64_t(block_bytes - at - len)));
+        const Chains c = warp_unit_seg<false, true, false>(tl, buf, reinterpret_cast<const char*>(base), nullptr,
+                                                           len, lane, none, 0);
+        const uint32_t r = gf_mulmod(warp_xor(lane_shift.place(c, seg_bytes(len), lane)),
+                                     dev_xpow8n(uint64_t(block_bytes - at - len)));
         if (lane == 0) atomicXor(&crc[i], r);
     }
 }
@@ -536,13 +621,14 @@ __global__ void __launch_bounds__(256) crc_kernel(const int64_t* addrs, int64_t 
     }
 }
 
-// crc[i] <- crc[i] ^ (~0 ^ ~0 * x^(8*block_bytes)): the inverted register and
-// output of the standard CRC32C, applied once per block; then the comparison.
-__global__ void finish_kernel(uint32_t* crc, const uint32_t* expect, int64_t n, uint32_t init_term,
-                              uint32_t* status) {
+// crc[i] <- crc[i] * unscale ^ (~0 ^ ~0 * x^(8*block_bytes)): the factor a
+// kernel left on the raw CRC divided out, then the inverted register and
+// output of the standard CRC32C, once per block; then the comparison.
+__global__ void finish_kernel(uint32_t* crc, const uint32_t* expect, int64_t n, uint32_t unscale,
+                              uint32_t init_term, uint32_t* status) {
     const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= n) return;
-    const uint32_t value = crc[i] ^ init_term;
+    const uint32_t value = gf_mulmod(crc[i], unscale) ^ init_term;
     crc[i] = value;
     if (expect && value != expect[i]) flag(status, KVSNAP_DP_CRC_MISMATCH);
 }
@@ -858,6 +944,19 @@ int enter_stream(uintptr_t stream) {
     return sms;
 }
 
+// Raise a kernel's dynamic shared memory limit on the current device, once per
+// (kernel, device): the attribute belongs to the kernel's instance on that device.
+void configure_once(const void* fn, int bytes) {
+    static std::mutex mu;
+    static std::set<std::pair<const void*, int>> done;
+    int device = 0;
+    check(cudaGetDevice(&device));
+    std::lock_guard<std::mutex> hold(mu);
+    if (done.count({fn, device})) return;
+    check(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
+    done.insert({fn, device});
+}
+
 int grid_for(int64_t warps_of_work, int ctas, int sms) {
     if (ctas > 0) return ctas;
     int64_t want = (warps_of_work + 7) / 8;   // 8 warps a CTA
@@ -867,9 +966,10 @@ int grid_for(int64_t warps_of_work, int ctas, int sms) {
 
 uint32_t init_term(uint64_t block_bytes) { return ~0u ^ gf_mulmod(~0u, gf_xpow8n(block_bytes)); }
 
+// unscale: kSegUnscale after the segment kernels, 1 (x^0) after the others.
 void finish(uint32_t* crc, const uint32_t* expect, int64_t n, uint64_t block_bytes, uint32_t* status,
-            cudaStream_t s) {
-    finish_kernel<<<int((n + 255) / 256), 256, 0, s>>>(crc, expect, n, init_term(block_bytes), status);
+            cudaStream_t s, uint32_t unscale = 1u << 31) {
+    finish_kernel<<<int((n + 255) / 256), 256, 0, s>>>(crc, expect, n, unscale, init_term(block_bytes), status);
     check(cudaGetLastError());
 }
 
@@ -921,17 +1021,29 @@ int launch_spans(const kvsnap_span* spans, int nspans, uint64_t block_bytes, con
         if (crc) check(cudaMemsetAsync(crc, 0, sizeof(uint32_t) * size_t(n), s));
         SpanArgs a{spans, nspans, blocks, packed, n, valid, crc, gate, status};
         if (hbm) {
-            static bool configured = false;
-            if (!configured) {
-                check(cudaFuncSetAttribute(span_kernel_hbm<MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                           kWideSmemBytes));
-                configured = true;
+            auto grid_of = [&](int64_t blocks_of_work) {
+                const int64_t want = (blocks_of_work * nspans + kSegWarps - 1) / kSegWarps;
+                return ctas > 0 ? ctas : int(want < sms ? want : sms);
+            };
+            const int smem = crc ? kSegSmemBytes : 0;
+            int64_t body = n;
+            if constexpr (MODE == kGather) {
+                if (valid > 0) {   // the last block, masked, in a launch of its own
+                    body = n - 1;
+                    SpanArgs last{spans, nspans, blocks + body, packed + body, 1, valid, crc ? crc + body : nullptr,
+                                  gate, status};
+                    configure_once(reinterpret_cast<const void*>(span_kernel_hbm<MODE, true>), kSegSmemBytes);
+                    span_kernel_hbm<MODE, true><<<grid_of(1), kSegThreads, smem, s>>>(last);
+                    check(cudaGetLastError());
+                }
             }
-            const int64_t want = (n * nspans + kHbmThreads<MODE> / 32 - 1) / (kHbmThreads<MODE> / 32);
-            const int grid = ctas > 0 ? ctas : int(want < sms ? want : sms);
-            span_kernel_hbm<MODE><<<grid, kHbmThreads<MODE>, crc ? kWideSmemBytes : 0, s>>>(a);
-            check(cudaGetLastError());
-            if (crc) finish(crc, expect, n, block_bytes, status, s);
+            if (body > 0) {
+                a.n = body;
+                configure_once(reinterpret_cast<const void*>(span_kernel_hbm<MODE, false>), kSegSmemBytes);
+                span_kernel_hbm<MODE, false><<<grid_of(body), kSegThreads, smem, s>>>(a);
+                check(cudaGetLastError());
+            }
+            if (crc) finish(crc, expect, n, block_bytes, status, s, kSegUnscale);
             return;
         }
         const int grid = grid_for(n * nspans, ctas, sms);
@@ -977,17 +1089,12 @@ extern "C" int kvsnap_dp_crc32c(const int64_t* addrs, int64_t n, uint64_t block_
         cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
         check(cudaMemsetAsync(crc_out, 0, sizeof(uint32_t) * size_t(n), s));
         if (hbm && vec == 16) {
-            static bool configured = false;
-            if (!configured) {
-                check(cudaFuncSetAttribute(crc_kernel_hbm, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                           kWideSmemBytes));
-                configured = true;
-            }
-            const int64_t want = (n * ((int64_t(block_bytes) + kPiece - 1) / kPiece) + 31) / 32;
+            configure_once(reinterpret_cast<const void*>(crc_kernel_hbm), kSegSmemBytes);
+            const int64_t want = (n * ((int64_t(block_bytes) + kPiece - 1) / kPiece) + kSegWarps - 1) / kSegWarps;
             const int grid = ctas > 0 ? ctas : int(want < sms ? want : sms);
-            crc_kernel_hbm<<<grid, 1024, kWideSmemBytes, s>>>(addrs, n, int64_t(block_bytes), crc_out, status);
+            crc_kernel_hbm<<<grid, kSegThreads, kSegSmemBytes, s>>>(addrs, n, int64_t(block_bytes), crc_out, status);
             check(cudaGetLastError());
-            finish(crc_out, expect, n, block_bytes, status, s);
+            finish(crc_out, expect, n, block_bytes, status, s, kSegUnscale);
             return;
         }
         const int64_t pieces = (int64_t(block_bytes) + kPiece - 1) / kPiece;
@@ -1011,11 +1118,7 @@ extern "C" int kvsnap_dp_sha256(const int64_t* addrs, int64_t n, uint64_t block_
         enter_stream(stream);
         cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
         constexpr int smem = kShaPairs * kShaSlots * kShaSlotWords * int(sizeof(uint32_t));
-        static bool configured = false;   // per process; the attribute is per function, not per device
-        if (!configured) {
-            check(cudaFuncSetAttribute(sha256_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-            configured = true;
-        }
+        configure_once(reinterpret_cast<const void*>(sha256_kernel), smem);
         const int64_t per_cta = 32 * kShaPairs;
         sha256_kernel<<<int((n + per_cta - 1) / per_cta), 64 * kShaPairs, smem, s>>>(addrs, n,
                                                                                     int64_t(block_bytes), out, 1u);
