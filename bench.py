@@ -62,9 +62,11 @@ def parse():
     p.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     p.add_argument("--explore", type=str, default="", help="write a per-phase / CTA sweep breakdown to this path")
     p.add_argument("--seed", type=int, default=0)
-    p.add_argument("--workload", choices=["session", "disk", "reshard", "rotation"], default="session",
+    p.add_argument("--workload", choices=["session", "disk", "reshard", "rotation", "kernels"], default="session",
                    help="session: BASELINE config 2 (the default line); disk: config 3, verified restores of "
-                        "8k and 32k-token snapshots from one pinned staging buffer with seeded corruption")
+                        "8k and 32k-token snapshots from one pinned staging buffer with seeded corruption; "
+                        "reshard: TP regroup over NVLink; rotation: config 4; kernels: the on-device "
+                        "gather, scatter and CRC kernels alone against a torch device copy")
     p.add_argument("--quick", action="store_true",
                    help="only the device-timed steps (a short run for profiling captures)")
     return p.parse_args()
@@ -77,27 +79,55 @@ def log(*args):
 # ---- clocks ----------------------------------------------------------------------------------
 
 class Clocks:
-    """nvidia-smi samples of the SM clock and throttle reasons while the timed region runs."""
+    """nvidia-smi samples of the SM clock and throttle reasons while the timed region runs.
+
+    The sampler starts early (its first sample can take a second or more with eight
+    ranks starting it at once); ``begin`` and ``stop`` bound the timed region, and
+    only samples that arrive inside it count.
+    """
     FIELDS = ("clocks.sm,clocks.max.sm,clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
     def __init__(self, index):
-        self.proc = None
+        import threading
+        self.proc, self.lines, self.t0 = None, [], None
         try:
             self.proc = subprocess.Popen(["nvidia-smi", "-i", str(index), f"--query-gpu={self.FIELDS}",
                                           "--format=csv,noheader,nounits", "-lms", "100"],
                                          stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
         except OSError:
             self.proc = None
+            return
+        self.reader = threading.Thread(target=self._read, daemon=True)
+        self.reader.start()
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append((time.monotonic(), line))
+
+    def begin(self, wait=15.0):
+        """Wait (bounded) for the sampler's first line, then open the timed window."""
+        deadline = time.monotonic() + wait
+        while self.proc is not None and not self.lines and time.monotonic() < deadline:
+            time.sleep(0.05)
+        self.t0 = time.monotonic()
 
     def stop(self):
         if self.proc is None:
             return {"unavailable": "nvidia-smi not found"}
+        t1 = time.monotonic()
+        time.sleep(0.25)                      # let a sample taken inside the window arrive
         self.proc.terminate()
-        out, _ = self.proc.communicate(timeout=10)
+        try:
+            self.proc.wait(timeout=10)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        self.reader.join(timeout=5)
+        t0 = self.t0 if self.t0 is not None else t1
+        inside = [line for t, line in self.lines if t0 <= t <= t1 + 0.25]
         sm, mx, reasons = [], [], set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for line in out.strip().splitlines():
+        for line in inside:
             parts = [x.strip() for x in line.split(",")]
             if len(parts) != 6:
                 continue
@@ -113,6 +143,15 @@ class Clocks:
             return {"unavailable": "no samples"}
         return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "reasons": sorted(reasons),
                 "samples": len(sm)}
+
+
+def smi_index(local):
+    """nvidia-smi's index of this rank's GPU (CUDA_VISIBLE_DEVICES may renumber them)."""
+    visible = os.environ.get("CUDA_VISIBLE_DEVICES", "")
+    parts = [p.strip() for p in visible.split(",") if p.strip()]
+    if local < len(parts) and parts[local].isdigit():
+        return int(parts[local])
+    return local
 
 
 # ---- distributed plumbing ----------------------------------------------------------------------
@@ -187,6 +226,42 @@ def pinned_copy_peaks(nbytes, device, repeats=5):
         out[name] = nbytes / (best / 1e3) / 1e9
     del dev, host
     return out
+
+
+def duplex_box_peak(nbytes, device, world, repeats=3):
+    """Every rank at once: pinned H2D and D2H cudaMemcpy of the session's size on two streams.
+
+    Barrier-aligned and timed with events on each rank (max over ranks, best of
+    ``repeats``); returns the box's aggregate GB/s, both directions summed. This is
+    the ceiling the whole save + restore pipeline shares: on one GPU its full-duplex
+    link, on several GPUs also the host memory and PCIe switches they share.
+    """
+    import torch
+    dev_in = torch.empty(nbytes, dtype=torch.uint8, device=device)
+    dev_out = torch.empty(nbytes, dtype=torch.uint8, device=device)
+    host_in = torch.empty(nbytes, dtype=torch.uint8, pin_memory=True)
+    host_out = torch.empty(nbytes, dtype=torch.uint8, pin_memory=True)
+    up, down = torch.cuda.Stream(device), torch.cuda.Stream(device)
+    best = float("inf")
+    for _ in range(repeats + 1):
+        torch.cuda.synchronize()
+        barrier(world)
+        start = torch.cuda.Event(enable_timing=True)
+        start.record(up)
+        down.wait_event(start)
+        with torch.cuda.stream(up):
+            dev_in.copy_(host_in, non_blocking=True)
+        with torch.cuda.stream(down):
+            host_out.copy_(dev_out, non_blocking=True)
+        done = torch.cuda.Event()
+        done.record(down)
+        up.wait_event(done)
+        end = torch.cuda.Event(enable_timing=True)
+        end.record(up)
+        end.synchronize()
+        best = min(best, max_over_ranks(start.elapsed_time(end), world))
+    del dev_in, dev_out, host_in, host_out
+    return world * 2 * nbytes / (best / 1e3) / 1e9
 
 
 class Engine:
@@ -498,6 +573,9 @@ def main():
     if args.workload == "rotation":
         run_rotation(args, world, rank, device)
         return
+    if args.workload == "kernels":
+        run_kernels(args, world, rank, device)
+        return
     n = (args.tokens + BLOCK - 1) // BLOCK
     t_setup = time.perf_counter()
     caches = make_caches(args, device)
@@ -512,18 +590,20 @@ def main():
     log(f"setup {time.perf_counter() - t_setup:.1f} s; block {size} B, session {session} B")
 
     link = pinned_copy_peaks(session, device)
+    box_duplex = duplex_box_peak(session, device, world)
     engine = Engine(plane, save_ids, restore_ids, args.ctas, args.restore_mode)
 
     # Device-timed steps: a stream of sessions, each step saving one and restoring the previous.
+    clocks = Clocks(smi_index(local))
     for _ in range(max(1, args.warmup)):
         engine.step()
     torch.cuda.synchronize()
     if int(engine.status.item()) != 0:
         raise RuntimeError(f"kernel status {int(engine.status.item())} (CRC mismatch or bad table)")
     barrier(world)
-    clocks = Clocks(local)
     marks = []
     torch.cuda.synchronize()
+    clocks.begin()
     barrier(world)
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     start.record(engine.copy)
@@ -602,20 +682,26 @@ def main():
             a.close()
     digests_ok = check_session(plane, save_ids, restore_ids, args.tokens)
 
-    # One session at a time through the API: restore latency, and save latency with digests.
+    # One session at a time through the API: restore latency; save latency until the
+    # blocks are in pinned memory (when save_gather returns) and until their digests are.
+    from kvsnap_b200.dataplane import PendingDigests
     with plane.staging(n) as snap:
         places = [(snap, i * size) for i in range(n)]
-        save_times, restore_times = [], []
+        save_times, digest_times, restore_times = [], [], []
         for _ in range(max(3, args.steps // 2)):
             torch.cuda.synchronize()
             t0 = time.perf_counter()
-            plane.save_gather(save_ids, places, args.tokens, digests=[])
+            pending = PendingDigests()
+            plane.save_gather(save_ids, places, args.tokens, digests=pending)
             save_times.append((time.perf_counter() - t0) * 1e3)
+            pending.result()
+            digest_times.append((time.perf_counter() - t0) * 1e3)
             t0 = time.perf_counter()
             plane.load_scatter(restore_ids, places)
             restore_times.append((time.perf_counter() - t0) * 1e3)
     restore_ms = max_over_ranks(statistics.median(restore_times), world)
     save_ms = max_over_ranks(statistics.median(save_times), world)
+    save_digests_ms = max_over_ranks(statistics.median(digest_times), world)
 
     explore = {}
     if args.explore and rank == 0:
@@ -648,13 +734,21 @@ def main():
         "phases_ms": {k: round(v, 3) for k, v in phases.items()},
         "restore_ms": round(restore_ms, 3),
         "save_ms": round(save_ms, 3),
+        "save_digests_ms": round(save_digests_ms, 3),
         "host_link": {"h2d_memcpy_gbs": round(link["h2d"], 2), "d2h_memcpy_gbs": round(link["d2h"], 2),
                       "restore_gbs": round(restore_gbs, 2), "restore_frac": round(restore_gbs / link["h2d"], 3),
                       "save_d2h_gbs": round(d2h_gbs, 2), "save_frac": round(d2h_gbs / link["d2h"], 3),
-                      "note": "per-phase rates measured while the other direction runs concurrently"},
+                      "note": "per-phase rates measured while the other direction runs concurrently",
+                      "restore_alone_frac": round(session / (restore_ms / 1e3) / 1e9 / link["h2d"], 3),
+                      "save_alone_frac": round(session / (save_ms / 1e3) / 1e9 / link["d2h"], 3),
+                      "alone_note": "one session at a time through the API (restore_ms, save_ms) over the "
+                                    "pinned cudaMemcpy of the same bytes",
+                      "box_duplex_gbs": round(box_duplex, 2), "value_frac_of_box_duplex": round(value / box_duplex, 3),
+                      "box_note": "every rank's pinned H2D and D2H cudaMemcpy at once, both directions summed: "
+                                  "the ceiling the whole-job value shares"},
         "roofline": {"bound": "hbm", "kernel": "span_kernel_hbm<gather>: KV -> device staging, tail zero, CRC32C",
                      "achieved": round(gather_gbs, 1), "peak": hbm_peak, "unit": "GB/s",
-                     "frac": round(gather_gbs / hbm_peak, 3), "traffic": 2.588e9,
+                     "frac": round(gather_gbs / hbm_peak, 3), "traffic": 2.369e9,
                      "traffic_note": "ncu dram read+write per launch, profiles/span_kernel_hbm_gather_qwen3-8b_512-blocks.md",
                      "algorithmic_bytes": 2 * session, "ms": round(kernel_ms["gather"], 4),
                      "peak_source": f"{peak_src} hbm_gbs (burst copy)"},
@@ -678,6 +772,83 @@ def main():
     if world > 1:
         import torch.distributed as dist
         dist.destroy_process_group()
+
+
+def run_kernels(args, world, rank, device):
+    """The on-device kernels alone on one session (HBM on both sides), each timed with CUDA events.
+
+    Gather and scatter with and without CRC32C, the CRC of device blocks, and a torch
+    device-to-device copy of the same bytes as the control: the fraction of the measured
+    HBM copy rate each reaches (2 x bytes for the copies, 1 x bytes for the CRC alone).
+    """
+    import torch
+    from kvsnap_b200.dataplane import TorchBlockDataPlane
+    n = (args.tokens + BLOCK - 1) // BLOCK
+    caches = make_caches(args, device)
+    save_ids, restore_ids = session_blocks(args, n)
+    plane = TorchBlockDataPlane(caches, BLOCK, 64 << 20, ctas=args.ctas)
+    plane.warm_up()
+    lib, spans, nspans, size = plane.pool.lib, plane._spans(), len(plane.layers), plane.block_bytes
+    total = n * size
+    stage = torch.empty(total, dtype=torch.uint8, device=device)
+    other = torch.empty_like(stage)
+    addrs = torch.arange(n, dtype=torch.int64, device=device) * size + stage.data_ptr()
+    ids = torch.tensor(save_ids, dtype=torch.int64, device=device)
+    ids2 = torch.tensor(restore_ids, dtype=torch.int64, device=device)
+    crc = torch.zeros(n, dtype=torch.int32, device=device)
+    crc2 = torch.zeros(n, dtype=torch.int32, device=device)
+    status = torch.zeros(1, dtype=torch.int32, device=device)
+    stream = torch.cuda.current_stream(device).cuda_stream
+    hbm = 16 | plane._hbm
+
+    def ok(rc):
+        if rc != 0:
+            raise RuntimeError(lib.kvsnap_cuda_error().decode())
+
+    def gather(with_crc):
+        ok(lib.kvsnap_dp_gather(spans.data_ptr(), nspans, size, ids.data_ptr(), addrs.data_ptr(), n, 0,
+                                crc.data_ptr() if with_crc else 0, status.data_ptr(), hbm, args.ctas, stream))
+
+    def scatter(with_crc):
+        ok(lib.kvsnap_dp_scatter(spans.data_ptr(), nspans, size, addrs.data_ptr(), ids2.data_ptr(), n,
+                                 crc2.data_ptr() if with_crc else 0, crc.data_ptr() if with_crc else 0, 0,
+                                 status.data_ptr(), hbm, args.ctas, stream))
+
+    def crc_only():
+        ok(lib.kvsnap_dp_crc32c(addrs.data_ptr(), n, size, crc2.data_ptr(), crc.data_ptr(), status.data_ptr(),
+                                hbm, args.ctas, stream))
+
+    def timed(fn):
+        for _ in range(max(3, args.warmup)):
+            fn()
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(args.steps):
+            fn()
+        b.record()
+        torch.cuda.synchronize()
+        return a.elapsed_time(b) / args.steps
+
+    peak = json.loads(PEAKS.read_text()).get("hbm_gbs", 6650.0) if PEAKS.is_file() else 6650.0
+    gather(True)                  # the CRCs every later check compares against
+    torch.cuda.synchronize()
+    rows = {"torch_copy": (timed(lambda: other.copy_(stage)), 2),
+            "gather_crc": (timed(lambda: gather(True)), 2),
+            "gather_copy": (timed(lambda: gather(False)), 2),
+            "scatter_crc": (timed(lambda: scatter(True)), 2),
+            "scatter_copy": (timed(lambda: scatter(False)), 2),
+            "crc_only": (timed(crc_only), 1)}
+    torch.cuda.synchronize()
+    if int(status.item()) != 0:
+        raise RuntimeError(f"kernel status {int(status.item())}: a verified scatter or CRC disagreed")
+    if rank == 0:
+        print(json.dumps({"workload": f"on-device kernels, qwen3-8b {n}-block session ({total} B)",
+                          "steps": args.steps, "peak_gbs": peak,
+                          "kernels": {k: {"ms": round(ms, 4), "gbs": round(m * total / ms / 1e6, 1),
+                                          "frac": round(m * total / ms / 1e6 / peak, 3)}
+                                      for k, (ms, m) in rows.items()}}), flush=True)
+    plane.close()
 
 
 def run_disk(args, world, rank, device):
@@ -768,7 +939,7 @@ def run_reshard(args, world, rank, device):
     import torch
     import torch.distributed as dist
     from kvsnap_b200.dataplane import TorchBlockDataPlane
-    from kvsnap_b200.reshard import RegroupPlan, regroup_restore
+    from kvsnap_b200.reshard import RegroupPlan, Regrouper
     if world < 2 or world % 2:
         raise SystemExit("the regroup workload needs an even number of ranks (torchrun --nproc-per-node 2|4|8)")
     plan = RegroupPlan(world, world // 2)
@@ -788,16 +959,18 @@ def run_reshard(args, world, rank, device):
     sources = [(snapshot, i * shard) for i in range(n)]
     order = np.random.Generator(np.random.PCG64(args.seed + 5)).permutation(pool - 1) + 1
     restored = [int(b) for b in order[:n]]
-    regroup_restore(plane, plan, rank, restored, sources)                 # warm: maps, loads kernels
+    regrouper = Regrouper(plane, plan, rank)
+    regrouper.restore(restored, sources)                 # warm: shard buffer, IPC maps, kernels
     runs = []
     for _ in range(max(3, args.steps // 2)):
         torch.cuda.synchronize()
         dist.barrier()
         timings = {}
         t0 = time.perf_counter()
-        regroup_restore(plane, plan, rank, restored, sources, timings=timings)
+        regrouper.restore(restored, sources, timings=timings)
         timings["total_s"] = time.perf_counter() - t0
         runs.append(timings)
+    regrouper.close()
     # Parity on sample blocks: destination rank r's packed block i = interleave of shards 2r, 2r+1.
     samples = [0, n // 2, n - 1]
     mine = torch.stack([noise[i * shard:(i + 1) * shard] for i in samples])

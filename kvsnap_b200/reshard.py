@@ -19,6 +19,9 @@ Design (one process per GPU, torch.distributed for the plumbing):
    NVLink, and writes each (head, token) row into its own cache blocks;
 4. a second barrier keeps the source buffers alive until every reader is done.
 
+``Regrouper`` keeps the shard buffer, its handle and the peer mappings from
+one restore to the next; ``regroup_restore`` is the one-shot form.
+
 Parity is defined by slicing: after the regroup, rank r's cache blocks hold
 exactly the heads a TP-size-T save of the same KV would hold
 (oracle ``slice_heads``), and re-saving them gives the same packed bytes, CRCs
@@ -116,98 +119,178 @@ def close_peer(lib, ptr: int) -> None:
         raise RuntimeError(lib.kvsnap_cuda_error().decode())
 
 
+class Regrouper:
+    """A TP regroup that keeps its shard buffer and peer mappings from one restore to the next.
+
+    Collective: every rank of ``group`` builds one, calls ``restore`` the same
+    number of times and then ``close``. Source rank s of the plan runs on
+    torch.distributed rank s; destination rank r on rank r.
+
+    What a one-shot regroup pays on every call is paid here once:
+    - the shareable device buffer of this rank's shard, kept and grown on demand;
+    - its CUDA IPC handle, exported once per buffer;
+    - the destination's mappings of its peers' buffers, reopened only when a
+      peer's handle changes.
+    A buffer replaced by a larger one stays alive until the barrier that ends
+    the restore, by which time every destination has closed its mapping.
+    """
+
+    def __init__(self, plane, plan: RegroupPlan, rank: int, *, group=None, is_destination=None):
+        import torch
+        from .dataplane import _dp
+        self.plane, self.plan, self.rank, self.group = plane, plan, rank, group
+        self.lib = _dp(plane.pool.lib)
+        self.device = plane._device()
+        plane._spans()
+        self.stream = plane._scatter_targets()
+        host_spans = _abi.Span * len(plane.layers)
+        dst_host = host_spans.from_buffer_copy(plane._span_table.cpu().numpy().tobytes())
+        self.src_spans, self.shard_bytes = shard_spans(dst_host, plan.groups)
+        self.src_table = torch.frombuffer(bytearray(bytes(self.src_spans)), dtype=torch.uint8).to(self.device)
+        self.is_source = rank < plan.src_tp
+        self.is_destination = rank < plan.dst_tp if is_destination is None else is_destination
+        self.buffer, self.handle, self.retired = None, None, []
+        self.peers = {}                  # source rank -> (IPC handle, mapped pointer)
+        self.closed = False
+
+    def restore(self, block_ids, shard_sources, *, expected_crc32c=None, timings=None) -> int:
+        """Regroup one snapshot into this rank's cache blocks; returns the launches on this rank.
+
+        ``shard_sources``: this rank's own shard of the snapshot,
+        ``[(allocation, offset), ...]`` one packed block per entry of ``block_ids``
+        (source ranks only; ``None`` elsewhere). ``block_ids``: the destination
+        rank's cache blocks (ignored on ranks that are not a destination).
+        ``expected_crc32c``: this rank's shard CRCs, checked on the GPU before
+        anyone reads the shard; a mismatch on any rank raises CorruptBlockError on
+        every rank with no cache written. ``timings``: receives the host-side
+        seconds of the stage, exchange and regroup phases and the regroup
+        kernel's device milliseconds.
+        """
+        import time
+        import torch
+        import torch.distributed as dist
+        from .dataplane import CorruptBlockError
+        if self.closed:
+            raise RuntimeError("regrouper is closed")
+        n = len(block_ids)
+        # 1. Source ranks stage their shard in shareable device memory and check it.
+        #    A failure here is carried into the exchange, so every rank still takes
+        #    the same collective steps and all of them raise it afterwards.
+        failure = None
+        t0 = time.perf_counter()
+        try:
+            if self.is_source and n:
+                self._stage(n, shard_sources, expected_crc32c)
+        except CorruptBlockError as exc:
+            failure = str(exc)
+        except Exception as exc:          # noqa: BLE001 - reported to every rank, then raised
+            failure = f"rank {self.rank}: {type(exc).__name__}: {exc}"
+
+        # 2. Exchange handles and verdicts; every rank takes the same collective steps.
+        t1 = time.perf_counter()
+        failures, everyone = exchange((self.handle if self.is_source else None, failure), self.group)
+        t2 = time.perf_counter()
+        launches = 0
+        try:
+            if self.is_destination and n:
+                # Remap every changed peer now, failed restore or not, so that no
+                # mapping of a buffer its owner retires outlives the barrier below.
+                for src in self.plan.sources(self.rank):
+                    if src != self.rank and everyone[src][0] is not None:
+                        self._shard(src, everyone[src][0])
+            if not failures and self.is_destination and n:
+                shards = [self._shard(src, everyone[src][0]) for src in self.plan.sources(self.rank)]
+                rows = [shards[q] + i * self.shard_bytes for i in range(n) for q in range(self.plan.groups)]
+                device, stream = self.device, self.stream
+                with torch.cuda.stream(stream):
+                    table = torch.tensor(rows + list(block_ids), dtype=torch.int64, device=device)
+                    status = torch.zeros(1, dtype=torch.int32, device=device)
+                    begin, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                    begin.record(stream)
+                    if self.lib.kvsnap_dp_regroup(self.plane._span_table.data_ptr(), self.src_table.data_ptr(),
+                                                  len(self.plane.layers), table.data_ptr(), self.plan.groups,
+                                                  table[len(rows):].data_ptr(), n, status.data_ptr(), 0,
+                                                  stream.cuda_stream) < 0:
+                        raise RuntimeError(self.lib.kvsnap_cuda_error().decode())
+                    end.record(stream)
+                    launches = 1
+                stream.synchronize()
+                if timings is not None:
+                    timings["kernel_ms"] = begin.elapsed_time(end)
+                if int(status.item()):
+                    raise RuntimeError(f"regroup kernel reported status {int(status.item())}")
+        finally:
+            # 3. Nobody frees a shard another rank may still be reading.
+            dist.barrier(group=self.group)
+            if timings is not None:
+                timings.update(stage_s=t1 - t0, exchange_s=t2 - t1, regroup_s=time.perf_counter() - t2)
+            for old in self.retired:
+                old.close()
+            self.retired = []
+        if failures:
+            raise CorruptBlockError("; ".join(failures))
+        return launches
+
+    def close(self):
+        """Collective: close the peer mappings, wait for every rank, then free this rank's buffer."""
+        import torch.distributed as dist
+        if self.closed:
+            return
+        self.closed = True
+        try:
+            for _, ptr in self.peers.values():
+                close_peer(self.lib, ptr)
+            self.peers = {}
+        finally:
+            dist.barrier(group=self.group)
+            for buf in [self.buffer, *self.retired]:
+                if buf is not None:
+                    buf.close()
+            self.buffer, self.handle, self.retired = None, None, []
+
+    def _shard(self, src: int, handle) -> int:
+        """Device address of source rank ``src``'s shard: this rank's own buffer, or a peer mapping."""
+        if src == self.rank:
+            return self.buffer.ptr
+        if handle is None:
+            raise RuntimeError(f"source rank {src} shared no shard")
+        cached = self.peers.get(src)
+        if cached is not None and cached[0] == handle:
+            return cached[1]
+        if cached is not None:
+            del self.peers[src]
+            close_peer(self.lib, cached[1])
+        ptr = open_peer(self.lib, handle, self.device.index)
+        self.peers[src] = (handle, ptr)
+        return ptr
+
+    def _stage(self, n, shard_sources, expected_crc32c):
+        """Copy this rank's shard into its shareable buffer (grown if needed) and check its CRCs there."""
+        need = n * self.shard_bytes
+        if self.buffer is None or self.buffer.size < need:
+            if self.buffer is not None:
+                self.retired.append(self.buffer)
+            self.buffer, self.handle = None, None
+            self.buffer = SharedBuffer(self.lib, need, self.device.index)
+            self.handle = self.buffer.handle()
+        _stage_shard(self.lib, self.plane, self.stream, self.rank, n, self.shard_bytes, shard_sources,
+                     expected_crc32c, self.buffer)
+
+
 def regroup_restore(plane, plan: RegroupPlan, rank: int, block_ids, shard_sources, *, group=None,
                     expected_crc32c=None, is_destination=None, timings=None):
-    """Collective TP regroup restore; every rank of ``group`` calls it.
+    """One collective TP regroup restore; every rank of ``group`` calls it.
 
     ``plane``: this rank's TorchBlockDataPlane, registered at the destination TP
-    size (its caches hold this rank's heads). ``shard_sources``: this rank's own
-    shard of the snapshot, ``[(allocation, offset), ...]`` one packed block per
-    entry of ``block_ids`` (source ranks only; ``None`` elsewhere).
-    ``block_ids``: the destination rank's cache blocks (ignored on ranks that are
-    not a destination). ``expected_crc32c``: this rank's shard CRCs, checked on
-    the GPU before anyone reads the shard. Source rank s of the plan runs on
-    torch.distributed rank s; destination rank r on rank r. Returns the number
-    of regroup launches on this rank. ``timings``: a dict that receives the
-    host-side seconds of the stage, exchange and regroup phases and the regroup
-    kernel's device milliseconds.
+    size (its caches hold this rank's heads). The other arguments are those of
+    ``Regrouper.restore``. A caller that regroups repeatedly keeps a Regrouper
+    instead, which skips the per-call buffer and IPC setup.
     """
-    import time
-    import torch
-    import torch.distributed as dist
-    from .dataplane import CorruptBlockError, _dp
-
-    lib = _dp(plane.pool.lib)
-    device = plane._device()
-    plane._spans()
-    stream = plane._scatter_targets()
-    host_spans = _abi.Span * len(plane.layers)
-    dst_host = host_spans.from_buffer_copy(plane._span_table.cpu().numpy().tobytes())
-    src_spans, shard_bytes = shard_spans(dst_host, plan.groups)
-    n = len(block_ids)
-    is_source = rank < plan.src_tp
-    is_destination = rank < plan.dst_tp if is_destination is None else is_destination
-
-    # 1. Source ranks stage their shard in shareable device memory and check it.
-    #    A failure here is carried into the exchange, so every rank still takes
-    #    the same collective steps and all of them raise it afterwards.
-    buffer, failure = None, None
-    t0 = time.perf_counter()
+    regrouper = Regrouper(plane, plan, rank, group=group, is_destination=is_destination)
     try:
-        if is_source and n:
-            buffer = _stage_shard(lib, plane, stream, rank, n, shard_bytes, shard_sources, expected_crc32c)
-    except CorruptBlockError as exc:
-        failure = str(exc)
-    except Exception as exc:          # noqa: BLE001 - reported to every rank, then raised
-        failure = f"rank {rank}: {type(exc).__name__}: {exc}"
-
-    # 2. Exchange handles and verdicts; every rank takes the same collective steps.
-    t1 = time.perf_counter()
-    mine = (buffer.handle() if buffer is not None else None, failure)
-    failures, everyone = exchange(mine, group)
-    t2 = time.perf_counter()
-    launches = 0
-    peers = []
-    try:
-        if not failures and is_destination and n:
-            shards = []
-            for src in plan.sources(rank):
-                handle = everyone[src][0]
-                if src == rank:
-                    shards.append(buffer.ptr)
-                else:
-                    peers.append(open_peer(lib, handle, device.index))
-                    shards.append(peers[-1])
-            src_table = torch.frombuffer(bytearray(bytes(src_spans)), dtype=torch.uint8).to(device)
-            rows = [shards[q] + i * shard_bytes for i in range(n) for q in range(plan.groups)]
-            with torch.cuda.stream(stream):
-                table = torch.tensor(rows + list(block_ids), dtype=torch.int64, device=device)
-                status = torch.zeros(1, dtype=torch.int32, device=device)
-                begin, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-                begin.record(stream)
-                if lib.kvsnap_dp_regroup(plane._span_table.data_ptr(), src_table.data_ptr(), len(plane.layers),
-                                         table.data_ptr(), plan.groups, table[len(rows):].data_ptr(), n,
-                                         status.data_ptr(), 0, stream.cuda_stream) < 0:
-                    raise RuntimeError(lib.kvsnap_cuda_error().decode())
-                end.record(stream)
-                launches = 1
-            stream.synchronize()
-            if timings is not None:
-                timings["kernel_ms"] = begin.elapsed_time(end)
-            if int(status.item()):
-                raise RuntimeError(f"regroup kernel reported status {int(status.item())}")
+        return regrouper.restore(block_ids, shard_sources, expected_crc32c=expected_crc32c, timings=timings)
     finally:
-        # 3. Nobody frees a shard another rank may still be reading.
-        dist.barrier(group=group)
-        if timings is not None:
-            timings.update(stage_s=t1 - t0, exchange_s=t2 - t1, regroup_s=time.perf_counter() - t2)
-        for ptr in peers:
-            close_peer(lib, ptr)
-        if buffer is not None:
-            buffer.close()
-    if failures:
-        raise CorruptBlockError("; ".join(failures))
-    return launches
+        regrouper.close()
 
 
 def exchange(mine, group=None):
@@ -218,8 +301,11 @@ def exchange(mine, group=None):
     return [f for _, f in everyone if f], everyone
 
 
-def _stage_shard(lib, plane, stream, rank, n, shard_bytes, shard_sources, expected_crc32c):
-    """Copy this rank's shard into shareable device memory and check its CRCs there."""
+def _stage_shard(lib, plane, stream, rank, n, shard_bytes, shard_sources, expected_crc32c, buffer):
+    """Copy this rank's shard into ``buffer`` and check its CRCs there.
+
+    Runs of sources adjacent in one allocation move in one copy.
+    """
     import torch
     from .dataplane import CorruptBlockError
     if shard_sources is None or len(shard_sources) != n:
@@ -229,11 +315,17 @@ def _stage_shard(lib, plane, stream, rank, n, shard_bytes, shard_sources, expect
         if offset < 0 or offset + shard_bytes > allocation.size:
             raise ValueError("shard source outside its allocation")
     device = plane._device()
-    buffer = SharedBuffer(lib, n * shard_bytes, device.index)
     try:
         with torch.cuda.stream(stream):
-            for i, (allocation, offset) in enumerate(shard_sources):
-                allocation.copy(buffer.ptr + i * shard_bytes, shard_bytes, offset, to_host=False)
+            i = 0
+            while i < n:
+                allocation, offset = shard_sources[i]
+                j = i + 1
+                while j < n and shard_sources[j][0] is allocation and \
+                        shard_sources[j][1] == offset + (j - i) * shard_bytes:
+                    j += 1
+                allocation.copy(buffer.ptr + i * shard_bytes, (j - i) * shard_bytes, offset, to_host=False)
+                i = j
             if expected_crc32c is not None:
                 table = torch.tensor([buffer.ptr + i * shard_bytes for i in range(n)], dtype=torch.int64,
                                      device=device)
@@ -250,6 +342,4 @@ def _stage_shard(lib, plane, stream, rank, n, shard_bytes, shard_sources, expect
         stream.synchronize()
     except BaseException:
         stream.synchronize()
-        buffer.close()
         raise
-    return buffer

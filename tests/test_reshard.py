@@ -168,7 +168,7 @@ def _collective_worker(rank, world, port, env):
     sys.path[:0] = [str(ROOT), str(ROOT / "tests")]
     import torch.distributed as dist
     from kvsnap_b200.dataplane import CorruptBlockError, TorchBlockDataPlane
-    from kvsnap_b200.reshard import RegroupPlan, regroup_restore
+    from kvsnap_b200.reshard import Regrouper, RegroupPlan, regroup_restore
     device = rank % torch.cuda.device_count()
     torch.cuda.set_device(device)
     dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world)
@@ -200,12 +200,35 @@ def _collective_worker(rank, world, port, env):
             assert not tensor.view(torch.int16).any().item(), "cache written despite a corrupt shard"
         launches = regroup_restore(plane, plan, rank, restored, sources, expected_crc32c=crcs)
         assert launches == (1 if rank == 0 else 0)
-        if rank == 0:
-            for name, tensor in caches.items():
-                got = tensor.view(torch.int16).cpu().numpy().view(np.uint16)
-                expect = np.zeros_like(full[name])
-                expect[:, restored] = full[name][:, saved]
-                assert np.array_equal(got, expect), name
+
+        def check(into, count):
+            if rank == 0:
+                for name, tensor in caches.items():
+                    got = tensor.view(torch.int16).cpu().numpy().view(np.uint16)
+                    expect = np.zeros_like(full[name])
+                    expect[:, into[:count]] = full[name][:, saved[:count]]
+                    assert np.array_equal(got, expect), name
+
+        check(restored, len(saved))
+        # A kept Regrouper: a smaller restore, a corrupt one, then a larger one that grows
+        # every source buffer (so every destination remaps), all through the same object.
+        for tensor in caches.values():
+            tensor.zero_()
+        regrouper = Regrouper(plane, plan, rank)
+        try:
+            assert regrouper.restore(restored[:2], sources[:2], expected_crc32c=crcs[:2]) == (1 if rank == 0 else 0)
+            check(restored, 2)
+            with_error = None
+            try:
+                regrouper.restore(restored, sources, expected_crc32c=bad)
+            except CorruptBlockError as exc:
+                with_error = str(exc)
+            assert with_error and "failed its CRC32C check" in with_error
+            check(restored, 2)
+            regrouper.restore(restored, sources, expected_crc32c=crcs)
+            check(restored, len(saved))
+        finally:
+            regrouper.close()
         dist.barrier()
         snapshot.close()
         plane.close()
