@@ -31,6 +31,7 @@ import os
 import statistics
 import subprocess
 import sys
+import threading
 import time
 from concurrent.futures import ThreadPoolExecutor
 from pathlib import Path
@@ -644,24 +645,37 @@ def main():
 
     # End to end through the public API, host tier (one pinned allocation per block), with the
     # connector's threads: two save workers (vllm.py:202) and one load worker (vllm.py:203). Session k
-    # is saved into snapshot k % 3 (with its digests) and restored once its save has returned.
+    # is saved into snapshot k % 3 the way the drop-in connector saves: save_gather returns once the
+    # blocks are in pinned memory (PendingDigests), and the save worker then collects the content ids
+    # and CRCs the store needs. Session k is restored once save_gather has returned for it; a
+    # snapshot is reused once its digests are in and its restore is done.
+    from kvsnap_b200.dataplane import PendingDigests
     sets = [[plane.pool.reserve(size) for _ in range(n)] for _ in range(3)]
     places = [[(a, 0) for a in owned] for owned in sets]
     savers, loader = ThreadPoolExecutor(max_workers=2), ThreadPoolExecutor(max_workers=1)
 
+    def save_session(k, landed):
+        pending = PendingDigests()
+        try:
+            plane.save_gather(save_ids, places[k % 3], args.tokens, digests=pending)
+        finally:
+            landed.set()                             # a failed save surfaces through its future
+        return pending.result()
+
     def run_sessions(first, count):
-        saves, restores = {}, []
+        saves, landed, restores = {}, {}, []
         for k in range(first, first + count):
             if k - 3 in saves:                       # snapshot k % 3 is free once its restore is done
                 saves.pop(k - 3).result()
                 while restores and restores[0][0] <= k - 3:
                     restores.pop(0)[1].result()
-            saves[k] = savers.submit(plane.save_gather, save_ids, places[k % 3], args.tokens, digests=[])
+            landed[k] = threading.Event()
+            saves[k] = savers.submit(save_session, k, landed[k])
             if k - 1 >= first:
-                saves[k - 1].result()
+                landed[k - 1].wait()
                 restores.append((k - 1, loader.submit(plane.load_scatter, restore_ids, places[(k - 1) % 3])))
         last = first + count - 1
-        saves[last].result()
+        landed[last].wait()
         restores.append((last, loader.submit(plane.load_scatter, restore_ids, places[last % 3])))
         for _, f in restores:
             f.result()
@@ -843,7 +857,8 @@ def run_kernels(args, world, rank, device):
     if int(status.item()) != 0:
         raise RuntimeError(f"kernel status {int(status.item())}: a verified scatter or CRC disagreed")
     if rank == 0:
-        print(json.dumps({"workload": f"on-device kernels, qwen3-8b {n}-block session ({total} B)",
+        print(json.dumps({"workload": f"on-device kernels, {args.layers} layers x {args.heads} KV heads, "
+                                      f"{n}-block session ({total} B)",
                           "steps": args.steps, "peak_gbs": peak,
                           "kernels": {k: {"ms": round(ms, 4), "gbs": round(m * total / ms / 1e6, 1),
                                           "frac": round(m * total / ms / 1e6 / peak, 3)}

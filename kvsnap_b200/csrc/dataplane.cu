@@ -342,10 +342,11 @@ constexpr int kRepWords = 4 * 256 * 32;                 // replicated T_12..T_15
 constexpr int kSegLine = 128;                           // bytes of a segment per step
 constexpr int kSegStep = 32 * kSegLine;                 // bytes a warp moves per step
 // Warps a CTA and steps of loads in flight a warp: build-time tuning knobs. On
-// B200 eight warps with two steps in flight measured fastest (more warps leave
-// each thread too few registers to keep its loads in flight).
+// B200 twelve warps with two steps in flight measured fastest over 4, 8 and
+// 32 KiB spans (more warps leave each thread too few registers to keep its
+// loads in flight; fewer leave small spans' per-unit work exposed).
 #ifndef KVSNAP_SEG_WARPS
-#define KVSNAP_SEG_WARPS 8
+#define KVSNAP_SEG_WARPS 12
 #endif
 #ifndef KVSNAP_SEG_DEPTH
 #define KVSNAP_SEG_DEPTH 2
@@ -364,6 +365,12 @@ __device__ __forceinline__ void load_rep_tables(uint32_t* tb) {
         const int h = i >> 14, v = (i >> 6) & 255, p = (i >> 5) & 1;
         tb[i] = g_tables.t[15 - (2 * h + p)][v];
     }
+}
+
+// The replicated T_12..T_15 and one plain copy of T_0..T_3.
+__device__ __forceinline__ void load_seg_tables(uint32_t* tb, uint32_t* t4) {
+    load_rep_tables(tb);
+    for (int i = threadIdx.x; i < 4 * 256; i += blockDim.x) t4[i] = g_tables.t[i >> 8][i & 255];
 }
 
 // The factor the segment kernels leave on every block's raw CRC, inverted.
@@ -422,10 +429,6 @@ struct TailMask {
     }
 };
 
-// One warp over one unit of `len` bytes (a multiple of 16). Lane l issues, in
-// every step, the 16-byte slot (l & 7) of lines 4j + (l >> 3), j = 0..7.
-// Returns the lane's four chains over its segment; LaneShift places them.
-// `buf` is the warp's line buffer (used only when CRC).
 __device__ __forceinline__ uint4 seg_load(const char* src, int64_t at) {
     return at >= 0 ? __ldcs(reinterpret_cast<const uint4*>(src + at)) : make_uint4(0, 0, 0, 0);
 }
@@ -436,159 +439,283 @@ __device__ __forceinline__ void seg_store(char* dst, int64_t at, uint4 v) {
     __stcs(reinterpret_cast<uint4*>(dst + at), v);
 }
 
-template <bool STORE, bool CRC, bool TAIL>
-__device__ __forceinline__ Chains warp_unit_seg(const RepTables& tl, uint4* buf, const char* __restrict__ src,
-                                                  char* __restrict__ dst, int64_t len, int lane,
-                                                  const kvsnap_span& sp, int valid) {
-    const int64_t seg = seg_bytes(len);
-    const int64_t steps = seg / kSegLine;
+// r * x^32 mod P: four zero bytes through slicing-by-4 (T_0..T_3, one shared copy).
+__device__ __forceinline__ uint32_t mul_x32(const uint32_t* t4, uint32_t r) {
+    return t4[768 + (r & 255)] ^ t4[512 + ((r >> 8) & 255)] ^ t4[256 + ((r >> 16) & 255)] ^ t4[r >> 24];
+}
+
+// Places a lane's chains in its unit: ((c0 x^32 + c1) x^32 + c2) x^32 + c3
+// = raw(segment) * x^96, times x^(8*S*(31-lane)) to move it to the segment's
+// place. That last factor is recomputed only when the segment size S changes.
+struct LaneShift {
+    int64_t seg = -1;
+    uint32_t k = 0;
+    __device__ __forceinline__ uint32_t place(const Chains& r, const uint32_t* t4, int64_t s, int lane) {
+        if (s != seg) {
+            seg = s;
+            k = dev_xpow8n(uint64_t(s) * uint64_t(31 - lane));
+        }
+        uint32_t h = mul_x32(t4, r.c[0]) ^ r.c[1];
+        h = mul_x32(t4, h) ^ r.c[2];
+        h = mul_x32(t4, h) ^ r.c[3];
+        return gf_mulmod(h, k);
+    }
+};
+
+// ---- a warp's stream of units --------------------------------------------------
+//
+// A warp takes its units (grid-stride) as one stream of 4 KiB steps, so the
+// loads of the next units' first steps are in flight while the current unit
+// finishes: small units (a TP shard's 4 or 8 KiB spans) pay no load latency of
+// their own. The load side runs kSegDepth steps ahead of the fold side and
+// hands each unit's description over through a ring in shared memory.
+
+// One unit as the warp's stream carries it (the same in every lane).
+struct alignas(16) SegUnit {
+    const char* src;
+    char* dst;
+    int64_t seg;         // bytes a lane owns, a multiple of kSegLine
+    int64_t pad;         // zero bytes in front of the unit
+    int64_t block;       // the packed block it belongs to (its CRC accumulator)
+    uint32_t shift;      // x^(8 * bytes after the unit in its packed block)
+    int32_t steps;       // seg / kSegLine
+    int32_t span;        // span index (the tail mask)
+};
+// The load side is at most kSegDepth steps, so at most kSegDepth + 1 units
+// (it moves on to the next unit as soon as it issues a unit's last step),
+// ahead of the unit being folded: kSegDepth + 2 entries never collide.
+constexpr int kRing = 4;
+static_assert(kRing >= kSegDepth + 2 && (kRing & (kRing - 1)) == 0, "ring of unit descriptions");
+constexpr int kSegRingBytes = kSegWarps * kRing * int(sizeof(SegUnit));
+constexpr int kSegT4Bytes = 4 * 256 * 4;                // T_0..T_3, one copy (the chain combine)
+constexpr int kSegSmemTotal = kSegRingBytes + kSegT4Bytes + kSegSmemBytes;
+static_assert(kSegSmemTotal <= 227 * 1024, "segment kernels exceed the shared memory of a CTA");
+
+// (block, span) units of a gather or scatter: unit u is span u % nspans of
+// packed block u / nspans. A warp's cursor moves by the grid's warp count,
+// tracked as (block, span) steps so that no unit costs a 64-bit division.
+template <int MODE>
+struct SpanUnits {
+    SpanArgs a;
+    int64_t i, di;       // packed block of the cursor, and its step
+    int s, ds;           // span of the cursor, and its step
+    __device__ SpanUnits(const SpanArgs& args, int64_t u0, int64_t du)
+        : a(args), i(u0 / args.nspans), di(du / args.nspans), s(int(u0 % args.nspans)), ds(int(du % args.nspans)) {}
+    __device__ __forceinline__ void step() {
+        i += di;
+        s += ds;
+        if (s >= a.nspans) {
+            s -= a.nspans;
+            ++i;
+        }
+    }
+    // Describes the next valid unit at or after the cursor in `out` and moves
+    // the cursor past it; flags and skips bad ones.
+    __device__ __forceinline__ bool next(SegUnit& out, int lane) {
+        for (; i < a.n; step()) {
+            const kvsnap_span& sp = a.spans[s];
+            const int64_t block = a.blocks[i];
+            if (block < 0 || block >= sp.nblocks) {
+                if (lane == 0) flag(a.status, KVSNAP_DP_BAD_BLOCK);
+                continue;
+            }
+            const int64_t bytes = sp.bytes;
+            const int64_t packed = a.packed[i] + sp.offset;
+            const int64_t cache = sp.base + block * sp.pitch;
+            if ((packed | cache | bytes) & 15) {
+                if (lane == 0) flag(a.status, KVSNAP_DP_MISALIGNED);
+                continue;
+            }
+            out.src = reinterpret_cast<const char*>(MODE == kGather ? cache : packed);
+            out.dst = reinterpret_cast<char*>(MODE == kGather ? packed : cache);
+            out.seg = seg_bytes(bytes);
+            out.pad = 32 * out.seg - bytes;
+            out.block = i;
+            out.shift = sp.crc_shift;
+            out.steps = int32_t(out.seg / kSegLine);
+            out.span = s;
+            step();
+            return true;
+        }
+        return false;
+    }
+};
+
+// 64 KiB pieces of packed blocks in device memory (the CRC of whole blocks).
+constexpr int64_t kSegPiece = 64 << 10;
+struct PieceUnits {
+    const int64_t* addrs;
+    int64_t n, block_bytes, pieces;
+    uint32_t* status;
+    int64_t u, du;
+    __device__ __forceinline__ bool next(SegUnit& out, int lane) {
+        for (; u < n * pieces; u += du) {
+            const int64_t i = u / pieces, p = u - i * pieces;
+            const int64_t at = p * kSegPiece, len = min(kSegPiece, block_bytes - at);
+            const int64_t base = addrs[i] + at;
+            if ((base | len) & 15) {
+                if (lane == 0) flag(status, KVSNAP_DP_MISALIGNED);
+                continue;
+            }
+            out.src = reinterpret_cast<const char*>(base);
+            out.dst = nullptr;
+            out.seg = seg_bytes(len);
+            out.pad = 32 * out.seg - len;
+            out.block = i;
+            out.shift = dev_xpow8n(uint64_t(block_bytes - at - len));
+            out.steps = int32_t(out.seg / kSegLine);
+            out.span = 0;
+            u += du;
+            return true;
+        }
+        return false;
+    }
+};
+
+// One warp's stream: every unit's bytes moved (STORE) and CRC'd (CRC; the
+// unit's share XORed into crc_out[block]), the last block's tail masked (TAIL).
+// Lane l issues, in every step, the 16-byte slot (l & 7) of lines 4j + (l >> 3),
+// j = 0..7; `buf` is the warp's line buffer, `ring` its unit descriptions.
+template <bool STORE, bool CRC, bool TAIL, class Units>
+__device__ __forceinline__ void warp_stream(Units units, const RepTables& tl, const uint32_t* t4, uint4* buf,
+                                            SegUnit* ring, int lane, uint32_t* crc_out, const kvsnap_span* spans,
+                                            int valid) {
     const int row = lane >> 3, slot = lane & 7;
-    const int64_t first = row * seg + 16 * slot - (32 * seg - len);   // + 4*j*seg + t*kSegLine
-    const TailMask mask = TAIL ? TailMask(sp, valid) : TailMask{};
+    SegUnit L;                                   // the unit the load side is in
+    if (!units.next(L, lane)) return;
+    int lk = 0, lt = 0;                          // its ring entry and next step
+    bool loading = true;
+    if (lane == 0) ring[0] = L;
+    __syncwarp();
+    SegUnit P = L;                               // the unit being stored and folded
+    int pk = 0, pt = 0;
     Chains r;
-    // Step t: store and buffer the vectors in v, refill v with step t + kSegDepth
-    // (kSegDepth steps of loads stay in flight), then fold the lane's line.
-    auto step = [&](uint4(&v)[8], int64_t t) {
-        const int64_t here = first + t * kSegLine;
+    LaneShift place;
+
+    // Issue the load side's next step into v and move the load side on.
+    auto load_next = [&](uint4(&v)[8]) -> bool {
+        if (!loading) return false;
+        const int64_t first = row * L.seg + 16 * slot - L.pad + int64_t(lt) * kSegLine;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) v[j] = seg_load(L.src, first + 4 * j * L.seg);
+        if (++lt == L.steps) {
+            lt = 0;
+            loading = units.next(L, lane);
+            if (loading) {
+                lk = (lk + 1) & (kRing - 1);
+                if (lane == 0) ring[lk] = L;
+            }
+        }
+        return true;
+    };
+    // Store the step in v and write it to the line buffer.
+    auto emit = [&](uint4(&v)[8]) {
+        const int64_t first = row * P.seg + 16 * slot - P.pad + int64_t(pt) * kSegLine;
+        TailMask mask;
+        kvsnap_span sp{};
+        if (TAIL) {
+            sp = spans[P.span];
+            mask = TailMask(sp, valid);
+        }
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
-            const int64_t at = here + 4 * j * seg;
+            const int64_t at = first + 4 * j * P.seg;   // the front padding can cover whole segments
             if (TAIL && at >= 0) v[j] = mask.apply(v[j], at, sp, valid);
-            if (STORE && at >= 0) seg_store(dst, at, v[j]);
+            if (STORE && at >= 0) seg_store(P.dst, at, v[j]);
             if (CRC) {
                 const int line = 4 * j + row;
                 buf[line * 8 + (slot ^ (line & 7))] = v[j];
             }
         }
-        if (t + kSegDepth < steps) {
-            // The front padding can cover whole segments, so every step checks.
-#pragma unroll
-            for (int j = 0; j < 8; ++j) v[j] = seg_load(src, here + kSegDepth * kSegLine + 4 * j * seg);
-        }
-        if (CRC) {
-            __syncwarp();
-            const uint4* mine = buf + lane * 8;
-            uint4 w = mine[slot];
-#pragma unroll 1
-            for (int k = 1; k < 8; ++k) {   // one slot read ahead of the fold
-                const uint4 now = w;
-                w = mine[k ^ slot];
-                r.fold(tl, now);
-            }
-            r.fold(tl, w);
-            __syncwarp();
-        }
     };
-    uint4 v[kSegDepth][8];
-#pragma unroll
-    for (int j = 0; j < 8; ++j) v[0][j] = seg_load(src, first + 4 * j * seg);
-#pragma unroll
-    for (int d = 1; d < kSegDepth; ++d) {
-        if (d < steps) {
-#pragma unroll
-            for (int j = 0; j < 8; ++j) v[d][j] = seg_load(src, first + d * kSegLine + 4 * j * seg);
+    // Fold the lane's line of the step just buffered.
+    auto fold = [&]() {
+        __syncwarp();
+        const uint4* mine = buf + lane * 8;
+        uint4 w = mine[slot];
+#pragma unroll 1
+        for (int k = 1; k < 8; ++k) {   // one slot read ahead of the fold
+            const uint4 now = w;
+            w = mine[k ^ slot];
+            r.fold(tl, now);
         }
-    }
-    for (int64_t t = 0; t < steps; t += kSegDepth) {
-        step(v[0], t);
-#pragma unroll
-        for (int d = 1; d < kSegDepth; ++d)
-            if (t + d < steps) step(v[d], t + d);
-    }
-    return r;
-}
+        r.fold(tl, w);
+        __syncwarp();
+    };
+    // After a step: at the end of a unit, its CRC share goes out and the next unit comes in.
+    auto advance = [&]() {
+        if (++pt < P.steps) return;
+        if (CRC) {
+            const uint32_t x = gf_mulmod(warp_xor(place.place(r, t4, P.seg, lane)), P.shift);
+            if (lane == 0) atomicXor(&crc_out[P.block], x);
+            r = Chains{};
+        }
+        pt = 0;
+        pk = (pk + 1) & (kRing - 1);
+        __syncwarp();
+        P = ring[pk];                            // stale once the stream has ended; then unused
+        __syncwarp();
+    };
 
-// Places a lane's chains in its unit: sum_k c_k * x^(32*(3-k)) * x^(8*S*(31-lane))
-// = raw(segment) * x^96 moved to the segment's place. The four factors are
-// recomputed only when the segment size S changes.
-struct LaneShift {
-    int64_t seg = -1;
-    uint32_t k[4] = {0, 0, 0, 0};
-    __device__ __forceinline__ uint32_t place(const Chains& r, int64_t s, int lane) {
-        if (s != seg) {
-            seg = s;
-            k[3] = dev_xpow8n(uint64_t(s) * uint64_t(31 - lane));
-            k[2] = gf_mulmod(k[3], g_pow8.p[2]);             // * x^32
-            k[1] = gf_mulmod(k[3], g_pow8.p[3]);             // * x^64
-            k[0] = gf_mulmod(k[2], g_pow8.p[3]);             // * x^96
+    uint4 v[kSegDepth][8];
+    int pending = 0;
+#pragma unroll
+    for (int d = 0; d < kSegDepth; ++d)
+        if (load_next(v[d])) ++pending;
+    while (pending > 0) {
+#pragma unroll
+        for (int d = 0; d < kSegDepth; ++d) {
+            if (pending > 0) {                   // slot d holds the oldest step in flight
+                emit(v[d]);
+                --pending;
+                if (load_next(v[d])) ++pending;  // refill before folding, so the loads overlap it
+                if (CRC) fold();
+                advance();
+            }
         }
-        return gf_mulmod(r.c[0], k[0]) ^ gf_mulmod(r.c[1], k[1]) ^ gf_mulmod(r.c[2], k[2]) ^
-               gf_mulmod(r.c[3], k[3]);
     }
-};
+}
 
 // TAIL: every unit belongs to the save's last block, whose token slots from
 // `valid` on are written as zeros. The launcher gives that block a launch of
 // its own, so the common kernel carries none of the masking code.
+// Shared memory: unit rings, then (with a CRC) the tables and line buffers.
 template <int MODE, bool TAIL>
 __global__ void __launch_bounds__(kSegThreads, 1) span_kernel_hbm(SpanArgs a) {
     extern __shared__ uint4 smem[];
-    uint32_t* tb = reinterpret_cast<uint32_t*>(smem);
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    SegUnit* ring = reinterpret_cast<SegUnit*>(smem) + warp * kRing;
+    uint32_t* t4 = reinterpret_cast<uint32_t*>(smem + kSegRingBytes / 16);
+    uint32_t* tb = t4 + kSegT4Bytes / 4;
+    uint4* buf = smem + (kSegRingBytes + kSegT4Bytes) / 16 + kRepWords / 4 + warp * (kSegStep / 16);
     const bool crc = a.crc != nullptr;
-    if (crc) load_rep_tables(tb);
+    if (crc) load_seg_tables(tb, t4);
     __syncthreads();
     if (MODE == kScatter && a.gate && *a.gate) return;
-    const int lane = threadIdx.x & 31;
     const RepTables tl{reinterpret_cast<const char*>(tb), 4u * lane};
-    uint4* buf = smem + kRepWords / 4 + (threadIdx.x >> 5) * (kSegStep / 16);
-    LaneShift lane_shift;
-    const int64_t warps = (int64_t)gridDim.x * kSegWarps;
-    const int64_t units = a.n * a.nspans;
-    for (int64_t u = (int64_t)blockIdx.x * kSegWarps + (threadIdx.x >> 5); u < units; u += warps) {
-        const int64_t i = u / a.nspans;
-        const kvsnap_span sp = a.spans[u - i * a.nspans];
-        const int64_t block = a.blocks[i];
-        if (block < 0 || block >= sp.nblocks) {
-            if (lane == 0) flag(a.status, KVSNAP_DP_BAD_BLOCK);
-            continue;
-        }
-        const int64_t packed = a.packed[i] + sp.offset;
-        const int64_t cache = sp.base + block * sp.pitch;
-        if ((packed | cache | sp.bytes) & 15) {
-            if (lane == 0) flag(a.status, KVSNAP_DP_MISALIGNED);
-            continue;
-        }
-        const char* src = reinterpret_cast<const char*>(MODE == kGather ? cache : packed);
-        char* dst = reinterpret_cast<char*>(MODE == kGather ? packed : cache);
-        if (crc) {
-            const Chains c = warp_unit_seg<true, true, TAIL>(tl, buf, src, dst, sp.bytes, lane, sp, a.valid);
-            const uint32_t r = gf_mulmod(warp_xor(lane_shift.place(c, seg_bytes(sp.bytes), lane)), sp.crc_shift);
-            if (lane == 0) atomicXor(&a.crc[i], r);
-        } else {
-            warp_unit_seg<true, false, TAIL>(tl, buf, src, dst, sp.bytes, lane, sp, a.valid);
-        }
-    }
+    const int64_t u0 = (int64_t)blockIdx.x * kSegWarps + warp, du = (int64_t)gridDim.x * kSegWarps;
+    const SpanUnits<MODE> units(a, u0, du);
+    if (crc)
+        warp_stream<true, true, TAIL>(units, tl, t4, buf, ring, lane, a.crc, a.spans, a.valid);
+    else
+        warp_stream<true, false, TAIL>(units, tl, t4, buf, ring, lane, nullptr, a.spans, a.valid);
 }
 
 __global__ void __launch_bounds__(kSegThreads, 1) crc_kernel_hbm(const int64_t* addrs, int64_t n,
                                                                  int64_t block_bytes, uint32_t* crc,
                                                                  uint32_t* status) {
     extern __shared__ uint4 smem[];
-    uint32_t* tb = reinterpret_cast<uint32_t*>(smem);
-    load_rep_tables(tb);
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    SegUnit* ring = reinterpret_cast<SegUnit*>(smem) + warp * kRing;
+    uint32_t* t4 = reinterpret_cast<uint32_t*>(smem + kSegRingBytes / 16);
+    uint32_t* tb = t4 + kSegT4Bytes / 4;
+    uint4* buf = smem + (kSegRingBytes + kSegT4Bytes) / 16 + kRepWords / 4 + warp * (kSegStep / 16);
+    load_seg_tables(tb, t4);
     __syncthreads();
-    const int lane = threadIdx.x & 31;
     const RepTables tl{reinterpret_cast<const char*>(tb), 4u * lane};
-    uint4* buf = smem + kRepWords / 4 + (threadIdx.x >> 5) * (kSegStep / 16);
-    LaneShift lane_shift;
-    constexpr int64_t piece = 64 << 10;
-    const int64_t pieces = (block_bytes + piece - 1) / piece;
-    const int64_t warps = (int64_t)gridDim.x * kSegWarps;
-    kvsnap_span none{};
-    for (int64_t u = (int64_t)blockIdx.x * kSegWarps + (threadIdx.x >> 5); u < n * pieces; u += warps) {
-        const int64_t i = u / pieces, p = u - i * pieces;
-        const int64_t at = p * piece, len = min(piece, block_bytes - at);
-        const int64_t base = addrs[i] + at;
-        if ((base | len) & 15) {
-            if (lane == 0) flag(status, KVSNAP_DP_MISALIGNED);
-            continue;
-        }
-        const Chains c = warp_unit_seg<false, true, false>(tl, buf, reinterpret_cast<const char*>(base), nullptr,
-                                                           len, lane, none, 0);
-        const uint32_t r = gf_mulmod(warp_xor(lane_shift.place(c, seg_bytes(len), lane)),
-                                     dev_xpow8n(uint64_t(block_bytes - at - len)));
-        if (lane == 0) atomicXor(&crc[i], r);
-    }
+    const int64_t u0 = (int64_t)blockIdx.x * kSegWarps + warp, du = (int64_t)gridDim.x * kSegWarps;
+    const PieceUnits units{addrs, n, block_bytes, (block_bytes + kSegPiece - 1) / kSegPiece, status, u0, du};
+    warp_stream<false, true, false>(units, tl, t4, buf, ring, lane, crc, nullptr, 0);
 }
 
 // CRC32C of whole packed blocks, in pieces of kPiece bytes per warp.
@@ -1025,21 +1152,21 @@ int launch_spans(const kvsnap_span* spans, int nspans, uint64_t block_bytes, con
                 const int64_t want = (blocks_of_work * nspans + kSegWarps - 1) / kSegWarps;
                 return ctas > 0 ? ctas : int(want < sms ? want : sms);
             };
-            const int smem = crc ? kSegSmemBytes : 0;
+            const int smem = crc ? kSegSmemTotal : kSegRingBytes;
             int64_t body = n;
             if constexpr (MODE == kGather) {
                 if (valid > 0) {   // the last block, masked, in a launch of its own
                     body = n - 1;
                     SpanArgs last{spans, nspans, blocks + body, packed + body, 1, valid, crc ? crc + body : nullptr,
                                   gate, status};
-                    configure_once(reinterpret_cast<const void*>(span_kernel_hbm<MODE, true>), kSegSmemBytes);
+                    configure_once(reinterpret_cast<const void*>(span_kernel_hbm<MODE, true>), kSegSmemTotal);
                     span_kernel_hbm<MODE, true><<<grid_of(1), kSegThreads, smem, s>>>(last);
                     check(cudaGetLastError());
                 }
             }
             if (body > 0) {
                 a.n = body;
-                configure_once(reinterpret_cast<const void*>(span_kernel_hbm<MODE, false>), kSegSmemBytes);
+                configure_once(reinterpret_cast<const void*>(span_kernel_hbm<MODE, false>), kSegSmemTotal);
                 span_kernel_hbm<MODE, false><<<grid_of(body), kSegThreads, smem, s>>>(a);
                 check(cudaGetLastError());
             }
@@ -1089,10 +1216,10 @@ extern "C" int kvsnap_dp_crc32c(const int64_t* addrs, int64_t n, uint64_t block_
         cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
         check(cudaMemsetAsync(crc_out, 0, sizeof(uint32_t) * size_t(n), s));
         if (hbm && vec == 16) {
-            configure_once(reinterpret_cast<const void*>(crc_kernel_hbm), kSegSmemBytes);
+            configure_once(reinterpret_cast<const void*>(crc_kernel_hbm), kSegSmemTotal);
             const int64_t want = (n * ((int64_t(block_bytes) + kPiece - 1) / kPiece) + kSegWarps - 1) / kSegWarps;
             const int grid = ctas > 0 ? ctas : int(want < sms ? want : sms);
-            crc_kernel_hbm<<<grid, kSegThreads, kSegSmemBytes, s>>>(addrs, n, int64_t(block_bytes), crc_out, status);
+            crc_kernel_hbm<<<grid, kSegThreads, kSegSmemTotal, s>>>(addrs, n, int64_t(block_bytes), crc_out, status);
             check(cudaGetLastError());
             finish(crc_out, expect, n, block_bytes, status, s, kSegUnscale);
             return;
