@@ -77,6 +77,17 @@ int kvsnap_pool_copy_on(void* pool, uint64_t id, size_t host_offset, void* devic
    event on `stream` (0: the pool's copy stream) now, so wait/ready/release
    also fence kernels queued there that read or write the allocation in place. */
 int kvsnap_pool_mark(void* pool, uint64_t id, uintptr_t stream);
+/* Extension (no reference counterpart): n copies in one call, entry k moving
+   sizes[k] bytes between allocation ids[k] at host_offsets[k] and device
+   address device_ptrs[k], queued in order on `stream` (0: the pool's copy
+   stream) with no producer fence. Every entry is checked before any is
+   queued; each allocation's completion event is recorded after the last copy.
+   Replaces n kvsnap_pool_copy_on calls (one per block of a host-tier
+   snapshot, reference volatile.py:281-307) with one. */
+int kvsnap_pool_copy_many(void* pool, int64_t n, const uint64_t* ids, const uint64_t* host_offsets,
+                          const uint64_t* device_ptrs, const uint64_t* sizes, int to_host, uintptr_t stream);
+/* Extension: kvsnap_pool_wait for each of n allocations, in one call. */
+int kvsnap_pool_wait_many(void* pool, int64_t n, const uint64_t* ids);
 
 /* ---- 2. data-plane kernels --------------------------------------------------- */
 

@@ -50,6 +50,8 @@ POOL_API = {
 POOL_EXTRA = {
     "kvsnap_pool_mark": ([_P, C.c_uint64, _SZ], C.c_int),
     "kvsnap_pool_copy_on": ([_P, C.c_uint64, _SZ, _P, _SZ, C.c_int, _SZ], C.c_int),
+    "kvsnap_pool_copy_many": ([_P, C.c_int64, _P, _P, _P, _P, C.c_int, _SZ], C.c_int),
+    "kvsnap_pool_wait_many": ([_P, C.c_int64, _P], C.c_int),
 }
 
 DP_API = {

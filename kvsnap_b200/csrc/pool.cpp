@@ -15,6 +15,7 @@
 
 #include <cstdint>
 #include <map>
+#include <vector>
 #include <memory>
 #include <mutex>
 #include <stdexcept>
@@ -282,6 +283,58 @@ extern "C" int kvsnap_pool_mark(void* pool, uint64_t id, uintptr_t stream) {
         s.foreign = on != a->stream;
         cuda(cudaEventRecord(s.done, on));
         s.done_valid = true;
+    });
+}
+
+extern "C" int kvsnap_pool_copy_many(void* pool, int64_t n, const uint64_t* ids, const uint64_t* host_offsets,
+                                     const uint64_t* device_ptrs, const uint64_t* sizes, int to_host,
+                                     uintptr_t stream) {
+    return guarded([&] {
+        if (n < 0 || (n > 0 && (!ids || !host_offsets || !device_ptrs || !sizes)))
+            throw Failure("invalid copy list");
+        Arena* a = live(pool);
+        std::lock_guard<std::mutex> lock(a->mutex);
+        // Every entry is checked before anything is queued.
+        std::vector<Slot*> slots(static_cast<size_t>(n));
+        for (int64_t k = 0; k < n; ++k) {
+            Slot& s = a->slot(ids[k]);
+            if (host_offsets[k] > s.size || sizes[k] > s.size - host_offsets[k])
+                throw Failure("copy outside pinned allocation");
+            slots[static_cast<size_t>(k)] = &s;
+        }
+        if (n == 0) return;
+        cuda(cudaSetDevice(a->device));
+        cudaStream_t on = stream ? reinterpret_cast<cudaStream_t>(stream) : a->stream;
+        for (Slot* s : slots) {
+            a->begin(*s);
+            s->foreign = on != a->stream;
+        }
+        for (int64_t k = 0; k < n; ++k) {
+            const Slot& s = *slots[static_cast<size_t>(k)];
+            char* host = a->base + s.offset + host_offsets[k];
+            void* device = reinterpret_cast<void*>(static_cast<uintptr_t>(device_ptrs[k]));
+            if (to_host)
+                cuda(cudaMemcpyAsync(host, device, sizes[k], cudaMemcpyDeviceToHost, on));
+            else
+                cuda(cudaMemcpyAsync(device, host, sizes[k], cudaMemcpyHostToDevice, on));
+        }
+        for (Slot* s : slots) {
+            if (s->done_valid) continue;      // listed twice: recorded already, after every copy
+            cuda(cudaEventRecord(s->done, on));
+            s->done_valid = true;
+        }
+    });
+}
+
+extern "C" int kvsnap_pool_wait_many(void* pool, int64_t n, const uint64_t* ids) {
+    return guarded([&] {
+        if (n < 0 || (n > 0 && !ids)) throw Failure("invalid allocation list");
+        Arena* a = live(pool);
+        std::lock_guard<std::mutex> lock(a->mutex);
+        for (int64_t k = 0; k < n; ++k) a->slot(ids[k]);
+        if (n == 0) return;
+        cuda(cudaSetDevice(a->device));
+        for (int64_t k = 0; k < n; ++k) a->settle(a->slot(ids[k]));
     });
 }
 

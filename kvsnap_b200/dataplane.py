@@ -193,6 +193,39 @@ class CudaPool:
                         allocation._tensor_references.clear()
                 self._allocations.clear()
 
+    def copy_many(self, entries, *, to_host, stream=0):
+        """Queue copies ``(allocation, offset, device_ptr, size)`` in order on ``stream`` in one native call.
+
+        ``stream`` 0 is the pool's copy stream; another stream orders its own
+        producers. Every entry is checked before any copy is queued; each
+        allocation's completion event covers all of them (kvsnap_pool_copy_many).
+        """
+        with self.operation():
+            n = len(entries)
+            if n == 0:
+                return
+            for allocation, offset, device_ptr, size in entries:
+                if allocation.pool is not self:
+                    raise ValueError("allocation belongs to another pool")
+                allocation._open()
+                if min(offset, device_ptr, size, stream) < 0:
+                    raise ValueError("negative copy argument")
+            arrays = [(C.c_uint64 * n)(*column) for column in
+                      zip(*((a.ident, offset, ptr, size) for a, offset, ptr, size in entries))]
+            self.check(self.lib.kvsnap_pool_copy_many(self.handle, n, *arrays, int(bool(to_host)), stream))
+
+    def wait_many(self, allocations):
+        """``wait`` for each allocation, in one native call (kvsnap_pool_wait_many)."""
+        with self.operation():
+            allocations = list(allocations)
+            for allocation in allocations:
+                if allocation.pool is not self:
+                    raise ValueError("allocation belongs to another pool")
+                allocation._open()
+            if allocations:
+                ids = (C.c_uint64 * len(allocations))(*(a.ident for a in allocations))
+                self.check(self.lib.kvsnap_pool_wait_many(self.handle, len(allocations), ids))
+
     def stream_handle(self) -> int:
         """The copy stream's handle (borrowed; valid while the pool is open)."""
         with self.operation():
@@ -641,10 +674,9 @@ class TorchBlockDataPlane:
                         stage = torch.empty(n * size, dtype=torch.uint8, device=device)
                         stage.record_stream(copies)
                         base = stage.data_ptr()
-                        for i, j in self._runs(sources, 0, n, size):
-                            allocation, offset = sources[i]
-                            allocation.copy_on(base + i * size, (j - i) * size, offset, to_host=False,
-                                               stream=copies.cuda_stream)
+                        self.pool.copy_many([(sources[i][0], sources[i][1], base + i * size, (j - i) * size)
+                                             for i, j in self._runs(sources, 0, n, size)],
+                                            to_host=False, stream=copies.cuda_stream)
                         landed = torch.cuda.Event()
                         landed.record(copies)
                         kernels.wait_event(landed)
@@ -700,10 +732,9 @@ class TorchBlockDataPlane:
             slot = chunk % 2
             if chunk >= 2:
                 copies.wait_event(scattered[chunk - 2])      # the slot's previous chunk is in the cache
-            for i, j in self._runs(sources, first, last, size):
-                allocation, offset = sources[i]
-                allocation.copy_on(base + (slot * depth + i - first) * size, (j - i) * size, offset, to_host=False,
-                                   stream=copies.cuda_stream)
+            self.pool.copy_many([(sources[i][0], sources[i][1], base + (slot * depth + i - first) * size,
+                                  (j - i) * size) for i, j in self._runs(sources, first, last, size)],
+                                to_host=False, stream=copies.cuda_stream)
             landed = torch.cuda.Event()
             landed.record(copies)
             kernels.wait_event(landed)
@@ -806,19 +837,20 @@ class TorchBlockDataPlane:
                     if digests is not None:
                         side = self._sha_stream()
                         digest = self._sha256_after(stage, table[n:], n, stream, side)
+                    entries = []
                     for first in range(0, n, per_chunk):
                         for i, j in self._runs(targets, first, min(n, first + per_chunk), size):
                             allocation, offset = targets[i]
-                            allocation.copy(stage.data_ptr() + i * size, (j - i) * size, offset, to_host=True)
-                            copies += 1
+                            entries.append((allocation, offset, stage.data_ptr() + i * size, (j - i) * size))
+                    self.pool.copy_many(entries, to_host=True)
+                    copies += len(entries)
                 done = torch.cuda.Event()
                 done.record()
             except BaseException:
                 stream.synchronize()
                 raise
         done.synchronize()
-        for allocation in {id(a): a for a, _ in targets}.values():
-            allocation.wait()
+        self.pool.wait_many({id(a): a for a, _ in targets}.values())
         self._status_error(status)
         if digests is not None:
             finished = torch.cuda.Event()
@@ -876,9 +908,8 @@ class TorchBlockDataPlane:
                     raise ValueError("digest source outside its allocation")
             with torch.cuda.stream(stream):
                 stage = torch.empty(n * size, dtype=torch.uint8, device=device)
-                for i, j in self._runs(sources, 0, n, size):
-                    allocation, offset = sources[i]
-                    allocation.copy(stage.data_ptr() + i * size, (j - i) * size, offset, to_host=False)
+                self.pool.copy_many([(sources[i][0], sources[i][1], stage.data_ptr() + i * size, (j - i) * size)
+                                     for i, j in self._runs(sources, 0, n, size)], to_host=False)
                 addresses = torch.tensor([stage.data_ptr() + i * size for i in range(n)],
                                          dtype=torch.int64).pin_memory().to(device, non_blocking=True)
                 crc = torch.empty(n, dtype=torch.int32, device=device)

@@ -261,3 +261,60 @@ def test_copy_on_another_stream_is_fenced_by_its_own_event(lib):
         assert lib.fake_cuda_pending() == 0
     finally:
         lib.kvsnap_pool_destroy(pool)
+
+
+def _arrays(*columns):
+    return [(C.c_uint64 * len(col))(*col) for col in columns]
+
+
+def test_copy_many_checks_every_entry_before_queueing_any(lib):
+    pool = lib.kvsnap_pool_create(64, 0)
+    try:
+        _, a, pa = reserve(lib, pool, 16)
+        _, b, pb = reserve(lib, pool, 16)
+        C.memmove(pa, b"A" * 16, 16)
+        C.memmove(pb, b"B" * 16, 16)
+        device = C.create_string_buffer(48)
+        dev = C.addressof(device)
+        # The third entry runs past its allocation: nothing at all is queued.
+        ids, offs, ptrs, sizes = _arrays([a, b, b], [0, 0, 8], [dev, dev + 16, dev + 32], [16, 16, 9])
+        assert lib.kvsnap_pool_copy_many(pool, 3, ids, offs, ptrs, sizes, 0, 0) == -1
+        assert "outside" in error(lib) and lib.fake_cuda_pending() == 0
+        ids, offs, ptrs, sizes = _arrays([a, 99], [0, 0], [dev, dev], [16, 16])
+        assert lib.kvsnap_pool_copy_many(pool, 2, ids, offs, ptrs, sizes, 0, 0) == -1
+        assert "unknown pinned allocation" in error(lib) and lib.fake_cuda_pending() == 0
+        # A valid list: copies in order on the given stream, each allocation fenced by its event.
+        ids, offs, ptrs, sizes = _arrays([a, b, b], [0, 0, 8], [dev, dev + 16, dev + 32], [16, 8, 8])
+        assert lib.kvsnap_pool_copy_many(pool, 3, ids, offs, ptrs, sizes, 0, 555) == 0
+        assert lib.fake_cuda_last_stream() == 555 and lib.fake_cuda_pending() == 3
+        assert lib.kvsnap_pool_ready(pool, a) == 0 and lib.kvsnap_pool_ready(pool, b) == 0
+        waits = _arrays([a, b])[0]
+        assert lib.kvsnap_pool_wait_many(pool, 2, waits) == 0
+        assert device.raw[:40] == b"A" * 16 + b"B" * 8 + b"\0" * 8 + b"B" * 8
+        assert lib.kvsnap_pool_copy_many(pool, 0, None, None, None, None, 0, 0) == 0
+        assert lib.kvsnap_pool_copy_many(pool, -1, None, None, None, None, 0, 0) == -1
+    finally:
+        lib.kvsnap_pool_destroy(pool)
+
+
+def test_copy_many_failures_fall_back_to_draining(lib):
+    pool = lib.kvsnap_pool_create(64, 0)
+    try:
+        _, a, pa = reserve(lib, pool, 16)
+        _, b, pb = reserve(lib, pool, 16)
+        device = C.create_string_buffer(32)
+        dev = C.addressof(device)
+        ids, offs, ptrs, sizes = _arrays([a, b], [0, 0], [dev, dev + 16], [16, 16])
+        lib.fake_cuda_fail_next(b"cudaEventRecord")            # the first allocation's event is lost
+        assert lib.kvsnap_pool_copy_many(pool, 2, ids, offs, ptrs, sizes, 1, 0) == -1
+        assert lib.kvsnap_pool_release(pool, a) == 0            # no event: release drains the pool stream
+        assert lib.fake_cuda_pending() == 0
+        lib.fake_cuda_fail_next(b"cudaMemcpyAsync")            # the first copy is refused
+        ids, offs, ptrs, sizes = _arrays([b], [0], [dev], [16])
+        assert lib.kvsnap_pool_copy_many(pool, 1, ids, offs, ptrs, sizes, 1, 777) == -1
+        assert lib.kvsnap_pool_ready(pool, b) in (0, 1)
+        waits = _arrays([b])[0]
+        assert lib.kvsnap_pool_wait_many(pool, 1, waits) == 0   # a foreign stream without an event: drain
+        assert lib.kvsnap_pool_wait_many(pool, 1, _arrays([12345])[0]) == -1
+    finally:
+        lib.kvsnap_pool_destroy(pool)

@@ -142,3 +142,27 @@ def test_borrowed_stream_handle(pool):
     with pool.borrow_copy_stream() as handle:
         assert handle
     assert pool.stream_handle() == handle
+
+
+def test_copy_many_and_wait_many(pool, fake_library):
+    _, lib = fake_library
+    a, b = pool.reserve(16), pool.reserve(16)
+    a.write(b"a" * 16)
+    b.write(b"b" * 16)
+    device = C.create_string_buffer(32)
+    dev = C.addressof(device)
+    pool.copy_many([(a, 0, dev, 16), (b, 4, dev + 16, 12)], to_host=False)
+    assert lib.fake_cuda_pending() == 2 and not a.ready()
+    pool.wait_many([a, b])
+    assert device.raw[:28] == b"a" * 16 + b"b" * 12
+    pool.copy_many([], to_host=True)
+    with pytest.raises(RuntimeError, match="outside"):
+        pool.copy_many([(a, 0, dev, 16), (b, 8, dev, 16)], to_host=True)
+    assert lib.fake_cuda_pending() == 0
+    with pytest.raises(ValueError):
+        pool.copy_many([(a, -1, dev, 4)], to_host=True)
+    a.close()
+    with pytest.raises(RuntimeError, match="closed"):
+        pool.copy_many([(a, 0, dev, 4)], to_host=True)
+    with pytest.raises(RuntimeError, match="closed"):
+        pool.wait_many([a])
