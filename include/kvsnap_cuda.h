@@ -82,6 +82,8 @@ int kvsnap_pool_mark(void* pool, uint64_t id, uintptr_t stream);
    address device_ptrs[k], queued in order on `stream` (0: the pool's copy
    stream) with no producer fence. Every entry is checked before any is
    queued; each allocation's completion event is recorded after the last copy.
+   Consecutive entries whose host and device ranges both continue the previous
+   one's move in one copy.
    Replaces n kvsnap_pool_copy_on calls (one per block of a host-tier
    snapshot, reference volatile.py:281-307) with one. */
 int kvsnap_pool_copy_many(void* pool, int64_t n, const uint64_t* ids, const uint64_t* host_offsets,

@@ -286,7 +286,8 @@ def test_copy_many_checks_every_entry_before_queueing_any(lib):
         # A valid list: copies in order on the given stream, each allocation fenced by its event.
         ids, offs, ptrs, sizes = _arrays([a, b, b], [0, 0, 8], [dev, dev + 16, dev + 32], [16, 8, 8])
         assert lib.kvsnap_pool_copy_many(pool, 3, ids, offs, ptrs, sizes, 0, 555) == 0
-        assert lib.fake_cuda_last_stream() == 555 and lib.fake_cuda_pending() == 3
+        # The first two entries continue each other on both sides and move as one copy.
+        assert lib.fake_cuda_last_stream() == 555 and lib.fake_cuda_pending() == 2
         assert lib.kvsnap_pool_ready(pool, a) == 0 and lib.kvsnap_pool_ready(pool, b) == 0
         waits = _arrays([a, b])[0]
         assert lib.kvsnap_pool_wait_many(pool, 2, waits) == 0
@@ -316,5 +317,29 @@ def test_copy_many_failures_fall_back_to_draining(lib):
         waits = _arrays([b])[0]
         assert lib.kvsnap_pool_wait_many(pool, 1, waits) == 0   # a foreign stream without an event: drain
         assert lib.kvsnap_pool_wait_many(pool, 1, _arrays([12345])[0]) == -1
+    finally:
+        lib.kvsnap_pool_destroy(pool)
+
+
+def test_copy_many_merges_entries_adjacent_on_both_sides(lib):
+    pool = lib.kvsnap_pool_create(96, 0)
+    try:
+        blocks = [reserve(lib, pool, 16) for _ in range(4)]      # reserved in a row: adjacent in the arena
+        for k, (_, _, ptr) in enumerate(blocks):
+            C.memmove(ptr, bytes([65 + k]) * 16, 16)
+        device = C.create_string_buffer(80)
+        dev = C.addressof(device)
+        ids = [b[1] for b in blocks]
+        # Device side adjacent for blocks 0-1 and 2-3, a 16-byte gap between them: two copies.
+        arrays = _arrays(ids, [0, 0, 0, 0], [dev, dev + 16, dev + 48, dev + 64], [16] * 4)
+        assert lib.kvsnap_pool_copy_many(pool, 4, *arrays, 0, 0) == 0
+        assert lib.fake_cuda_pending() == 2
+        assert lib.kvsnap_pool_wait_many(pool, 4, _arrays(ids)[0]) == 0
+        assert device.raw == b"A" * 16 + b"B" * 16 + b"\0" * 16 + b"C" * 16 + b"D" * 16
+        # Host side out of order: nothing merges.
+        arrays = _arrays([ids[1], ids[0]], [0, 0], [dev, dev + 16], [16, 16])
+        assert lib.kvsnap_pool_copy_many(pool, 2, *arrays, 1, 0) == 0
+        assert lib.fake_cuda_pending() == 2
+        assert lib.kvsnap_pool_wait_many(pool, 2, _arrays(ids[:2])[0]) == 0
     finally:
         lib.kvsnap_pool_destroy(pool)
