@@ -68,6 +68,8 @@ def parse():
                         "8k and 32k-token snapshots from one pinned staging buffer with seeded corruption; "
                         "reshard: TP regroup over NVLink; rotation: config 4; kernels: the on-device "
                         "gather, scatter and CRC kernels alone against a torch device copy")
+    p.add_argument("--blob-dir", type=str, default="",
+                   help="where the disk workload writes its blob files (default: the system temp dir)")
     p.add_argument("--quick", action="store_true",
                    help="only the device-timed steps (a short run for profiling captures)")
     return p.parse_args()
@@ -883,7 +885,8 @@ def run_disk(args, world, rank, device):
     caches = make_caches(args, device)
     rows = []
     size_guess = args.layers * 2 * BLOCK * HEADS * HEAD_DIM * 2
-    plane = TorchBlockDataPlane(caches, BLOCK, 2048 * size_guess + (256 << 20), ctas=args.ctas)
+    # Two 32k-token snapshots' worth of pinned memory: the snapshot and the blob phase's staging.
+    plane = TorchBlockDataPlane(caches, BLOCK, 2 * 2048 * size_guess + (256 << 20), ctas=args.ctas)
     plane.warm_up()
     size = plane.block_bytes
     rng = np.random.Generator(np.random.PCG64(args.seed + 33))
@@ -926,16 +929,77 @@ def run_disk(args, world, rank, device):
                 plane.load_scatter(restored, sources, expected_crc32c=crcs)
                 times.append((time.perf_counter() - t0) * 1e3)
             ms = statistics.median(times)
+            row = {"tokens": tokens, "blocks": n, "bytes": n * size, "corrupted": corrupt,
+                   "detected": detected, "detected_exactly": detected == corrupt,
+                   "cache_untouched_on_failure": before == after,
+                   "verified_restore_ms": round(ms, 3), "gbs": round(n * size / (ms / 1e3) / 1e9, 2)}
+            row.update(blob_phase(plane, sources, digests, restored, n, size, args))
             restored_digests = []      # re-save the restored blocks over the snapshot and compare ids
             plane.save_gather(restored, sources, tokens, digests=restored_digests)
-            rows.append({"tokens": tokens, "blocks": n, "bytes": n * size, "corrupted": corrupt,
-                         "detected": detected, "detected_exactly": detected == corrupt,
-                         "cache_untouched_on_failure": before == after,
-                         "restore_bit_exact": restored_digests == digests,
-                         "verified_restore_ms": round(ms, 3), "gbs": round(n * size / (ms / 1e3) / 1e9, 2)})
+            row["restore_bit_exact"] = restored_digests == digests
+            rows.append(row)
     if rank == 0:
         print(json.dumps({"workload": "disk-tier verified restore (BASELINE config 3)", "rows": rows}), flush=True)
     plane.close()
+
+
+def blob_phase(plane, sources, digests, restored, n, size, args):
+    """The same snapshot as KVSBLOB1 files: write_blobs, then restores from the files.
+
+    Timed, with the files in the page cache (nothing here drops caches):
+    * blob_write: write_blobs from the pinned snapshot ("process" durability: no fdatasync);
+    * read_restore: read_and_restore, reads overlapped with GPU copies and CRC checks;
+    * read_then_restore: the reference's order of work on the same files: every block read and
+      CRC-checked on the host (8 threads, reference store.py:676-713), then load_scatter.
+    Skipped (with the reason) when the file system lacks room for three copies of the snapshot.
+    """
+    import shutil
+    import tempfile
+    from concurrent.futures import ThreadPoolExecutor
+    from kvsnap_b200 import blobs
+    from kvsnap_b200.native_io import NativeIO, resolve_io_library
+    root = args.blob_dir or tempfile.gettempdir()
+    if shutil.disk_usage(root).free < 3 * n * size:
+        return {"blobs": f"skipped: {root} has less than {3 * n * size} bytes free"}
+    blob_dir = tempfile.mkdtemp(prefix="kvsnap-blobs-", dir=root)
+    out = {}
+    try:
+        t0 = time.perf_counter()
+        segments = blobs.write_blobs(blob_dir, sources, digests, size, durability="process")
+        write_ms = (time.perf_counter() - t0) * 1e3
+        io = NativeIO(resolve_io_library(), workers=8, queue_bytes=256 << 20)
+        pipelined, serial = [], []
+        with plane.staging(n) as staged:
+            blobs.read_and_restore(plane, blob_dir, segments, restored, staged, io=io)      # warm
+            for _ in range(3):
+                t0 = time.perf_counter()
+                blobs.read_and_restore(plane, blob_dir, segments, restored, staged, io=io)
+                pipelined.append((time.perf_counter() - t0) * 1e3)
+
+            def read_checked(i):
+                address = staged.pointer + i * size
+                blobs._read_block(io, blob_dir, segments[i], address, size)
+                if io.crc32c_at(address, size) != segments[i]["crc32c"]:
+                    raise RuntimeError("host CRC mismatch")
+
+            targets = [(staged, i * size) for i in range(n)]
+            with ThreadPoolExecutor(max_workers=8) as pool:
+                for _ in range(3):
+                    t0 = time.perf_counter()
+                    list(pool.map(read_checked, range(n)))
+                    plane.load_scatter(restored, targets)
+                    serial.append((time.perf_counter() - t0) * 1e3)
+        io.close()
+        p_ms, s_ms = statistics.median(pipelined), statistics.median(serial)
+        out = {"blob_files": len({s["blob_id"] for s in segments}),
+               "blob_write_ms": round(write_ms, 2), "blob_write_gbs": round(n * size / (write_ms / 1e3) / 1e9, 2),
+               "read_restore_ms": round(p_ms, 2), "read_restore_gbs": round(n * size / (p_ms / 1e3) / 1e9, 2),
+               "read_then_restore_ms": round(s_ms, 2),
+               "read_then_restore_gbs": round(n * size / (s_ms / 1e3) / 1e9, 2),
+               "blob_note": "page-cache reads; read_then_restore is the reference's order: host CRC, then H2D"}
+    finally:
+        shutil.rmtree(blob_dir, ignore_errors=True)
+    return out
 
 
 def run_reshard(args, world, rank, device):

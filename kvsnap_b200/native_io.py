@@ -89,6 +89,13 @@ class NativeIO:
             count = min(self.queue_bytes, size - index)
             self._transfer(fd, C.c_void_p(address + index), count, offset + index, 0)
 
+    def pwrite_from(self, fd, address, size, offset):
+        """Write straight from caller memory (e.g. pinned host memory), no Python copy."""
+        self._offset(size, offset)
+        for index in range(0, size, self.queue_bytes):
+            count = min(self.queue_bytes, size - index)
+            self._transfer(fd, C.c_void_p(address + index), count, offset + index, 1)
+
     def crc32c(self, data, crc=0):
         self._open()
         data = bytes(data)

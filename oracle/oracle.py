@@ -24,6 +24,8 @@ What it restates (reference paths are relative to the kvsnap source tree):
   (``kvsnap/store/store.py:616-629``, ``kvsnap/connector/volatile.py:141-151``).
 * Dedup: one blob per distinct content id, segments keep every block
   (``store.py:625-628``, ``volatile.py:254-279``).
+* Blob files: a 32-byte KVSBLOB1 header, then the packed block
+  (``kvsnap/store/common.py:10-11``, ``blobs.py:33-36, 95-101``).
 * TP regroup (no reference code exists; a TP-size mismatch is a miss there):
   defined by slicing the full-head KV by KV head, see ``slice_heads``.
 
@@ -35,6 +37,7 @@ from __future__ import annotations
 
 import ctypes
 import hashlib
+import struct
 from dataclasses import dataclass, field
 from pathlib import Path
 
@@ -261,6 +264,27 @@ def dedup(blocks) -> tuple:
         segments.append(dict(blob_id=key, offset=0, length=len(blocks[index]), first_block=index, nblocks=1,
                              crc32c=checksum))
     return list(unique), segments
+
+
+# ---- blob files ----------------------------------------------------------
+
+# KVSBLOB1 header: magic, version 1, payload length, payload CRC32C, 8 reserved
+# zero bytes, little-endian (kvsnap/store/common.py:10-11).
+BLOB_HEADER = struct.Struct("<8sIQI8s")
+BLOB_MAGIC = b"KVSBLOB1"
+
+
+def blob_name(blob_id: str) -> str:
+    """File name of a blob: its 64-hex content id plus ``.blob`` (``kvsnap/store/blobs.py:33-36``)."""
+    if len(blob_id) != 64 or any(c not in "0123456789abcdef" for c in blob_id):
+        raise ValueError("invalid blob identifier")
+    return blob_id + ".blob"
+
+
+def blob_file(payload) -> bytes:
+    """The bytes of one blob file: header, then the payload (``kvsnap/store/blobs.py:95-101``)."""
+    payload = bytes(payload)
+    return BLOB_HEADER.pack(BLOB_MAGIC, 1, len(payload), crc32c(payload), bytes(8)) + payload
 
 
 # ---- tensor-parallel shards -----------------------------------------------

@@ -298,6 +298,25 @@ def main():
                      "heads": 8, "head_dim": 128})
         golden[key] = case
 
+    # 6. Blob files: the reference's BlobWriter.prepare_blocks (kvsnap/store/store.py:647-674) on
+    #    seeded payloads, one of them twice (dedup). Recorded: the segments it returns and each
+    #    KVSBLOB1 file it wrote (whole file for short payloads, header + SHA-256 for long ones).
+    import tempfile
+    from kvsnap.store.store import BlobWriter
+    payloads = [kvgen.random_bytes(60 + i, length).tobytes()
+                for i, length in enumerate([16, 4096, 65536 + 48])]
+    blocks = [payloads[0], payloads[1], payloads[0], payloads[2]]
+    with tempfile.TemporaryDirectory() as root:
+        record = BlobWriter(root).prepare_blocks(blocks, durability="process")
+        files = {}
+        for segment in record["segments"]:
+            raw = (Path(root) / "blobs" / (segment["blob_id"] + ".blob")).read_bytes()
+            files[segment["blob_id"]] = ({"file_hex": raw.hex()} if len(raw) <= 8192 else
+                                         {"header_hex": raw[:32].hex(), "file_sha256": hashlib.sha256(raw).hexdigest(),
+                                          "file_bytes": len(raw)})
+    golden["blobs"] = {"payload_seeds": [60, 61, 62], "payload_lengths": [16, 4096, 65536 + 48],
+                       "blocks": [0, 1, 0, 2], "segments": record["segments"], "files": files}
+
     Path(args.out).write_text(json.dumps(golden, indent=1, sort_keys=True) + "\n")
     print(f"wrote {args.out}")
 

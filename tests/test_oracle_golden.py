@@ -98,3 +98,23 @@ def test_reshard_slice_is_the_tp4_shard_of_two_tp8_shards():
     for r in range(4):
         pair = np.concatenate([oracle.slice_heads(full, 8, 2 * r), oracle.slice_heads(full, 8, 2 * r + 1)], axis=3)
         assert np.array_equal(pair, oracle.slice_heads(full, 4, r))
+
+
+def test_blob_files_equal_the_references():
+    """The reference's BlobWriter wrote these files (tests/golden/make_golden.py, section 6)."""
+    import hashlib
+    g = GOLDEN["blobs"]
+    payloads = [kvgen.random_bytes(seed, length).tobytes()
+                for seed, length in zip(g["payload_seeds"], g["payload_lengths"])]
+    blocks = [payloads[i] for i in g["blocks"]]
+    assert oracle.dedup(blocks)[1] == g["segments"]
+    for segment in g["segments"]:
+        payload = blocks[segment["first_block"]]
+        raw = oracle.blob_file(payload)
+        want = g["files"][segment["blob_id"]]
+        if "file_hex" in want:
+            assert raw.hex() == want["file_hex"]
+        else:
+            assert raw[:32].hex() == want["header_hex"] and len(raw) == want["file_bytes"]
+            assert hashlib.sha256(raw).hexdigest() == want["file_sha256"]
+        assert oracle.blob_name(segment["blob_id"]) == segment["blob_id"] + ".blob"
