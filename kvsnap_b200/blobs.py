@@ -189,7 +189,7 @@ def _read_block(io, blob_dir, segment, address, size):
 
 
 def read_and_restore(plane, blob_dir, segments, block_ids, staged, *, first_block=0, io=None, workers=8,
-                     chunk_bytes=64 << 20, progress=None, lock_path=None):
+                     chunk_bytes=64 << 20, progress=None, lock_path=None, cache=None, generations=None):
     """Restore a disk-tier snapshot: blob reads, host-to-device copies and GPU CRC checks overlapped.
 
     ``segments``: the manifest's segments of the blocks restored here, block
@@ -208,12 +208,18 @@ def read_and_restore(plane, blob_dir, segments, block_ids, staged, *, first_bloc
     unreadable blob, a bad header or a checksum mismatch raises
     :class:`CorruptBlockError` (its ``blocks`` lists the mismatching block
     indices) before any KV byte is written. Returns the scatter launch count.
+
+    ``cache`` (a ``DigestCache``) and ``generations``: once restored, each
+    block with a generation is recorded under it with its segment's content
+    id and CRC32C, so the next save of an unchanged block skips SHA-256.
     """
     torch = plane.torch
     plane._validate_ids(block_ids)
     n, size = len(block_ids), plane.block_bytes
     if len(segments) != n:
         raise ValueError("one segment per block is required")
+    if (cache is None) != (generations is None) or (generations is not None and len(generations) != n):
+        raise ValueError("a digest cache needs one generation per block")
     for index, segment in enumerate(segments, start=first_block):
         if segment["first_block"] != index or segment["nblocks"] != 1:
             raise CorruptBlockError("noncontiguous prepared block mapping")
@@ -300,4 +306,8 @@ def read_and_restore(plane, blob_dir, segments, block_ids, staged, *, first_bloc
                 progress.append((done, (n - last) * size))
     done.synchronize()
     plane._status_error(status)
+    if cache is not None:
+        for block, generation, segment in zip(block_ids, generations, segments):
+            if generation is not None:
+                cache.put(block, generation, (segment["blob_id"], segment["crc32c"]))
     return launches

@@ -22,6 +22,7 @@ There is no CPU path: without the CUDA library or a CUDA device these raise.
 """
 from __future__ import annotations
 
+import collections
 import ctypes as C
 import os
 import threading
@@ -116,11 +117,13 @@ class PendingDigests:
 
     def __init__(self):
         self._event = None
+        self._finish = None
         self._value = None
 
-    def _bind(self, event, crc, digest, stage, n):
-        # The staging buffer is kept referenced until the kernel reading it is done.
-        self._event, self._crc, self._digest, self._stage, self._n = event, crc, digest, stage, n
+    def _bind(self, event, finish):
+        # `finish` holds the staging buffer until the kernel reading it is done,
+        # and turns the kernels' outputs into the list once `event` has passed.
+        self._event, self._finish = event, finish
 
     def done(self) -> bool:
         return self._value is not None or (self._event is not None and self._event.query())
@@ -130,11 +133,61 @@ class PendingDigests:
             if self._event is None:
                 raise RuntimeError("no save has been bound to these digests")
             self._event.synchronize()
-            crcs = [v & 0xFFFFFFFF for v in self._crc.cpu().tolist()]
-            raw = self._digest.cpu().numpy().tobytes()
-            self._value = [(raw[32 * i:32 * i + 32].hex(), crcs[i]) for i in range(self._n)]
-            self._crc = self._digest = self._stage = None
+            self._value = self._finish()
+            self._finish = None
         return self._value
+
+
+class DigestCache:
+    """Known content ids of GPU KV blocks, so that a save hashes only the blocks a turn changed.
+
+    An entry maps (GPU block id, generation) to the ``(sha256 hex, crc32c)`` of
+    that block's packed bytes. The generation is the caller's: it must change
+    whenever the engine writes the block or the block is allocated anew (a
+    full vLLM block is immutable until it is freed). ``save_gather`` and
+    ``load_scatter`` fill the cache for the full blocks they move; a save then
+    skips SHA-256 for every full block it finds, after checking that the CRC32C
+    it just computed on the GPU equals the cached one (a mismatch is hashed
+    after all and counted in ``rejected``). The reference hashes every block of
+    every save (kvsnap/store/store.py:616-629, connector/volatile.py:141-151)
+    and lists "hashing only the blocks a turn changed" as its next step.
+    Least recently used entries go first beyond ``capacity``.
+    """
+
+    def __init__(self, capacity: int = 1 << 20):
+        if type(capacity) is not int or capacity <= 0:
+            raise ValueError("digest cache capacity must be a positive integer")
+        self.capacity = capacity
+        self._entries = collections.OrderedDict()
+        self._lock = threading.Lock()
+        self.hits = self.misses = self.rejected = 0
+
+    def get(self, block, generation):
+        with self._lock:
+            entry = self._entries.get((block, generation))
+            if entry is not None:
+                self._entries.move_to_end((block, generation))
+            return entry
+
+    def put(self, block, generation, digest):
+        sha, crc = digest
+        if not isinstance(sha, str) or len(sha) != 64:
+            raise ValueError("a digest is (64-hex sha256, crc32c)")
+        with self._lock:
+            self._entries[(block, generation)] = (sha, int(crc) & 0xFFFFFFFF)
+            self._entries.move_to_end((block, generation))
+            while len(self._entries) > self.capacity:
+                self._entries.popitem(last=False)
+
+    def forget(self, blocks):
+        """Drop every generation of these blocks (for example when the engine frees them)."""
+        blocks = set(blocks)
+        with self._lock:
+            for key in [k for k in self._entries if k[0] in blocks]:
+                del self._entries[key]
+
+    def __len__(self):
+        return len(self._entries)
 
 
 class CudaPool:
@@ -598,7 +651,8 @@ class TorchBlockDataPlane:
 
     # ---- restore ------------------------------------------------------------------------------
 
-    def load_scatter(self, block_ids, sources, *, progress=None, chunk_bytes=64 << 20, expected_crc32c=None):
+    def load_scatter(self, block_ids, sources, *, progress=None, chunk_bytes=64 << 20, expected_crc32c=None,
+                     cache=None, generations=None, known_digests=None):
         """Copy packed host blocks into ``block_ids`` and wait for it (reference dataplane.py:334-386).
 
         ``sources[i]`` is ``(allocation, offset)`` holding block i packed, in
@@ -620,9 +674,18 @@ class TorchBlockDataPlane:
         scatter is queued (and before ``progress`` is filled): a mismatch raises
         :class:`CorruptBlockError` with the KV cache untouched and no progress
         reported, so it stays a miss.
+
+        ``cache`` (a :class:`DigestCache`), ``generations`` and
+        ``known_digests``: the snapshot's ``(sha256 hex, crc32c)`` per block.
+        Once the restore has completed, each block with a generation (not
+        None) is recorded under it, so the next save of an unchanged block
+        skips SHA-256.
         """
         torch = self.torch
         self._validate_ids(block_ids)
+        if cache is not None and (generations is None or known_digests is None
+                                  or len(generations) != len(block_ids) or len(known_digests) != len(block_ids)):
+            raise ValueError("a digest cache needs one generation and one known digest per block")
         if len(sources) != len(block_ids):
             raise ValueError("one source per block is required")
         if expected_crc32c is not None and len(expected_crc32c) != len(block_ids):
@@ -707,6 +770,10 @@ class TorchBlockDataPlane:
                     raise
         done.synchronize()
         self._status_error(status)
+        if cache is not None:
+            for block, generation, digest in zip(block_ids, generations, known_digests):
+                if generation is not None:
+                    cache.put(block, generation, digest)
         return launches
 
     def _staged_chunks(self, sources, ids, n, per_launch, status, progress):
@@ -767,7 +834,8 @@ class TorchBlockDataPlane:
 
     # ---- save ---------------------------------------------------------------------------------
 
-    def save_gather(self, block_ids, targets, num_kv_tokens, *, chunk_bytes=64 << 20, digests=None):
+    def save_gather(self, block_ids, targets, num_kv_tokens, *, chunk_bytes=64 << 20, digests=None,
+                    cache=None, generations=None):
         """Gather blocks on the GPU and land them packed in pinned memory (reference dataplane.py:388-437).
 
         ``targets[i]`` is ``(allocation, offset)`` receiving block i packed, the
@@ -784,6 +852,11 @@ class TorchBlockDataPlane:
         instead returns as soon as the targets are written (the point at which
         the connector may free the GPU blocks) while the SHA-256 kernel still
         runs; its ``result()`` waits for it and returns the list.
+
+        ``cache`` (a :class:`DigestCache`) with ``generations[i]`` for each
+        block: full blocks found in the cache are not hashed again (their
+        CRC32C, computed by the gather anyway, must equal the cached one), and
+        every full block's digest is stored for the next save.
         """
         torch = self.torch
         self._validate_ids(block_ids)
@@ -799,6 +872,21 @@ class TorchBlockDataPlane:
         n, size = len(block_ids), self.block_bytes
         valid = num_kv_tokens % self.block_size
         per_chunk = max(1, min(n, chunk_bytes // size))
+        if (cache is None) != (generations is None):
+            raise ValueError("a digest cache needs one generation per block, and generations a cache")
+        if generations is not None and len(generations) != n:
+            raise ValueError("one generation per block is required")
+        if cache is not None and digests is None:
+            raise ValueError("a digest cache serves digests: pass digests= as well")
+        # Full blocks only: the last block's tail slots are zeroed and change with the next token.
+        full = n if valid == 0 else n - 1
+        known = {}
+        if cache is not None:
+            for i in range(full):
+                entry = cache.get(block_ids[i], generations[i])
+                if entry is not None:
+                    known[i] = entry
+        hashed = [i for i in range(n) if i not in known]
         direct = self.save_mode == "direct" and digests is None
         copies = 0
         with torch.cuda.stream(stream):
@@ -836,7 +924,9 @@ class TorchBlockDataPlane:
                         stream.cuda_stream))
                     if digests is not None:
                         side = self._sha_stream()
-                        digest = self._sha256_after(stage, table[n:], n, stream, side)
+                        addresses = table[n:] if not known else torch.tensor(
+                            [write_to[i] for i in hashed], dtype=torch.int64).pin_memory().to(device, non_blocking=True)
+                        digest = self._sha256_after(stage, addresses, len(hashed), stream, side)
                     entries = []
                     for first in range(0, n, per_chunk):
                         for i, j in self._runs(targets, first, min(n, first + per_chunk), size):
@@ -856,10 +946,48 @@ class TorchBlockDataPlane:
             finished = torch.cuda.Event()
             finished.record(side)
             pending = digests if isinstance(digests, PendingDigests) else PendingDigests()
-            pending._bind(finished, crc, digest, stage, n)
+            keys = [(block_ids[i], generations[i]) for i in range(full)] if cache is not None else []
+            pending._bind(finished, lambda: self._digests(crc, digest, hashed, known, stage, write_to, cache, keys))
             if not isinstance(digests, PendingDigests):
                 digests.extend(pending.result())
         return copies
+
+    def _digests(self, crc, digest, hashed, known, stage, write_to, cache, keys):
+        """The save's ``(sha256 hex, crc32c)`` list, once its SHA-256 kernel has finished.
+
+        Blocks served from ``cache`` must have kept their CRC32C; one that has
+        not is hashed now from the staging buffer, which is still alive.
+        """
+        torch = self.torch
+        crcs = [v & 0xFFFFFFFF for v in crc.cpu().tolist()]
+        raw = digest.cpu().numpy().tobytes()
+        out = [None] * len(crcs)
+        for k, i in enumerate(hashed):
+            out[i] = (raw[32 * k:32 * k + 32].hex(), crcs[i])
+        stale = [i for i, (sha, c) in known.items() if c != crcs[i]]
+        for i, entry in known.items():
+            out[i] = (entry[0], crcs[i])
+        if cache is not None:
+            cache.hits += len(known) - len(stale)
+            cache.misses += len(keys) - len(known)
+            cache.rejected += len(stale)
+        if stale:
+            lib = _dp(self.pool.lib)
+            stream = self._sha_stream()
+            device = stage.device
+            with torch.cuda.stream(stream):
+                addresses = torch.tensor([write_to[i] for i in stale], dtype=torch.int64, device=device)
+                fresh = torch.empty(len(stale) * 32, dtype=torch.uint8, device=device)
+                self._check(lib.kvsnap_dp_sha256(addresses.data_ptr(), len(stale), self.block_bytes,
+                                                 fresh.data_ptr(), stream.cuda_stream))
+            stream.synchronize()
+            raw = fresh.cpu().numpy().tobytes()
+            for k, i in enumerate(stale):
+                out[i] = (raw[32 * k:32 * k + 32].hex(), crcs[i])
+        if cache is not None:
+            for i, key in enumerate(keys):
+                cache.put(key[0], key[1], out[i])
+        return out
 
     def _sha_stream(self):
         with self._sha_lock:
