@@ -101,10 +101,16 @@ int kvsnap_pool_wait_many(void* pool, int64_t n, const uint64_t* ids);
 #define KVSNAP_DP_CRC_MISMATCH 4u    /* a block's CRC32C differed from the expected one */
 
 /* OR into a `vec` argument when every packed address is device memory: the
-   kernels then take 64 contiguous bytes a lane in 2 KiB warp steps with
-   per-lane CRC tables (HBM-friendly) instead of 16 bytes a lane in 512-byte
-   steps (host-link friendly). Needs vec 16. */
+   kernels then give each lane one contiguous segment of a span, move whole
+   128-byte lines coalesced and CRC through per-lane tables (HBM-friendly),
+   instead of 16 bytes a lane in 512-byte steps (host-link friendly).
+   Needs vec 16. */
 #define KVSNAP_DP_HBM 0x100
+/* With KVSNAP_DP_HBM, a hint when every span is small (up to 8 KiB, e.g. a
+   tensor-parallel shard's): each warp then takes contiguous units and folds
+   the CRCs of a block's consecutive spans as one run. Results are the same
+   with or without it. */
+#define KVSNAP_DP_RUNS 0x200
 
 /*
  * One registered layer view, i.e. one span of every packed block. A packed

@@ -15,6 +15,8 @@ IO_ABI_VERSION = 1
 MISALIGNED, BAD_BLOCK, CRC_MISMATCH = 1, 2, 4
 # OR into a kernel's `vec` when every packed address is device memory.
 HBM = 0x100
+RUNS = 0x200            # with HBM: spans of at most RUNS_SPAN_BYTES fold in runs
+RUNS_SPAN_BYTES = 8 << 10
 
 
 class Span(C.Structure):

@@ -444,31 +444,62 @@ __device__ __forceinline__ uint32_t mul_x32(const uint32_t* t4, uint32_t r) {
     return t4[768 + (r & 255)] ^ t4[512 + ((r >> 8) & 255)] ^ t4[256 + ((r >> 16) & 255)] ^ t4[r >> 24];
 }
 
-// Places a lane's chains in its unit: ((c0 x^32 + c1) x^32 + c2) x^32 + c3
-// = raw(segment) * x^96, times x^(8*S*(31-lane)) to move it to the segment's
-// place. That last factor is recomputed only when the segment size S changes.
+// A lane's chains over its segment, combined: ((c0 x^32 + c1) x^32 + c2) x^32 + c3
+// = raw(segment) * x^96.
+__device__ __forceinline__ uint32_t combine_chains(const Chains& r, const uint32_t* t4) {
+    uint32_t h = mul_x32(t4, r.c[0]) ^ r.c[1];
+    h = mul_x32(t4, h) ^ r.c[2];
+    return mul_x32(t4, h) ^ r.c[3];
+}
+
+// x^(8*S*(31-lane)), which moves a lane's segment to its place in a unit of 32
+// segments of S bytes; recomputed only when S changes.
 struct LaneShift {
     int64_t seg = -1;
     uint32_t k = 0;
-    __device__ __forceinline__ uint32_t place(const Chains& r, const uint32_t* t4, int64_t s, int lane) {
+    __device__ __forceinline__ uint32_t factor(int64_t s, int lane) {
         if (s != seg) {
             seg = s;
             k = dev_xpow8n(uint64_t(s) * uint64_t(31 - lane));
         }
-        uint32_t h = mul_x32(t4, r.c[0]) ^ r.c[1];
-        h = mul_x32(t4, h) ^ r.c[2];
-        h = mul_x32(t4, h) ^ r.c[3];
-        return gf_mulmod(h, k);
+        return k;
     }
 };
 
+// r * x^(8*m) for the m = `bytes` the table tx was built for (four lookups,
+// as mul_x32 with T_k[v] * x^(8m-32)), or by a GF(2) multiply for any other m.
+struct AppendBytes {
+    const uint32_t* tx;
+    int64_t bytes;
+    __device__ __forceinline__ uint32_t apply(uint32_t r, int64_t m) const {
+        if (m == bytes) return mul_x32(tx, r);
+        return gf_mulmod(r, dev_xpow8n(uint64_t(m)));
+    }
+};
+
+// Builds tx[k*256 + v] = T_k[v] * x^(8m - 32) (m >= 4), the table of AppendBytes.
+__device__ __forceinline__ void load_append_table(uint32_t* tx, int64_t m) {
+    const uint32_t f = dev_xpow8n(uint64_t(m - 4));
+    for (int i = threadIdx.x; i < 4 * 256; i += blockDim.x) tx[i] = gf_mulmod(g_tables.t[i >> 8][i & 255], f);
+}
+
 // ---- a warp's stream of units --------------------------------------------------
 //
-// A warp takes its units (grid-stride) as one stream of 4 KiB steps, so the
-// loads of the next units' first steps are in flight while the current unit
-// finishes: small units (a TP shard's 4 or 8 KiB spans) pay no load latency of
-// their own. The load side runs kSegDepth steps ahead of the fold side and
-// hands each unit's description over through a ring in shared memory.
+// A warp takes its units as one stream of 4 KiB steps, so the loads of the
+// next units' first steps are in flight while the current unit finishes: small
+// units (a TP shard's 4 or 8 KiB spans) pay no load latency of their own. The
+// load side runs kSegDepth steps ahead of the fold side and hands each unit's
+// description over through a ring in shared memory.
+//
+// Small spans (RUNS): a warp takes a contiguous range of units, mostly
+// consecutive spans of one packed block, and folds their CRCs as one run.
+// Each lane keeps a Horner sum of its segments' values over the run,
+// multiplying by x^(8 * bytes of the next unit): four lookups in a shared
+// table when that is the span size the table was built for. Placing the lanes
+// and the run in the block then costs two GF(2) multiplies and one atomic per
+// run, not per unit. The caller asks for this with KVSNAP_DP_RUNS when its
+// spans are small; otherwise units are placed one by one and dealt to warps
+// grid-stride, which measured faster for 32 KiB spans.
 
 // One unit as the warp's stream carries it (the same in every lane).
 struct alignas(16) SegUnit {
@@ -479,7 +510,7 @@ struct alignas(16) SegUnit {
     int64_t block;       // the packed block it belongs to (its CRC accumulator)
     uint32_t shift;      // x^(8 * bytes after the unit in its packed block)
     int32_t steps;       // seg / kSegLine
-    int32_t span;        // span index (the tail mask)
+    int32_t span;        // position of the unit in its block (span, or piece), for runs and the tail mask
 };
 // The load side is at most kSegDepth steps, so at most kSegDepth + 1 units
 // (it moves on to the next unit as soon as it issues a unit's last step),
@@ -487,32 +518,49 @@ struct alignas(16) SegUnit {
 constexpr int kRing = 4;
 static_assert(kRing >= kSegDepth + 2 && (kRing & (kRing - 1)) == 0, "ring of unit descriptions");
 constexpr int kSegRingBytes = kSegWarps * kRing * int(sizeof(SegUnit));
-constexpr int kSegT4Bytes = 4 * 256 * 4;                // T_0..T_3, one copy (the chain combine)
+constexpr int kSegT4Bytes = 2 * 4 * 256 * 4;            // T_0..T_3 (chain combine), then "append span bytes"
 constexpr int kSegSmemTotal = kSegRingBytes + kSegT4Bytes + kSegSmemBytes;
 static_assert(kSegSmemTotal <= 227 * 1024, "segment kernels exceed the shared memory of a CTA");
 
 // (block, span) units of a gather or scatter: unit u is span u % nspans of
-// packed block u / nspans. A warp's cursor moves by the grid's warp count,
-// tracked as (block, span) steps so that no unit costs a 64-bit division.
-template <int MODE>
+// packed block u / nspans, walked as (block, span) steps so that no unit costs
+// a 64-bit division. RANGE: warp w of W takes the contiguous units
+// [u*w/W, u*(w+1)/W), whose neighbours are mostly the next span of the same
+// block (runs); otherwise warp w takes units w, w + W, ..., so that
+// concurrent warps move neighbouring bytes.
+template <int MODE, bool RANGE>
 struct SpanUnits {
     SpanArgs a;
-    int64_t i, di;       // packed block of the cursor, and its step
-    int s, ds;           // span of the cursor, and its step
-    __device__ SpanUnits(const SpanArgs& args, int64_t u0, int64_t du)
-        : a(args), i(u0 / args.nspans), di(du / args.nspans), s(int(u0 % args.nspans)), ds(int(du % args.nspans)) {}
+    int64_t i, left;     // packed block of the cursor, and units left to walk
+    int64_t di;          // block step (grid-stride)
+    int s, ds;           // span of the cursor, and its step (grid-stride)
+    __device__ SpanUnits(const SpanArgs& args, int64_t w, int64_t warps) : a(args) {
+        const int64_t count = args.n * args.nspans;
+        const int64_t begin = RANGE ? count * w / warps : w;
+        i = begin / args.nspans;
+        s = int(begin - i * args.nspans);
+        di = warps / args.nspans;
+        ds = int(warps - di * args.nspans);
+        left = RANGE ? count * (w + 1) / warps - begin : (begin < count ? (count - begin + warps - 1) / warps : 0);
+    }
     __device__ __forceinline__ void step() {
-        i += di;
-        s += ds;
-        if (s >= a.nspans) {
-            s -= a.nspans;
-            ++i;
+        --left;
+        if (RANGE) {
+            if (++s == a.nspans) {
+                s = 0;
+                ++i;
+            }
+        } else {
+            i += di;
+            s += ds;
+            if (s >= a.nspans) {
+                s -= a.nspans;
+                ++i;
+            }
         }
     }
-    // Describes the next valid unit at or after the cursor in `out` and moves
-    // the cursor past it; flags and skips bad ones.
     __device__ __forceinline__ bool next(SegUnit& out, int lane) {
-        for (; i < a.n; step()) {
+        for (; left > 0; step()) {
             const kvsnap_span& sp = a.spans[s];
             const int64_t block = a.blocks[i];
             if (block < 0 || block >= sp.nblocks) {
@@ -564,7 +612,7 @@ struct PieceUnits {
             out.block = i;
             out.shift = dev_xpow8n(uint64_t(block_bytes - at - len));
             out.steps = int32_t(out.seg / kSegLine);
-            out.span = 0;
+            out.span = int32_t(p);
             u += du;
             return true;
         }
@@ -576,10 +624,10 @@ struct PieceUnits {
 // unit's share XORed into crc_out[block]), the last block's tail masked (TAIL).
 // Lane l issues, in every step, the 16-byte slot (l & 7) of lines 4j + (l >> 3),
 // j = 0..7; `buf` is the warp's line buffer, `ring` its unit descriptions.
-template <bool STORE, bool CRC, bool TAIL, class Units>
-__device__ __forceinline__ void warp_stream(Units units, const RepTables& tl, const uint32_t* t4, uint4* buf,
-                                            SegUnit* ring, int lane, uint32_t* crc_out, const kvsnap_span* spans,
-                                            int valid) {
+template <bool STORE, bool CRC, bool TAIL, bool RUNS, class Units>
+__device__ __forceinline__ void warp_stream(Units units, const RepTables& tl, const uint32_t* t4,
+                                            const AppendBytes& append, uint4* buf, SegUnit* ring, int lane,
+                                            uint32_t* crc_out, const kvsnap_span* spans, int valid) {
     const int row = lane >> 3, slot = lane & 7;
     SegUnit L;                                   // the unit the load side is in
     if (!units.next(L, lane)) return;
@@ -591,6 +639,16 @@ __device__ __forceinline__ void warp_stream(Units units, const RepTables& tl, co
     int pk = 0, pt = 0;
     Chains r;
     LaneShift place;
+    // The run of units being folded together: one packed block, consecutive
+    // positions, one segment size. acc is the lane's Horner sum over it.
+    bool run = false;
+    int64_t run_block = 0, run_seg = 0;
+    int32_t run_pos = 0;
+    uint32_t run_shift = 0, acc = 0;
+    auto flush = [&]() {
+        const uint32_t x = gf_mulmod(warp_xor(gf_mulmod(acc, place.factor(run_seg, lane))), run_shift);
+        if (lane == 0) atomicXor(&crc_out[run_block], x);
+    };
 
     // Issue the load side's next step into v and move the load side on.
     auto load_next = [&](uint4(&v)[8]) -> bool {
@@ -645,9 +703,25 @@ __device__ __forceinline__ void warp_stream(Units units, const RepTables& tl, co
     // After a step: at the end of a unit, its CRC share goes out and the next unit comes in.
     auto advance = [&]() {
         if (++pt < P.steps) return;
-        if (CRC) {
-            const uint32_t x = gf_mulmod(warp_xor(place.place(r, t4, P.seg, lane)), P.shift);
+        if (CRC && !RUNS) {
+            const uint32_t x = gf_mulmod(warp_xor(gf_mulmod(combine_chains(r, t4), place.factor(P.seg, lane))),
+                                         P.shift);
             if (lane == 0) atomicXor(&crc_out[P.block], x);
+            r = Chains{};
+        }
+        if (CRC && RUNS) {
+            const uint32_t h = combine_chains(r, t4);
+            if (run && P.block == run_block && P.span == run_pos + 1 && P.seg == run_seg) {
+                acc = append.apply(acc, 32 * P.seg - P.pad) ^ h;
+            } else {
+                if (run) flush();
+                run = true;
+                run_block = P.block;
+                run_seg = P.seg;
+                acc = h;
+            }
+            run_pos = P.span;
+            run_shift = P.shift;
             r = Chains{};
         }
         pt = 0;
@@ -674,31 +748,40 @@ __device__ __forceinline__ void warp_stream(Units units, const RepTables& tl, co
             }
         }
     }
+    if (CRC && RUNS && run) flush();
 }
 
 // TAIL: every unit belongs to the save's last block, whose token slots from
 // `valid` on are written as zeros. The launcher gives that block a launch of
 // its own, so the common kernel carries none of the masking code.
 // Shared memory: unit rings, then (with a CRC) the tables and line buffers.
-template <int MODE, bool TAIL>
+template <int MODE, bool TAIL, bool RUNS>
 __global__ void __launch_bounds__(kSegThreads, 1) span_kernel_hbm(SpanArgs a) {
     extern __shared__ uint4 smem[];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     SegUnit* ring = reinterpret_cast<SegUnit*>(smem) + warp * kRing;
     uint32_t* t4 = reinterpret_cast<uint32_t*>(smem + kSegRingBytes / 16);
+    uint32_t* tx = t4 + 4 * 256;
     uint32_t* tb = t4 + kSegT4Bytes / 4;
     uint4* buf = smem + (kSegRingBytes + kSegT4Bytes) / 16 + kRepWords / 4 + warp * (kSegStep / 16);
     const bool crc = a.crc != nullptr;
-    if (crc) load_seg_tables(tb, t4);
+    // Runs are folded with the first span's size; spans of other sizes take the multiply.
+    const int64_t span_bytes = a.spans[0].bytes >= 4 ? a.spans[0].bytes : 4;
+    if (crc) {
+        load_seg_tables(tb, t4);
+        if (RUNS) load_append_table(tx, span_bytes);
+    }
     __syncthreads();
     if (MODE == kScatter && a.gate && *a.gate) return;
     const RepTables tl{reinterpret_cast<const char*>(tb), 4u * lane};
-    const int64_t u0 = (int64_t)blockIdx.x * kSegWarps + warp, du = (int64_t)gridDim.x * kSegWarps;
-    const SpanUnits<MODE> units(a, u0, du);
-    if (crc)
-        warp_stream<true, true, TAIL>(units, tl, t4, buf, ring, lane, a.crc, a.spans, a.valid);
+    const AppendBytes append{tx, span_bytes};
+    const int64_t w = (int64_t)blockIdx.x * kSegWarps + warp, warps = (int64_t)gridDim.x * kSegWarps;
+    if (!crc)
+        warp_stream<true, false, TAIL, false>(SpanUnits<MODE, false>(a, w, warps), tl, t4, append, buf, ring, lane,
+                                              nullptr, a.spans, a.valid);
     else
-        warp_stream<true, false, TAIL>(units, tl, t4, buf, ring, lane, nullptr, a.spans, a.valid);
+        warp_stream<true, true, TAIL, RUNS>(SpanUnits<MODE, RUNS>(a, w, warps), tl, t4, append, buf, ring, lane,
+                                            a.crc, a.spans, a.valid);
 }
 
 __global__ void __launch_bounds__(kSegThreads, 1) crc_kernel_hbm(const int64_t* addrs, int64_t n,
@@ -708,14 +791,16 @@ __global__ void __launch_bounds__(kSegThreads, 1) crc_kernel_hbm(const int64_t* 
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     SegUnit* ring = reinterpret_cast<SegUnit*>(smem) + warp * kRing;
     uint32_t* t4 = reinterpret_cast<uint32_t*>(smem + kSegRingBytes / 16);
+    uint32_t* tx = t4 + 4 * 256;
     uint32_t* tb = t4 + kSegT4Bytes / 4;
     uint4* buf = smem + (kSegRingBytes + kSegT4Bytes) / 16 + kRepWords / 4 + warp * (kSegStep / 16);
     load_seg_tables(tb, t4);
     __syncthreads();
     const RepTables tl{reinterpret_cast<const char*>(tb), 4u * lane};
-    const int64_t u0 = (int64_t)blockIdx.x * kSegWarps + warp, du = (int64_t)gridDim.x * kSegWarps;
-    const PieceUnits units{addrs, n, block_bytes, (block_bytes + kSegPiece - 1) / kSegPiece, status, u0, du};
-    warp_stream<false, true, false>(units, tl, t4, buf, ring, lane, crc, nullptr, 0);
+    const AppendBytes append{tx, kSegPiece};
+    const PieceUnits units{addrs, n, block_bytes, (block_bytes + kSegPiece - 1) / kSegPiece, status,
+                           (int64_t)blockIdx.x * kSegWarps + warp, (int64_t)gridDim.x * kSegWarps};
+    warp_stream<false, true, false, false>(units, tl, t4, append, buf, ring, lane, crc, nullptr, 0);
 }
 
 // CRC32C of whole packed blocks, in pieces of kPiece bytes per warp.
@@ -1136,7 +1221,8 @@ int launch_spans(const kvsnap_span* spans, int nspans, uint64_t block_bytes, con
                  const uint32_t* gate, uint32_t* status, int vec, int ctas, uintptr_t stream) {
     return guarded([&] {
         const bool hbm = (vec & KVSNAP_DP_HBM) != 0;
-        vec &= ~KVSNAP_DP_HBM;
+        const bool runs = (vec & KVSNAP_DP_RUNS) != 0;
+        vec &= ~(KVSNAP_DP_HBM | KVSNAP_DP_RUNS);
         if (n < 0 || nspans <= 0 || !spans) throw Fail{"invalid span table"};
         if (vec != 16 && vec != 8) throw Fail{"vector width must be 16 or 8"};
         if (hbm && vec != 16) throw Fail{"the device-memory kernels need 16-byte alignment"};
@@ -1159,15 +1245,16 @@ int launch_spans(const kvsnap_span* spans, int nspans, uint64_t block_bytes, con
                     body = n - 1;
                     SpanArgs last{spans, nspans, blocks + body, packed + body, 1, valid, crc ? crc + body : nullptr,
                                   gate, status};
-                    configure_once(reinterpret_cast<const void*>(span_kernel_hbm<MODE, true>), kSegSmemTotal);
-                    span_kernel_hbm<MODE, true><<<grid_of(1), kSegThreads, smem, s>>>(last);
+                    configure_once(reinterpret_cast<const void*>(span_kernel_hbm<MODE, true, false>), kSegSmemTotal);
+                    span_kernel_hbm<MODE, true, false><<<grid_of(1), kSegThreads, smem, s>>>(last);
                     check(cudaGetLastError());
                 }
             }
             if (body > 0) {
                 a.n = body;
-                configure_once(reinterpret_cast<const void*>(span_kernel_hbm<MODE, false>), kSegSmemTotal);
-                span_kernel_hbm<MODE, false><<<grid_of(body), kSegThreads, smem, s>>>(a);
+                auto kernel = runs ? span_kernel_hbm<MODE, false, true> : span_kernel_hbm<MODE, false, false>;
+                configure_once(reinterpret_cast<const void*>(kernel), kSegSmemTotal);
+                kernel<<<grid_of(body), kSegThreads, smem, s>>>(a);
                 check(cudaGetLastError());
             }
             if (crc) finish(crc, expect, n, block_bytes, status, s, kSegUnscale);
@@ -1208,7 +1295,7 @@ extern "C" int kvsnap_dp_crc32c(const int64_t* addrs, int64_t n, uint64_t block_
                                 const uint32_t* expect, uint32_t* status, int vec, int ctas, uintptr_t stream) {
     return guarded([&] {
         const bool hbm = (vec & KVSNAP_DP_HBM) != 0;
-        vec &= ~KVSNAP_DP_HBM;
+        vec &= ~(KVSNAP_DP_HBM | KVSNAP_DP_RUNS);      // whole blocks: the hint has no use here
         if (n < 0 || vec != 16 && vec != 8) throw Fail{"invalid CRC request"};
         if (n == 0) return;
         if (!addrs || !crc_out || block_bytes == 0) throw Fail{"CRC needs addresses, output and a block size"};

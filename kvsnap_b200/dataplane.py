@@ -509,8 +509,10 @@ class TorchBlockDataPlane:
                 raise RuntimeError("packed block size disagrees with the registered layers")
             host = torch.frombuffer(bytearray(bytes(spans)), dtype=torch.uint8)
             self._span_vec = vec
-            # Device-side copies may use the lane-contiguous HBM kernels.
+            # Device-side copies may use the segment-lane HBM kernels; small spans fold in runs.
             self._hbm = _abi.HBM if vec == 16 else 0
+            if self._hbm and max(layer["bytes"] for layer in self.layers) <= _abi.RUNS_SPAN_BYTES:
+                self._hbm |= _abi.RUNS
             self._min_blocks = min(t.shape[0] for t in self.caches.values())
             self._span_table = host.to(self._device())
             # Side streams: restores that read pinned memory in place run on their

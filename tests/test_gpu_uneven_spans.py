@@ -11,7 +11,10 @@ empty. These layers make it non-empty and uneven:
 They also mix token-major storage ([B,N,H,C] under a [B,H,N,C] view) with
 head-major storage, and a 24-byte row that the tail mask handles byte by byte.
 With a single CTA, one warp meets units of every size in turn, so the
-per-size lane shift must be recomputed whenever the size changes.
+per-size lane shift must be recomputed whenever the size changes. The "small"
+set has only spans of at most 8 KiB, which the plane launches with
+KVSNAP_DP_RUNS: a warp folds a block's consecutive spans as one run, and
+spans of a size other than the first one's take the multiply fallback.
 The oracle (oracle/oracle.py) gives the packed bytes, the tail zeroing, the
 digests and the restored cache.
 """
@@ -36,9 +39,13 @@ LAYERS = {
 }
 
 
-def build():
+SETS = {"mixed": sorted(LAYERS), "small": ["layer.a", "layer.b", "layer.d"]}
+
+
+def build(names):
     storages, views, caches, tensors = {}, {}, {}, {}
-    for i, (name, (h, c, token_major)) in enumerate(sorted(LAYERS.items())):
+    for i, name in enumerate(names):
+        h, c, token_major = LAYERS[name]
         per_block = h * N * c * 2
         buf = kvgen.random_bytes(7000 + i, BLOCKS * per_block)
         storages[name] = buf
@@ -53,16 +60,19 @@ def build():
     return storages, oracle.register(views, N), caches, tensors
 
 
+@pytest.mark.parametrize("layer_set", ["mixed", "small"])
 @pytest.mark.parametrize("ctas", [0, 1, 3])
 @pytest.mark.parametrize("tokens", [5 * N, 4 * N + 5, 1 * N + 1, 3])
-def test_uneven_spans_save_and_restore(ctas, tokens):
+def test_uneven_spans_save_and_restore(layer_set, ctas, tokens):
+    from kvsnap_b200 import _abi
     from kvsnap_b200.dataplane import TorchBlockDataPlane
-    storages, layout, caches, tensors = build()
+    storages, layout, caches, tensors = build(SETS[layer_set])
     plane = TorchBlockDataPlane(caches, N, 64 << 20, save_mode="staged", restore_mode="staged", ctas=ctas)
     try:
         assert plane.block_bytes == layout.block_bytes
         plane.warm_up()
         assert plane._hbm, "these layers must take the device-memory kernels"
+        assert bool(plane._hbm & _abi.RUNS) == (layer_set == "small")
         saved = [7, 2, 9, 0, 11][: (tokens + N - 1) // N]
         expected = oracle.pack(storages, layout, saved, tokens)
         size = plane.block_bytes
