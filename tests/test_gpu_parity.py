@@ -204,7 +204,7 @@ def test_crc32c_kernel_matches_the_reference_crc(length, hbm):
     status = torch.zeros(1, dtype=torch.int32, device="cuda")
     vec = 16 if length % 16 == 0 else 8
     if hbm:
-        vec |= 0x100          # KVSNAP_DP_HBM: lane-contiguous kernel where the block allows it
+        vec |= 0x100          # KVSNAP_DP_HBM: the segment-lane kernel where the block allows it
     s = torch.cuda.current_stream().cuda_stream
     assert lib.kvsnap_dp_crc32c(addrs.data_ptr(), n, length, crc.data_ptr(), 0, status.data_ptr(), vec, 0, s) == 0
     torch.cuda.synchronize()
