@@ -3,7 +3,7 @@
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
-Workload ("Qwen3-8B shape on 1xB200"): 36 layers, each a
+Workload (benchmark configuration 2, "Qwen3-8B shape on 1xB200"): 36 layers, each a
 paged ``[2, 32768 blocks, 16 tokens, 8 kv heads, 128]`` bf16 cache filled with
 seeded N(0,1) values (72 GiB of HBM), one 8192-token session = 512 blocks
 (1,207,959,552 bytes packed) at seeded random block ids. One step = save the
@@ -56,7 +56,7 @@ def parse():
     p.add_argument("--layers", type=int, default=LAYERS)
     p.add_argument("--heads", type=int, default=HEADS, help="KV heads a rank holds")
     p.add_argument("--model", choices=["qwen3-8b", "qwen3-32b-tp"], default="qwen3-8b",
-                   help="qwen3-32b-tp: BASELINE config 5, each of N ranks saves and restores its 8/N-head shard "
+                   help="qwen3-32b-tp: benchmark configuration 5, each of N ranks saves and restores its 8/N-head shard "
                         "of a 32768-token Qwen3-32B session (64 layers)")
     p.add_argument("--ctas", type=int, default=0, help="CTAs for the data-plane kernels (0: library default)")
     p.add_argument("--restore-mode", choices=["direct", "staged"], default="staged")
@@ -64,9 +64,9 @@ def parse():
     p.add_argument("--explore", type=str, default="", help="write a per-phase / CTA sweep breakdown to this path")
     p.add_argument("--seed", type=int, default=0)
     p.add_argument("--workload", choices=["session", "disk", "reshard", "rotation", "kernels"], default="session",
-                   help="session: BASELINE config 2 (the default line); disk: config 3, verified restores of "
+                   help="session: benchmark configuration 2 (the default line); disk: configuration 3, verified restores of "
                         "8k and 32k-token snapshots from one pinned staging buffer with seeded corruption; "
-                        "reshard: TP regroup over NVLink; rotation: config 4; kernels: the on-device "
+                        "reshard: TP regroup over NVLink; rotation: configuration 4; kernels: the on-device "
                         "gather, scatter and CRC kernels alone against a torch device copy")
     p.add_argument("--blob-dir", type=str, default="",
                    help="where the disk workload writes its blob files (default: the system temp dir)")
@@ -869,7 +869,7 @@ def run_kernels(args, world, rank, device):
 
 
 def run_disk(args, world, rank, device):
-    """the disk tier's restore from one pinned staging buffer, CRC32C checked on the GPU.
+    """Benchmark configuration 3: the disk tier's restore from one pinned staging buffer, CRC32C checked on the GPU.
 
     For 8192- and 32768-token Qwen3-8B snapshots: save the session into one
     staging buffer (its CRCs recorded, as the store's manifest does), flip one
@@ -1003,7 +1003,7 @@ def blob_phase(plane, sources, digests, restored, n, size, args):
 
 
 def run_reshard(args, world, rank, device):
-    """BASELINE config 5's regroup: a TP-(2T) Qwen3-32B snapshot restored at TP-T over NVLink.
+    """Benchmark configuration 5's regroup: a TP-(2T) Qwen3-32B snapshot restored at TP-T over NVLink.
 
     World size W (torchrun, one GPU a rank): the snapshot was saved at TP=W (one
     shard a rank, 64 layers × 8/W heads, 2048 blocks = 32768 tokens), the cache
@@ -1092,7 +1092,7 @@ def run_reshard(args, world, rank, device):
 
 
 def run_rotation(args, world, rank, device):
-    """64 Qwen3-1.7B sessions saved and restored beside synthetic decode traffic.
+    """Benchmark configuration 4: 64 Qwen3-1.7B sessions saved and restored beside synthetic decode traffic.
 
     Session lengths are log-uniform in [512, 8192] tokens (seeded); blocks come
     from a shuffled free list (fragmented tables). Sessions 32..63 fork sessions

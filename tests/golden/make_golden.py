@@ -1,6 +1,6 @@
 """Generate tests/golden/golden.json by running the REFERENCE kvsnap data plane on the CPU.
 
-    python tests/golden/make_golden.py [--reference /root/reference]
+    python tests/golden/make_golden.py [--reference <kvsnap source tree>]
 
 Needs the reference source tree (read-only) and ``make -C oracle`` (which
 compiles the reference's own ``csrc/dataplane/io.cpp`` into
