@@ -341,21 +341,28 @@ __global__ void __launch_bounds__(256) span_kernel(SpanArgs a) {
 constexpr int kRepWords = 4 * 256 * 32;                 // replicated T_12..T_15
 constexpr int kSegLine = 128;                           // bytes of a segment per step
 constexpr int kSegStep = 32 * kSegLine;                 // bytes a warp moves per step
-// Warps a CTA and steps of loads in flight a warp: build-time tuning knobs. On
-// B200 twelve warps with two steps in flight measured fastest over 4, 8 and
-// 32 KiB spans (more warps leave each thread too few registers to keep its
-// loads in flight; fewer leave small spans' per-unit work exposed).
+// Warps a CTA and steps of loads in flight a warp: build-time tuning knobs.
+// kSegWarps sizes the register budget and the largest shared-memory layout; a
+// launch may use fewer warps (the kernels read their count from blockDim). On
+// B200, with two steps in flight, twelve warps measured fastest for runs of
+// spans of at most 8 KiB (fewer leave small spans' per-unit work exposed) and
+// for whole-block CRCs, which only read; eight (KVSNAP_SEG_BULK_WARPS) for 16
+// and 32 KiB spans, where 7 or 9 to 12 warps measured 4 to 10 % slower. More
+// than twelve leave each thread too few registers to keep its loads in flight.
 #ifndef KVSNAP_SEG_WARPS
 #define KVSNAP_SEG_WARPS 12
+#endif
+#ifndef KVSNAP_SEG_BULK_WARPS
+#define KVSNAP_SEG_BULK_WARPS 8
 #endif
 #ifndef KVSNAP_SEG_DEPTH
 #define KVSNAP_SEG_DEPTH 2
 #endif
 constexpr int kSegWarps = KVSNAP_SEG_WARPS;
+constexpr int kSegBulkWarps = KVSNAP_SEG_BULK_WARPS;
+static_assert(kSegBulkWarps >= 1 && kSegBulkWarps <= kSegWarps, "bulk launches use at most kSegWarps warps");
 constexpr int kSegDepth = KVSNAP_SEG_DEPTH;
 constexpr int kSegThreads = 32 * kSegWarps;
-constexpr int kSegSmemBytes = kRepWords * 4 + kSegWarps * kSegStep;
-static_assert(kSegSmemBytes <= 227 * 1024, "segment kernels exceed the shared memory of a CTA");
 
 // Replicated layout, 256 bytes an entry so one byte permute forms an address:
 // entry v of T_{15-(2h+p)} for lane l lies at byte h*65536 + v*256 + p*128 + 4l,
@@ -429,8 +436,16 @@ struct TailMask {
     }
 };
 
+// Loads bypass L1 and ask L2 for whole 256-byte sectors: eight lanes cover a
+// 128-byte line and a lane's next line follows in the same segment, so the
+// second half of each sector is read by the next step.
 __device__ __forceinline__ uint4 seg_load(const char* src, int64_t at) {
-    return at >= 0 ? __ldcs(reinterpret_cast<const uint4*>(src + at)) : make_uint4(0, 0, 0, 0);
+    uint4 v = make_uint4(0, 0, 0, 0);
+    if (at >= 0)
+        asm volatile("ld.global.L1::no_allocate.L2::256B.v4.u32 {%0, %1, %2, %3}, [%4];"
+                     : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                     : "l"(src + at));
+    return v;
 }
 
 // Both sides are streamed: a session is far larger than L2, so nothing a
@@ -517,10 +532,36 @@ struct alignas(16) SegUnit {
 // ahead of the unit being folded: kSegDepth + 2 entries never collide.
 constexpr int kRing = 4;
 static_assert(kRing >= kSegDepth + 2 && (kRing & (kRing - 1)) == 0, "ring of unit descriptions");
-constexpr int kSegRingBytes = kSegWarps * kRing * int(sizeof(SegUnit));
-constexpr int kSegT4Bytes = 2 * 4 * 256 * 4;            // T_0..T_3 (chain combine), then "append span bytes"
-constexpr int kSegSmemTotal = kSegRingBytes + kSegT4Bytes + kSegSmemBytes;
+
+// Dynamic shared memory of a segment kernel of `warps` warps, in order: the
+// unit rings, T_0..T_3 (the chain combine) and, for runs, the append table,
+// the replicated tables, one line buffer a warp. It is sized to the launch:
+// shared memory and L1 split one 256 KiB array a SM, and what L1 keeps holds
+// the loads in flight. Without the four unused line buffers and the append
+// table, 8-warp gathers measured 2 % and whole-block CRCs 6 % faster; a 200 KiB
+// layout (L1 at 28 KiB) measured 13 % slower.
+__host__ __device__ constexpr int seg_ring_bytes(int warps) { return warps * kRing * int(sizeof(SegUnit)); }
+__host__ __device__ constexpr int seg_smem_bytes(int warps, bool runs) {
+    return seg_ring_bytes(warps) + (runs ? 2 : 1) * 4 * 256 * 4 + kRepWords * 4 + warps * kSegStep;
+}
+constexpr int kSegSmemTotal = seg_smem_bytes(kSegWarps, true);
 static_assert(kSegSmemTotal <= 227 * 1024, "segment kernels exceed the shared memory of a CTA");
+
+// A warp's view of that layout.
+struct SegSmem {
+    SegUnit* ring;       // its unit ring
+    uint32_t* t4;        // T_0..T_3
+    uint32_t* tx;        // the append table (runs only)
+    uint32_t* tb;        // the replicated tables
+    uint4* buf;          // its line buffer
+    __device__ SegSmem(uint4* smem, int warp, int warps, bool runs) {
+        ring = reinterpret_cast<SegUnit*>(smem) + warp * kRing;
+        t4 = reinterpret_cast<uint32_t*>(smem + seg_ring_bytes(warps) / 16);
+        tx = t4 + 4 * 256;
+        tb = t4 + (runs ? 2 : 1) * 4 * 256;
+        buf = reinterpret_cast<uint4*>(tb + kRepWords) + warp * (kSegStep / 16);
+    }
+};
 
 // (block, span) units of a gather or scatter: unit u is span u % nspans of
 // packed block u / nspans, walked as (block, span) steps so that no unit costs
@@ -758,12 +799,11 @@ __device__ __forceinline__ void warp_stream(Units units, const RepTables& tl, co
 template <int MODE, bool TAIL, bool RUNS>
 __global__ void __launch_bounds__(kSegThreads, 1) span_kernel_hbm(SpanArgs a) {
     extern __shared__ uint4 smem[];
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    SegUnit* ring = reinterpret_cast<SegUnit*>(smem) + warp * kRing;
-    uint32_t* t4 = reinterpret_cast<uint32_t*>(smem + kSegRingBytes / 16);
-    uint32_t* tx = t4 + 4 * 256;
-    uint32_t* tb = t4 + kSegT4Bytes / 4;
-    uint4* buf = smem + (kSegRingBytes + kSegT4Bytes) / 16 + kRepWords / 4 + warp * (kSegStep / 16);
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, per_cta = blockDim.x >> 5;
+    const SegSmem sm(smem, warp, per_cta, RUNS);
+    SegUnit* ring = sm.ring;
+    uint32_t *t4 = sm.t4, *tx = sm.tx, *tb = sm.tb;
+    uint4* buf = sm.buf;
     const bool crc = a.crc != nullptr;
     // Runs are folded with the first span's size; spans of other sizes take the multiply.
     const int64_t span_bytes = a.spans[0].bytes >= 4 ? a.spans[0].bytes : 4;
@@ -775,7 +815,7 @@ __global__ void __launch_bounds__(kSegThreads, 1) span_kernel_hbm(SpanArgs a) {
     if (MODE == kScatter && a.gate && *a.gate) return;
     const RepTables tl{reinterpret_cast<const char*>(tb), 4u * lane};
     const AppendBytes append{tx, span_bytes};
-    const int64_t w = (int64_t)blockIdx.x * kSegWarps + warp, warps = (int64_t)gridDim.x * kSegWarps;
+    const int64_t w = (int64_t)blockIdx.x * per_cta + warp, warps = (int64_t)gridDim.x * per_cta;
     if (!crc)
         warp_stream<true, false, TAIL, false>(SpanUnits<MODE, false>(a, w, warps), tl, t4, append, buf, ring, lane,
                                               nullptr, a.spans, a.valid);
@@ -788,18 +828,17 @@ __global__ void __launch_bounds__(kSegThreads, 1) crc_kernel_hbm(const int64_t* 
                                                                  int64_t block_bytes, uint32_t* crc,
                                                                  uint32_t* status) {
     extern __shared__ uint4 smem[];
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    SegUnit* ring = reinterpret_cast<SegUnit*>(smem) + warp * kRing;
-    uint32_t* t4 = reinterpret_cast<uint32_t*>(smem + kSegRingBytes / 16);
-    uint32_t* tx = t4 + 4 * 256;
-    uint32_t* tb = t4 + kSegT4Bytes / 4;
-    uint4* buf = smem + (kSegRingBytes + kSegT4Bytes) / 16 + kRepWords / 4 + warp * (kSegStep / 16);
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, per_cta = blockDim.x >> 5;
+    const SegSmem sm(smem, warp, per_cta, false);
+    SegUnit* ring = sm.ring;
+    uint32_t *t4 = sm.t4, *tx = sm.tx, *tb = sm.tb;     // tx: unused without runs
+    uint4* buf = sm.buf;
     load_seg_tables(tb, t4);
     __syncthreads();
     const RepTables tl{reinterpret_cast<const char*>(tb), 4u * lane};
     const AppendBytes append{tx, kSegPiece};
     const PieceUnits units{addrs, n, block_bytes, (block_bytes + kSegPiece - 1) / kSegPiece, status,
-                           (int64_t)blockIdx.x * kSegWarps + warp, (int64_t)gridDim.x * kSegWarps};
+                           (int64_t)blockIdx.x * per_cta + warp, (int64_t)gridDim.x * per_cta};
     warp_stream<false, true, false, false>(units, tl, t4, append, buf, ring, lane, crc, nullptr, 0);
 }
 
@@ -1234,11 +1273,11 @@ int launch_spans(const kvsnap_span* spans, int nspans, uint64_t block_bytes, con
         if (crc) check(cudaMemsetAsync(crc, 0, sizeof(uint32_t) * size_t(n), s));
         SpanArgs a{spans, nspans, blocks, packed, n, valid, crc, gate, status};
         if (hbm) {
-            auto grid_of = [&](int64_t blocks_of_work) {
-                const int64_t want = (blocks_of_work * nspans + kSegWarps - 1) / kSegWarps;
+            auto grid_of = [&](int64_t blocks_of_work, int warps) {
+                const int64_t want = (blocks_of_work * nspans + warps - 1) / warps;
                 return ctas > 0 ? ctas : int(want < sms ? want : sms);
             };
-            const int smem = crc ? kSegSmemTotal : kSegRingBytes;
+
             int64_t body = n;
             if constexpr (MODE == kGather) {
                 if (valid > 0) {   // the last block, masked, in a launch of its own
@@ -1246,15 +1285,19 @@ int launch_spans(const kvsnap_span* spans, int nspans, uint64_t block_bytes, con
                     SpanArgs last{spans, nspans, blocks + body, packed + body, 1, valid, crc ? crc + body : nullptr,
                                   gate, status};
                     configure_once(reinterpret_cast<const void*>(span_kernel_hbm<MODE, true, false>), kSegSmemTotal);
-                    span_kernel_hbm<MODE, true, false><<<grid_of(1), kSegThreads, smem, s>>>(last);
+                    span_kernel_hbm<MODE, true, false><<<grid_of(1, kSegWarps), kSegThreads,
+                                                         crc ? seg_smem_bytes(kSegWarps, false) : seg_ring_bytes(kSegWarps),
+                                                         s>>>(last);
                     check(cudaGetLastError());
                 }
             }
             if (body > 0) {
                 a.n = body;
                 auto kernel = runs ? span_kernel_hbm<MODE, false, true> : span_kernel_hbm<MODE, false, false>;
+                const int warps = runs ? kSegWarps : kSegBulkWarps;
                 configure_once(reinterpret_cast<const void*>(kernel), kSegSmemTotal);
-                kernel<<<grid_of(body), kSegThreads, smem, s>>>(a);
+                kernel<<<grid_of(body, warps), 32 * warps, crc ? seg_smem_bytes(warps, runs) : seg_ring_bytes(warps),
+                         s>>>(a);
                 check(cudaGetLastError());
             }
             if (crc) finish(crc, expect, n, block_bytes, status, s, kSegUnscale);
@@ -1306,7 +1349,8 @@ extern "C" int kvsnap_dp_crc32c(const int64_t* addrs, int64_t n, uint64_t block_
             configure_once(reinterpret_cast<const void*>(crc_kernel_hbm), kSegSmemTotal);
             const int64_t want = (n * ((int64_t(block_bytes) + kPiece - 1) / kPiece) + kSegWarps - 1) / kSegWarps;
             const int grid = ctas > 0 ? ctas : int(want < sms ? want : sms);
-            crc_kernel_hbm<<<grid, kSegThreads, kSegSmemTotal, s>>>(addrs, n, int64_t(block_bytes), crc_out, status);
+            crc_kernel_hbm<<<grid, kSegThreads, seg_smem_bytes(kSegWarps, false), s>>>(addrs, n, int64_t(block_bytes),
+                                                                                       crc_out, status);
             check(cudaGetLastError());
             finish(crc_out, expect, n, block_bytes, status, s, kSegUnscale);
             return;
