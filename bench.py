@@ -204,7 +204,11 @@ def make_caches(args, device):
 
 
 def session_blocks(args, n):
+    """Two disjoint seeded block sets of n blocks each (save, restore); block 0 is kept free."""
     import numpy as np
+    if args.pool_blocks < 2 * n + 1:
+        raise SystemExit(f"--pool-blocks {args.pool_blocks} is too small: two disjoint {n}-block sessions "
+                         f"need at least {2 * n + 1}")
     order = np.random.Generator(np.random.PCG64(args.seed + 17)).permutation(args.pool_blocks - 1) + 1
     return [int(b) for b in order[:n]], [int(b) for b in order[n:2 * n]]
 

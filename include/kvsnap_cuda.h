@@ -99,6 +99,7 @@ int kvsnap_pool_wait_many(void* pool, int64_t n, const uint64_t* ids);
 #define KVSNAP_DP_MISALIGNED 1u      /* an address or size broke the vector width */
 #define KVSNAP_DP_BAD_BLOCK 2u       /* a block id outside its cache */
 #define KVSNAP_DP_CRC_MISMATCH 4u    /* a block's CRC32C differed from the expected one */
+#define KVSNAP_DP_BAD_PAIR 8u        /* KVSNAP_DP_PAIRS met two spans of different sizes, or apart */
 
 /* OR into a `vec` argument when every packed address is device memory: the
    kernels then give each lane one contiguous segment of a span, move whole
@@ -111,6 +112,13 @@ int kvsnap_pool_wait_many(void* pool, int64_t n, const uint64_t* ids);
    the CRCs of a block's consecutive spans as one run. Results are the same
    with or without it. */
 #define KVSNAP_DP_RUNS 0x200
+/* With KVSNAP_DP_RUNS, a hint when every span has one size S of 2 or 4 KiB
+   (a TP-8 or TP-16 shard's) and nspans is even: each unit is then a pair of
+   consecutive spans, so each lane owns 2 * S / 32 contiguous packed bytes and
+   a unit's CRC is placed once per 2 * S. A pair whose spans differ sets
+   KVSNAP_DP_BAD_PAIR and is skipped. Results are the same with or without
+   it. */
+#define KVSNAP_DP_PAIRS 0x400
 
 /*
  * One registered layer view, i.e. one span of every packed block. A packed

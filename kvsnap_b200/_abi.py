@@ -12,11 +12,13 @@ DP_ABI_VERSION = 1
 POOL_ABI_VERSION = 2
 IO_ABI_VERSION = 1
 
-MISALIGNED, BAD_BLOCK, CRC_MISMATCH = 1, 2, 4
+MISALIGNED, BAD_BLOCK, CRC_MISMATCH, BAD_PAIR = 1, 2, 4, 8
 # OR into a kernel's `vec` when every packed address is device memory.
 HBM = 0x100
 RUNS = 0x200            # with HBM: spans of at most RUNS_SPAN_BYTES fold in runs
 RUNS_SPAN_BYTES = 8 << 10
+PAIRS = 0x400           # with RUNS: spans all of one size in PAIR_SPAN_BYTES, an even count: units of two spans
+PAIR_SPAN_BYTES = (2 << 10, 4 << 10)
 
 
 class Span(C.Structure):

@@ -270,6 +270,7 @@ struct SpanArgs {
     uint32_t* crc;           // raw XOR accumulators, zeroed before launch, or null
     const uint32_t* gate;    // scatter: skip all writes when *gate != 0
     uint32_t* status;
+    int pairs = 0;           // runs of segment kernels: units are pairs of spans (KVSNAP_DP_PAIRS)
 };
 
 template <int VEC, int MODE>
@@ -525,7 +526,9 @@ struct alignas(16) SegUnit {
     int64_t block;       // the packed block it belongs to (its CRC accumulator)
     uint32_t shift;      // x^(8 * bytes after the unit in its packed block)
     int32_t steps;       // seg / kSegLine
-    int32_t span;        // position of the unit in its block (span, or piece), for runs and the tail mask
+    int32_t span;        // position of the unit in its block (span, pair or piece), for runs and the tail mask
+    int64_t alt;         // the cache-side base of lines 16..31: the second span of a pair, less S; else
+                         // the same base as lines 0..15
 };
 // The load side is at most kSegDepth steps, so at most kSegDepth + 1 units
 // (it moves on to the next unit as soon as it issues a unit's last step),
@@ -575,11 +578,14 @@ struct SpanUnits {
     int64_t i, left;     // packed block of the cursor, and units left to walk
     int64_t di;          // block step (grid-stride)
     int s, ds;           // span of the cursor, and its step (grid-stride)
+    int width;           // spans a unit: 2 for pairs (RANGE only), else 1
     __device__ SpanUnits(const SpanArgs& args, int64_t w, int64_t warps) : a(args) {
-        const int64_t count = args.n * args.nspans;
+        width = RANGE && args.pairs ? 2 : 1;
+        const int per_block = args.nspans / width;
+        const int64_t count = args.n * per_block;
         const int64_t begin = RANGE ? count * w / warps : w;
-        i = begin / args.nspans;
-        s = int(begin - i * args.nspans);
+        i = begin / per_block;
+        s = int(begin - i * per_block) * width;
         di = warps / args.nspans;
         ds = int(warps - di * args.nspans);
         left = RANGE ? count * (w + 1) / warps - begin : (begin < count ? (count - begin + warps - 1) / warps : 0);
@@ -587,7 +593,7 @@ struct SpanUnits {
     __device__ __forceinline__ void step() {
         --left;
         if (RANGE) {
-            if (++s == a.nspans) {
+            if ((s += width) == a.nspans) {
                 s = 0;
                 ++i;
             }
@@ -608,21 +614,40 @@ struct SpanUnits {
                 if (lane == 0) flag(a.status, KVSNAP_DP_BAD_BLOCK);
                 continue;
             }
-            const int64_t bytes = sp.bytes;
+            int64_t bytes = sp.bytes;
             const int64_t packed = a.packed[i] + sp.offset;
             const int64_t cache = sp.base + block * sp.pitch;
+            int64_t second = cache;      // the cache-side base of lines 16..31
+            uint32_t shift = sp.crc_shift;
+            if (width == 2) {            // the pair's second span follows in the packed block
+                const kvsnap_span& sq = a.spans[s + 1];
+                uint32_t bad = 0;
+                if (sq.bytes != bytes || sq.offset != sp.offset + bytes || (2 * bytes) % (32 * kSegLine))
+                    bad |= KVSNAP_DP_BAD_PAIR;
+                if (block >= sq.nblocks) bad |= KVSNAP_DP_BAD_BLOCK;
+                const int64_t other = sq.base + block * sq.pitch;
+                if (other & 15) bad |= KVSNAP_DP_MISALIGNED;
+                if (bad) {
+                    if (lane == 0) flag(a.status, bad);
+                    continue;
+                }
+                second = other - bytes;
+                shift = sq.crc_shift;
+                bytes *= 2;
+            }
             if ((packed | cache | bytes) & 15) {
                 if (lane == 0) flag(a.status, KVSNAP_DP_MISALIGNED);
                 continue;
             }
             out.src = reinterpret_cast<const char*>(MODE == kGather ? cache : packed);
             out.dst = reinterpret_cast<char*>(MODE == kGather ? packed : cache);
+            out.alt = second;
             out.seg = seg_bytes(bytes);
             out.pad = 32 * out.seg - bytes;
             out.block = i;
-            out.shift = sp.crc_shift;
+            out.shift = shift;
             out.steps = int32_t(out.seg / kSegLine);
-            out.span = s;
+            out.span = s / width;
             step();
             return true;
         }
@@ -648,6 +673,7 @@ struct PieceUnits {
             }
             out.src = reinterpret_cast<const char*>(base);
             out.dst = nullptr;
+            out.alt = base;
             out.seg = seg_bytes(len);
             out.pad = 32 * out.seg - len;
             out.block = i;
@@ -665,7 +691,9 @@ struct PieceUnits {
 // unit's share XORed into crc_out[block]), the last block's tail masked (TAIL).
 // Lane l issues, in every step, the 16-byte slot (l & 7) of lines 4j + (l >> 3),
 // j = 0..7; `buf` is the warp's line buffer, `ring` its unit descriptions.
-template <bool STORE, bool CRC, bool TAIL, bool RUNS, class Units>
+// ALT (runs): the cache side of lines 16..31, the loads' (1, gather) or the
+// stores' (2, scatter), is addressed from the unit's `alt` base.
+template <bool STORE, bool CRC, bool TAIL, bool RUNS, int ALT = 0, class Units>
 __device__ __forceinline__ void warp_stream(Units units, const RepTables& tl, const uint32_t* t4,
                                             const AppendBytes& append, uint4* buf, SegUnit* ring, int lane,
                                             uint32_t* crc_out, const kvsnap_span* spans, int valid) {
@@ -696,7 +724,8 @@ __device__ __forceinline__ void warp_stream(Units units, const RepTables& tl, co
         if (!loading) return false;
         const int64_t first = row * L.seg + 16 * slot - L.pad + int64_t(lt) * kSegLine;
 #pragma unroll
-        for (int j = 0; j < 8; ++j) v[j] = seg_load(L.src, first + 4 * j * L.seg);
+        for (int j = 0; j < 8; ++j)
+            v[j] = seg_load(ALT == 1 && j >= 4 ? reinterpret_cast<const char*>(L.alt) : L.src, first + 4 * j * L.seg);
         if (++lt == L.steps) {
             lt = 0;
             loading = units.next(L, lane);
@@ -720,7 +749,7 @@ __device__ __forceinline__ void warp_stream(Units units, const RepTables& tl, co
         for (int j = 0; j < 8; ++j) {
             const int64_t at = first + 4 * j * P.seg;   // the front padding can cover whole segments
             if (TAIL && at >= 0) v[j] = mask.apply(v[j], at, sp, valid);
-            if (STORE && at >= 0) seg_store(P.dst, at, v[j]);
+            if (STORE && at >= 0) seg_store(ALT == 2 && j >= 4 ? reinterpret_cast<char*>(P.alt) : P.dst, at, v[j]);
             if (CRC) {
                 const int line = 4 * j + row;
                 buf[line * 8 + (slot ^ (line & 7))] = v[j];
@@ -805,8 +834,9 @@ __global__ void __launch_bounds__(kSegThreads, 1) span_kernel_hbm(SpanArgs a) {
     uint32_t *t4 = sm.t4, *tx = sm.tx, *tb = sm.tb;
     uint4* buf = sm.buf;
     const bool crc = a.crc != nullptr;
-    // Runs are folded with the first span's size; spans of other sizes take the multiply.
-    const int64_t span_bytes = a.spans[0].bytes >= 4 ? a.spans[0].bytes : 4;
+    // Runs are folded with the first unit's size (a pair: two spans); units of other sizes take the multiply.
+    const int64_t first_bytes = (RUNS && a.pairs ? 2 : 1) * a.spans[0].bytes;
+    const int64_t span_bytes = first_bytes >= 4 ? first_bytes : 4;
     if (crc) {
         load_seg_tables(tb, t4);
         if (RUNS) load_append_table(tx, span_bytes);
@@ -820,8 +850,8 @@ __global__ void __launch_bounds__(kSegThreads, 1) span_kernel_hbm(SpanArgs a) {
         warp_stream<true, false, TAIL, false>(SpanUnits<MODE, false>(a, w, warps), tl, t4, append, buf, ring, lane,
                                               nullptr, a.spans, a.valid);
     else
-        warp_stream<true, true, TAIL, RUNS>(SpanUnits<MODE, RUNS>(a, w, warps), tl, t4, append, buf, ring, lane,
-                                            a.crc, a.spans, a.valid);
+        warp_stream<true, true, TAIL, RUNS, RUNS ? (MODE == kGather ? 1 : 2) : 0>(
+            SpanUnits<MODE, RUNS>(a, w, warps), tl, t4, append, buf, ring, lane, a.crc, a.spans, a.valid);
 }
 
 __global__ void __launch_bounds__(kSegThreads, 1) crc_kernel_hbm(const int64_t* addrs, int64_t n,
@@ -1260,9 +1290,11 @@ int launch_spans(const kvsnap_span* spans, int nspans, uint64_t block_bytes, con
                  const uint32_t* gate, uint32_t* status, int vec, int ctas, uintptr_t stream) {
     return guarded([&] {
         const bool hbm = (vec & KVSNAP_DP_HBM) != 0;
-        const bool runs = (vec & KVSNAP_DP_RUNS) != 0;
-        vec &= ~(KVSNAP_DP_HBM | KVSNAP_DP_RUNS);
+        const bool runs = (vec & KVSNAP_DP_RUNS) != 0, pairs = (vec & KVSNAP_DP_PAIRS) != 0;
+        vec &= ~(KVSNAP_DP_HBM | KVSNAP_DP_RUNS | KVSNAP_DP_PAIRS);
         if (n < 0 || nspans <= 0 || !spans) throw Fail{"invalid span table"};
+        if (pairs && (!hbm || !runs)) throw Fail{"pairs of spans need KVSNAP_DP_HBM and KVSNAP_DP_RUNS"};
+        if (pairs && nspans % 2) throw Fail{"pairs of spans need an even span count"};
         if (vec != 16 && vec != 8) throw Fail{"vector width must be 16 or 8"};
         if (hbm && vec != 16) throw Fail{"the device-memory kernels need 16-byte alignment"};
         if (n == 0) return;
@@ -1271,7 +1303,7 @@ int launch_spans(const kvsnap_span* spans, int nspans, uint64_t block_bytes, con
         const int sms = enter_stream(stream);
         cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
         if (crc) check(cudaMemsetAsync(crc, 0, sizeof(uint32_t) * size_t(n), s));
-        SpanArgs a{spans, nspans, blocks, packed, n, valid, crc, gate, status};
+        SpanArgs a{spans, nspans, blocks, packed, n, valid, crc, gate, status, pairs ? 1 : 0};
         if (hbm) {
             auto grid_of = [&](int64_t blocks_of_work, int warps) {
                 const int64_t want = (blocks_of_work * nspans + warps - 1) / warps;
@@ -1338,7 +1370,7 @@ extern "C" int kvsnap_dp_crc32c(const int64_t* addrs, int64_t n, uint64_t block_
                                 const uint32_t* expect, uint32_t* status, int vec, int ctas, uintptr_t stream) {
     return guarded([&] {
         const bool hbm = (vec & KVSNAP_DP_HBM) != 0;
-        vec &= ~(KVSNAP_DP_HBM | KVSNAP_DP_RUNS);      // whole blocks: the hint has no use here
+        vec &= ~(KVSNAP_DP_HBM | KVSNAP_DP_RUNS | KVSNAP_DP_PAIRS);   // whole blocks: the hints have no use here
         if (n < 0 || vec != 16 && vec != 8) throw Fail{"invalid CRC request"};
         if (n == 0) return;
         if (!addrs || !crc_out || block_bytes == 0) throw Fail{"CRC needs addresses, output and a block size"};

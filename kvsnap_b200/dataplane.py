@@ -509,10 +509,14 @@ class TorchBlockDataPlane:
                 raise RuntimeError("packed block size disagrees with the registered layers")
             host = torch.frombuffer(bytearray(bytes(spans)), dtype=torch.uint8)
             self._span_vec = vec
-            # Device-side copies may use the segment-lane HBM kernels; small spans fold in runs.
+            # Device-side copies may use the segment-lane HBM kernels; small spans fold in runs,
+            # 2 or 4 KiB spans of one size in pairs.
             self._hbm = _abi.HBM if vec == 16 else 0
             if self._hbm and max(layer["bytes"] for layer in self.layers) <= _abi.RUNS_SPAN_BYTES:
                 self._hbm |= _abi.RUNS
+                sizes = {layer["bytes"] for layer in self.layers}
+                if len(sizes) == 1 and sizes.pop() in _abi.PAIR_SPAN_BYTES and len(self.layers) % 2 == 0:
+                    self._hbm |= _abi.PAIRS
             self._min_blocks = min(t.shape[0] for t in self.caches.values())
             self._span_table = host.to(self._device())
             # Side streams: restores that read pinned memory in place run on their
@@ -649,6 +653,8 @@ class TorchBlockDataPlane:
             raise RuntimeError("data-plane kernel saw a block id outside its cache")
         if value & _abi.MISALIGNED:
             raise RuntimeError("data-plane kernel saw a misaligned address")
+        if value & _abi.BAD_PAIR:
+            raise RuntimeError("data-plane kernel saw a pair of spans of different sizes or apart")
         return value
 
     # ---- restore ------------------------------------------------------------------------------
