@@ -99,7 +99,7 @@ int kvsnap_pool_wait_many(void* pool, int64_t n, const uint64_t* ids);
 #define KVSNAP_DP_MISALIGNED 1u      /* an address or size broke the vector width */
 #define KVSNAP_DP_BAD_BLOCK 2u       /* a block id outside its cache */
 #define KVSNAP_DP_CRC_MISMATCH 4u    /* a block's CRC32C differed from the expected one */
-#define KVSNAP_DP_BAD_PAIR 8u        /* KVSNAP_DP_PAIRS met two spans of different sizes, or apart */
+#define KVSNAP_DP_BAD_CUT 8u         /* KVSNAP_DP_PAIRS or _SPLIT* met spans that do not cut that way */
 
 /* OR into a `vec` argument when every packed address is device memory: the
    kernels then give each lane one contiguous segment of a span, move whole
@@ -116,9 +116,18 @@ int kvsnap_pool_wait_many(void* pool, int64_t n, const uint64_t* ids);
    (a TP-8 or TP-16 shard's) and nspans is even: each unit is then a pair of
    consecutive spans, so each lane owns 2 * S / 32 contiguous packed bytes and
    a unit's CRC is placed once per 2 * S. A pair whose spans differ sets
-   KVSNAP_DP_BAD_PAIR and is skipped. Results are the same with or without
+   KVSNAP_DP_BAD_CUT and is skipped. Results are the same with or without
    it. */
 #define KVSNAP_DP_PAIRS 0x400
+/* With KVSNAP_DP_HBM, without KVSNAP_DP_RUNS: each unit is one of 2 (SPLIT2)
+   or 4 (SPLIT4) equal pieces of a span, so that large spans (a Qwen3-8B
+   layer's 32 KiB) move in 16 KiB units, which measured faster. Every span
+   must cut into pieces that are a multiple of 4 KiB; one that does not sets
+   KVSNAP_DP_BAD_CUT and is skipped. The last block of a gather with
+   valid_tokens > 0 is not split. Results are the same with or without it. */
+#define KVSNAP_DP_SPLIT2 0x800
+#define KVSNAP_DP_SPLIT4 0x1000
+#define KVSNAP_DP_SPLIT_MASK 0x1800
 
 /*
  * One registered layer view, i.e. one span of every packed block. A packed

@@ -12,13 +12,20 @@ DP_ABI_VERSION = 1
 POOL_ABI_VERSION = 2
 IO_ABI_VERSION = 1
 
-MISALIGNED, BAD_BLOCK, CRC_MISMATCH, BAD_PAIR = 1, 2, 4, 8
+MISALIGNED, BAD_BLOCK, CRC_MISMATCH, BAD_CUT = 1, 2, 4, 8
 # OR into a kernel's `vec` when every packed address is device memory.
 HBM = 0x100
 RUNS = 0x200            # with HBM: spans of at most RUNS_SPAN_BYTES fold in runs
 RUNS_SPAN_BYTES = 8 << 10
 PAIRS = 0x400           # with RUNS: spans all of one size in PAIR_SPAN_BYTES, an even count: units of two spans
 PAIR_SPAN_BYTES = (2 << 10, 4 << 10)
+SPLIT2, SPLIT4 = 0x800, 0x1000   # with HBM, without RUNS: units of 1/2 or 1/4 of a span
+SPLIT_PIECE_BYTES = 16 << 10     # the unit size the plane splits large spans of one size into
+
+
+def split_flag(span_bytes):
+    """The KVSNAP_DP_SPLIT* flag that cuts spans of ``span_bytes`` into SPLIT_PIECE_BYTES, or 0."""
+    return {2: SPLIT2, 4: SPLIT4}.get(span_bytes // SPLIT_PIECE_BYTES, 0) if span_bytes % SPLIT_PIECE_BYTES == 0 else 0
 
 
 class Span(C.Structure):

@@ -72,8 +72,10 @@ __host__ __device__ constexpr uint32_t gf_xpow8n(uint64_t n) {
 // Tables: slots 0..15 hold T_0..T_15, slots 16..19 T_492..T_495 (moving a lane's
 // register 496 bytes ahead), slots 20..23 T_244..T_247 (the same for 8-byte
 // vectors).
+// Slots 24..27 hold T_124..T_127 (a word, then the 124 bytes to the same word of
+// the next 128-byte line: the segment kernels' chains).
 struct CrcTables {
-    uint32_t t[24][256];
+    uint32_t t[28][256];
 };
 
 constexpr CrcTables make_tables() {
@@ -91,6 +93,10 @@ constexpr CrcTables make_tables() {
             r.t[16 + j][v] = gf_mulmod(r.t[0][v], far16);
             r.t[20 + j][v] = gf_mulmod(r.t[0][v], far8);
         }
+    }
+    const uint32_t line = gf_xpow8n(124);
+    for (int j = 0; j < 4; ++j) {
+        for (int v = 0; v < 256; ++v) r.t[24 + j][v] = gf_mulmod(r.t[j][v], line);
     }
     return r;
 }
@@ -271,6 +277,8 @@ struct SpanArgs {
     const uint32_t* gate;    // scatter: skip all writes when *gate != 0
     uint32_t* status;
     int pairs = 0;           // runs of segment kernels: units are pairs of spans (KVSNAP_DP_PAIRS)
+    int split = 0;           // grid-stride segment kernels: units are 1 / 2^split of a span (KVSNAP_DP_SPLIT*)
+    int place = 0;           // grid-stride segment kernels: placement tables follow the line buffers
 };
 
 template <int VEC, int MODE>
@@ -322,26 +330,27 @@ __global__ void __launch_bounds__(256) span_kernel(SpanArgs a) {
 //     (fully coalesced);
 //   * each lane owns one contiguous segment of the unit, so its register runs
 //     straight through its bytes with no jump between steps.
-// A unit of `len` bytes is front-padded with zeros to 32 equal segments of S
-// bytes, S a multiple of 128 (a zero prefix leaves a zero-started raw CRC as
-// is). Step t moves line t of every segment: the warp loads the 32 lines
-// coalesced, stores them to the destination, and writes them to a 4 KiB
-// per-warp buffer in shared memory; then lane l reads its own line back and
-// folds it in. The buffer is XOR-swizzled (16-byte slot s of line L lives at
-// slot s ^ (L & 7)), so the coalesced writes and the line-per-lane reads are
-// both free of bank conflicts.
-// A lane keeps four independent CRC chains, one per 32-bit word of each
-// 16-byte vector: chain k folds word k and then 12 zero bytes (the other
-// chains' words), which is slicing-by-4 with T_12..T_15. Four chains give the
-// lookup latency four times the work to hide behind. At the end of a unit the
-// lane's segment satisfies raw(seg) * x^96 = c0 x^96 + c1 x^64 + c2 x^32 + c3,
-// so every accumulated block CRC carries one factor x^96, which the finish
-// step divides out. The four tables are replicated once per lane (entry (k, v)
-// of lane l lies in bank l), so the lookups never conflict. One CTA per SM:
-// 128 KiB of tables and a 4 KiB line buffer per warp.
-constexpr int kRepWords = 4 * 256 * 32;                 // replicated T_12..T_15
-constexpr int kSegLine = 128;                           // bytes of a segment per step
-constexpr int kSegStep = 32 * kSegLine;                 // bytes a warp moves per step
+// A unit of `len` bytes is front-padded with zeros to 4 equal segments of S
+// bytes, S a multiple of 1 KiB (a zero prefix leaves a zero-started raw CRC as
+// is). Lanes 8r..8r+7 own segment r: in step t, load j of lane (r, s) moves
+// 16-byte slot s of line 8t + j of segment r, so each load instruction moves
+// four whole lines, each step 1 KiB of every segment straight through, and
+// every lane's bytes arrive in its own registers in stream order: nothing is
+// transposed through shared memory.
+// A lane keeps four independent CRC chains, one per 32-bit word of its
+// 16-byte slot: chain k folds word k of a line and then the 124 bytes up to
+// the same word of the next line, which is slicing-by-4 with T_124..T_127.
+// Four chains give the lookup latency four times the work to hide behind. At
+// the end of a unit, Horner over the chains, ((c0 x^32 + c1) x^32 + c2) x^32
+// + c3, and the lane's place, x^(8 * (16 * (7 - s) + S * (3 - r))), sum over
+// the warp to raw(unit) * x^(8 * 124), a constant factor that the finish step
+// divides out. The four tables are replicated once per lane (entry (k, v) of
+// lane l lies in bank l), so the lookups never conflict. One CTA per SM holds
+// 128 KiB of them.
+constexpr int kRepWords = 4 * 256 * 32;                 // replicated T_124..T_127
+constexpr int kSegLine = 128;                           // bytes of a line
+constexpr int kSegStepLines = 8;                        // lines of each segment a step moves
+constexpr int kSegStep = 4 * kSegStepLines * kSegLine;  // bytes a warp moves per step (4 KiB)
 // Warps a CTA and steps of loads in flight a warp: build-time tuning knobs.
 // kSegWarps sizes the register budget and the largest shared-memory layout; a
 // launch may use fewer warps (the kernels read their count from blockDim). On
@@ -366,23 +375,23 @@ constexpr int kSegDepth = KVSNAP_SEG_DEPTH;
 constexpr int kSegThreads = 32 * kSegWarps;
 
 // Replicated layout, 256 bytes an entry so one byte permute forms an address:
-// entry v of T_{15-(2h+p)} for lane l lies at byte h*65536 + v*256 + p*128 + 4l,
+// entry v of T_{127-(2h+p)} for lane l lies at byte h*65536 + v*256 + p*128 + 4l,
 // which puts every lane in its own bank whatever v is.
 __device__ __forceinline__ void load_rep_tables(uint32_t* tb) {
     for (int i = threadIdx.x; i < kRepWords; i += blockDim.x) {
         const int h = i >> 14, v = (i >> 6) & 255, p = (i >> 5) & 1;
-        tb[i] = g_tables.t[15 - (2 * h + p)][v];
+        tb[i] = g_tables.t[27 - (2 * h + p)][v];   // slot 27 - q holds T_{127-q}
     }
 }
 
-// The replicated T_12..T_15 and one plain copy of T_0..T_3.
+// The replicated T_124..T_127 and one plain copy of T_0..T_3.
 __device__ __forceinline__ void load_seg_tables(uint32_t* tb, uint32_t* t4) {
     load_rep_tables(tb);
     for (int i = threadIdx.x; i < 4 * 256; i += blockDim.x) t4[i] = g_tables.t[i >> 8][i & 255];
 }
 
 // The factor the segment kernels leave on every block's raw CRC, inverted.
-constexpr uint32_t kSegUnscale = gf_xpow_neg8n(12);
+constexpr uint32_t kSegUnscale = gf_xpow_neg8n(124);
 
 // The replicated tables as a lane sees them: the shared base and 4 * lane.
 struct RepTables {
@@ -394,8 +403,8 @@ struct RepTables {
     }
 };
 
-// r <- raw(r, the 4 bytes of w then 12 zero bytes), little-endian byte order:
-// T_15[x0] ^ T_14[x1] ^ T_13[x2] ^ T_12[x3] for x = r ^ w.
+// r <- raw(r, the 4 bytes of w then 124 zero bytes), little-endian byte order:
+// T_127[x0] ^ T_126[x1] ^ T_125[x2] ^ T_124[x3] for x = r ^ w.
 __device__ __forceinline__ uint32_t crc_word(const RepTables& tl, uint32_t r, uint32_t w) {
     const uint32_t x = r ^ w;
     return tl.at(0, x, 0x5504) ^ tl.at(128, x, 0x5514) ^ tl.at(65536, x, 0x5524) ^ tl.at(65536 + 128, x, 0x5534);
@@ -411,8 +420,17 @@ struct Chains {
     }
 };
 
-// Segment bytes S for a unit of `len` bytes.
-__device__ __forceinline__ int64_t seg_bytes(int64_t len) { return (len + kSegStep - 1) / kSegStep * kSegLine; }
+// Segment bytes S for a unit of `len` bytes: whole steps of 8 lines.
+__device__ __forceinline__ int64_t seg_bytes(int64_t len) { return (len + kSegStep - 1) / kSegStep * (kSegStep / 4); }
+
+// Bytes of one step of one segment.
+constexpr int kSegStepSeg = kSegStepLines * kSegLine;
+
+// The place of lane (row, slot)'s bytes in a unit of 4 segments of `seg` bytes,
+// as the exponent n of x^(8n) that puts them there.
+__host__ __device__ constexpr uint64_t lane_place(int64_t seg, int lane) {
+    return uint64_t(16 * (7 - (lane & 7))) + uint64_t(seg) * uint64_t(3 - (lane >> 3));
+}
 
 // Token-slot test of the save's last block: the bytes at span offset `at` belong
 // to token slot (at / token_pitch) % tokens, which is >= valid exactly when
@@ -468,17 +486,27 @@ __device__ __forceinline__ uint32_t combine_chains(const Chains& r, const uint32
     return mul_x32(t4, h) ^ r.c[3];
 }
 
-// x^(8*S*(31-lane)), which moves a lane's segment to its place in a unit of 32
-// segments of S bytes; recomputed only when S changes.
+// x^(8 * lane_place(S, lane)), which moves a lane's chains to their place in a
+// unit of 4 segments of S bytes; recomputed only when S changes.
+// With `after` > 0 (a piece of a split span, `after` pieces of 4 * S bytes
+// following it), times x^(8 * 4 * S * after), cached per value of `after`.
 struct LaneShift {
     int64_t seg = -1;
-    uint32_t k = 0;
-    __device__ __forceinline__ uint32_t factor(int64_t s, int lane) {
+    uint32_t k = 0, k1 = 0, k2 = 0, k3 = 0;
+    uint32_t known = 0;          // bit a: the factor for after = a is cached
+    __device__ __forceinline__ uint32_t factor(int64_t s, int lane, int after = 0) {
         if (s != seg) {
             seg = s;
-            k = dev_xpow8n(uint64_t(s) * uint64_t(31 - lane));
+            k = dev_xpow8n(lane_place(s, lane));
+            known = 1;
         }
-        return k;
+        if (after == 0) return k;
+        if (!(known >> after & 1)) {
+            const uint32_t f = gf_mulmod(k, dev_xpow8n(uint64_t(4 * s) * uint64_t(after)));
+            if (after == 1) k1 = f; else if (after == 2) k2 = f; else k3 = f;
+            known |= 1u << after;
+        }
+        return after == 1 ? k1 : after == 2 ? k2 : k3;
     }
 };
 
@@ -497,6 +525,79 @@ struct AppendBytes {
 __device__ __forceinline__ void load_append_table(uint32_t* tx, int64_t m) {
     const uint32_t f = dev_xpow8n(uint64_t(m - 4));
     for (int i = threadIdx.x; i < 4 * 256; i += blockDim.x) tx[i] = gf_mulmod(g_tables.t[i >> 8][i & 255], f);
+}
+
+// ---- placing a unit by table ------------------------------------------------------
+//
+// Without runs every unit ends with two products: each lane's segment value by
+// its placement factor F_l = x^(8 * lane_place(seg, l)), and the warp's sum by the
+// unit's shift x^(8 * bytes after it in its block). A GF(2) multiply loop is 32
+// dependent steps; both products go through shared tables instead, built once
+// a CTA, when the unit has the segment size and a position the tables hold.
+//
+// Window table (8 KiB): win[(4j + v)*32 + l] = (v << 2j) * F_l. A lane's
+// product is the XOR of sixteen lookups, one a 2-bit window of its value, each
+// in the lane's own bank.
+// Shift table: sh[33r + l] = shift_r * x^l for row r = (span << split) +
+// piece, shift_r = x^(8 * bytes after that unit in its block). Bit k of a value
+// stands for x^(31-k), so for a warp-uniform y, y * shift_r = XOR over lanes l
+// of (bit 31-l of y) * sh[33r + l]: one lookup a lane and a warp XOR.
+//
+// The tables are used only where the CTA's shared memory stays within
+// kSegCarveBytes. The SM splits 256 KiB between shared memory and L1 in steps;
+// above 196 KiB of shared memory (less 1 KiB the CTA reserves) L1 falls from
+// 60 to 28 KiB, too little for the loads a CTA keeps in flight: the same
+// kernel with 200 KiB requested measured 13 % slower.
+constexpr int kWinWords = 16 * 4 * 32;
+constexpr int kShiftPitch = 33;          // words a position: 32, and one so rows start in other banks
+constexpr int kSegCarveBytes = 195 * 1024;
+
+__host__ __device__ constexpr int place_bytes(int positions) { return (kWinWords + positions * kShiftPitch) * 4; }
+
+// r * x, reflected: one step of a GF(2) multiply loop.
+__device__ __forceinline__ uint32_t gf_mulx(uint32_t r) { return (r >> 1) ^ (kPoly & (0u - (r & 1u))); }
+
+struct Placement {
+    const char* win = nullptr;      // the window table + 4 * lane; null: no tables
+    const uint32_t* sh = nullptr;   // the shift table
+    int64_t seg = -1;               // the segment size the window table was built for
+    int split = 0;                  // log2 of the units a span: rows are (span << split) + piece
+};
+
+// Window table for segment size seg. Window j of lane l covers bits 2j and
+// 2j+1, which stand for x^(31-2j) and x^(30-2j) times F_l.
+__device__ void build_windows(uint32_t* win, int64_t seg) {
+    for (int e = threadIdx.x; e < 16 * 32; e += blockDim.x) {
+        const int j = e >> 5, l = e & 31;
+        uint32_t b1 = dev_xpow8n(lane_place(seg, l));
+        for (int k = 0; k < 30 - 2 * j; ++k) b1 = gf_mulx(b1);
+        const uint32_t b0 = gf_mulx(b1);
+        win[(4 * j + 0) * 32 + l] = 0u;
+        win[(4 * j + 1) * 32 + l] = b0;
+        win[(4 * j + 2) * 32 + l] = b1;
+        win[(4 * j + 3) * 32 + l] = b0 ^ b1;
+    }
+}
+
+// Shift table rows 0..count-1; shift_of(r) gives row r's x^(8 * bytes after its unit).
+template <class ShiftOf>
+__device__ void build_shifts(uint32_t* sh, int count, ShiftOf shift_of) {
+    for (int s = threadIdx.x; s < count; s += blockDim.x) {
+        uint32_t b = shift_of(s);
+        for (int l = 0; l < 32; ++l) {
+            sh[kShiftPitch * s + l] = b;
+            b = gf_mulx(b);
+        }
+    }
+}
+
+// a * F_lane through the window table (win already offset by 4 * lane).
+__device__ __forceinline__ uint32_t window_mul(const char* win, uint32_t a) {
+    uint32_t r = 0;
+#pragma unroll
+    for (int j = 0; j < 16; ++j)
+        r ^= *reinterpret_cast<const uint32_t*>(win + 512 * j + 128 * ((a >> (2 * j)) & 3u));
+    return r;
 }
 
 // ---- a warp's stream of units --------------------------------------------------
@@ -521,14 +622,15 @@ __device__ __forceinline__ void load_append_table(uint32_t* tx, int64_t m) {
 struct alignas(16) SegUnit {
     const char* src;
     char* dst;
-    int64_t seg;         // bytes a lane owns, a multiple of kSegLine
+    int64_t seg;         // bytes of each of the unit's 4 segments, a multiple of kSegStepSeg
     int64_t pad;         // zero bytes in front of the unit
     int64_t block;       // the packed block it belongs to (its CRC accumulator)
     uint32_t shift;      // x^(8 * bytes after the unit in its packed block)
-    int32_t steps;       // seg / kSegLine
+    int32_t steps;       // seg / kSegStepSeg
     int32_t span;        // position of the unit in its block (span, pair or piece), for runs and the tail mask
-    int64_t alt;         // the cache-side base of lines 16..31: the second span of a pair, less S; else
-                         // the same base as lines 0..15
+    int32_t after;       // pieces after this one in its span (a split span), else 0
+    int64_t alt;         // the cache-side base of segments 2 and 3: the second span of a pair, less
+                         // its size; else the same base as segments 0 and 1
 };
 // The load side is at most kSegDepth steps, so at most kSegDepth + 1 units
 // (it moves on to the next unit as soon as it issues a unit's last step),
@@ -538,17 +640,22 @@ static_assert(kRing >= kSegDepth + 2 && (kRing & (kRing - 1)) == 0, "ring of uni
 
 // Dynamic shared memory of a segment kernel of `warps` warps, in order: the
 // unit rings, T_0..T_3 (the chain combine) and, for runs, the append table,
-// the replicated tables, one line buffer a warp. It is sized to the launch:
-// shared memory and L1 split one 256 KiB array a SM, and what L1 keeps holds
-// the loads in flight. Without the four unused line buffers and the append
-// table, 8-warp gathers measured 2 % and whole-block CRCs 6 % faster; a 200 KiB
-// layout (L1 at 28 KiB) measured 13 % slower.
+// then the replicated tables. It is sized to the launch: shared memory and L1
+// split one 256 KiB array a SM, and what L1 keeps holds the loads in flight
+// (a 200 KiB layout, which leaves 28 KiB of L1 instead of 60, measured 13 %
+// slower).
 __host__ __device__ constexpr int seg_ring_bytes(int warps) { return warps * kRing * int(sizeof(SegUnit)); }
 __host__ __device__ constexpr int seg_smem_bytes(int warps, bool runs) {
-    return seg_ring_bytes(warps) + (runs ? 2 : 1) * 4 * 256 * 4 + kRepWords * 4 + warps * kSegStep;
+    return seg_ring_bytes(warps) + (runs ? 2 : 1) * 4 * 256 * 4 + kRepWords * 4;
 }
 constexpr int kSegSmemTotal = seg_smem_bytes(kSegWarps, true);
 static_assert(kSegSmemTotal <= 227 * 1024, "segment kernels exceed the shared memory of a CTA");
+// Rows of placement tables a grid-stride CTA of `warps` warps can hold after its line buffers.
+__host__ __device__ constexpr int place_rows(int warps) {
+    return (kSegCarveBytes - seg_smem_bytes(warps, false) - kWinWords * 4) / (kShiftPitch * 4);
+}
+constexpr int kSegSmemMax = kSegSmemTotal > kSegCarveBytes ? kSegSmemTotal : kSegCarveBytes;
+static_assert(kSegSmemMax <= 227 * 1024, "segment kernels exceed the shared memory of a CTA");
 
 // A warp's view of that layout.
 struct SegSmem {
@@ -556,13 +663,11 @@ struct SegSmem {
     uint32_t* t4;        // T_0..T_3
     uint32_t* tx;        // the append table (runs only)
     uint32_t* tb;        // the replicated tables
-    uint4* buf;          // its line buffer
     __device__ SegSmem(uint4* smem, int warp, int warps, bool runs) {
         ring = reinterpret_cast<SegUnit*>(smem) + warp * kRing;
         t4 = reinterpret_cast<uint32_t*>(smem + seg_ring_bytes(warps) / 16);
         tx = t4 + 4 * 256;
         tb = t4 + (runs ? 2 : 1) * 4 * 256;
-        buf = reinterpret_cast<uint4*>(tb + kRepWords) + warp * (kSegStep / 16);
     }
 };
 
@@ -578,16 +683,23 @@ struct SpanUnits {
     int64_t i, left;     // packed block of the cursor, and units left to walk
     int64_t di;          // block step (grid-stride)
     int s, ds;           // span of the cursor, and its step (grid-stride)
+    int p, dp;           // piece of the cursor in its span, and its step (grid-stride)
     int width;           // spans a unit: 2 for pairs (RANGE only), else 1
+    int split;           // log2 of the units a span (grid-stride only), else 0
     __device__ SpanUnits(const SpanArgs& args, int64_t w, int64_t warps) : a(args) {
         width = RANGE && args.pairs ? 2 : 1;
-        const int per_block = args.nspans / width;
+        split = RANGE ? 0 : args.split;
+        const int per_block = args.nspans / width << split;
         const int64_t count = args.n * per_block;
         const int64_t begin = RANGE ? count * w / warps : w;
         i = begin / per_block;
-        s = int(begin - i * per_block) * width;
-        di = warps / args.nspans;
-        ds = int(warps - di * args.nspans);
+        const int at = int(begin - i * per_block);
+        s = (at >> split) * width;
+        p = at & ((1 << split) - 1);
+        const int64_t spans_step = warps >> split;   // the grid stride in whole spans, and dp pieces
+        dp = int(warps & ((1 << split) - 1));
+        di = spans_step / args.nspans;
+        ds = int(spans_step - di * args.nspans);
         left = RANGE ? count * (w + 1) / warps - begin : (begin < count ? (count - begin + warps - 1) / warps : 0);
     }
     __device__ __forceinline__ void step() {
@@ -600,6 +712,10 @@ struct SpanUnits {
         } else {
             i += di;
             s += ds;
+            if ((p += dp) >> split) {
+                p -= 1 << split;
+                ++s;
+            }
             if (s >= a.nspans) {
                 s -= a.nspans;
                 ++i;
@@ -614,16 +730,20 @@ struct SpanUnits {
                 if (lane == 0) flag(a.status, KVSNAP_DP_BAD_BLOCK);
                 continue;
             }
-            int64_t bytes = sp.bytes;
-            const int64_t packed = a.packed[i] + sp.offset;
-            const int64_t cache = sp.base + block * sp.pitch;
+            int64_t bytes = sp.bytes >> split;
+            const int64_t packed = a.packed[i] + sp.offset + p * bytes;
+            const int64_t cache = sp.base + block * sp.pitch + p * bytes;
+            if (split && (bytes << split != sp.bytes || bytes % kSegStep)) {   // whole steps a segment, no padding
+                if (lane == 0) flag(a.status, KVSNAP_DP_BAD_CUT);
+                continue;
+            }
             int64_t second = cache;      // the cache-side base of lines 16..31
             uint32_t shift = sp.crc_shift;
             if (width == 2) {            // the pair's second span follows in the packed block
                 const kvsnap_span& sq = a.spans[s + 1];
                 uint32_t bad = 0;
-                if (sq.bytes != bytes || sq.offset != sp.offset + bytes || (2 * bytes) % (32 * kSegLine))
-                    bad |= KVSNAP_DP_BAD_PAIR;
+                if (sq.bytes != bytes || sq.offset != sp.offset + bytes || (2 * bytes) % kSegStep)
+                    bad |= KVSNAP_DP_BAD_CUT;
                 if (block >= sq.nblocks) bad |= KVSNAP_DP_BAD_BLOCK;
                 const int64_t other = sq.base + block * sq.pitch;
                 if (other & 15) bad |= KVSNAP_DP_MISALIGNED;
@@ -643,11 +763,12 @@ struct SpanUnits {
             out.dst = reinterpret_cast<char*>(MODE == kGather ? packed : cache);
             out.alt = second;
             out.seg = seg_bytes(bytes);
-            out.pad = 32 * out.seg - bytes;
+            out.pad = 4 * out.seg - bytes;
             out.block = i;
             out.shift = shift;
-            out.steps = int32_t(out.seg / kSegLine);
+            out.steps = int32_t(out.seg / kSegStepSeg);
             out.span = s / width;
+            out.after = (1 << split) - 1 - p;
             step();
             return true;
         }
@@ -675,10 +796,11 @@ struct PieceUnits {
             out.dst = nullptr;
             out.alt = base;
             out.seg = seg_bytes(len);
-            out.pad = 32 * out.seg - len;
+            out.pad = 4 * out.seg - len;
             out.block = i;
             out.shift = dev_xpow8n(uint64_t(block_bytes - at - len));
-            out.steps = int32_t(out.seg / kSegLine);
+            out.after = 0;
+            out.steps = int32_t(out.seg / kSegStepSeg);
             out.span = int32_t(p);
             u += du;
             return true;
@@ -689,14 +811,15 @@ struct PieceUnits {
 
 // One warp's stream: every unit's bytes moved (STORE) and CRC'd (CRC; the
 // unit's share XORed into crc_out[block]), the last block's tail masked (TAIL).
-// Lane l issues, in every step, the 16-byte slot (l & 7) of lines 4j + (l >> 3),
-// j = 0..7; `buf` is the warp's line buffer, `ring` its unit descriptions.
+// Lane (r, s) = (l >> 3, l & 7) moves, in step t, the 16-byte slot s of lines
+// 8t + j of segment r, j = 0..7; `ring` holds the warp's unit descriptions.
 // ALT (runs): the cache side of lines 16..31, the loads' (1, gather) or the
 // stores' (2, scatter), is addressed from the unit's `alt` base.
 template <bool STORE, bool CRC, bool TAIL, bool RUNS, int ALT = 0, class Units>
 __device__ __forceinline__ void warp_stream(Units units, const RepTables& tl, const uint32_t* t4,
-                                            const AppendBytes& append, uint4* buf, SegUnit* ring, int lane,
-                                            uint32_t* crc_out, const kvsnap_span* spans, int valid) {
+                                            const AppendBytes& append, SegUnit* ring, int lane,
+                                            uint32_t* crc_out, const kvsnap_span* spans, int valid,
+                                            const Placement& pl = Placement{}) {
     const int row = lane >> 3, slot = lane & 7;
     SegUnit L;                                   // the unit the load side is in
     if (!units.next(L, lane)) return;
@@ -719,13 +842,15 @@ __device__ __forceinline__ void warp_stream(Units units, const RepTables& tl, co
         if (lane == 0) atomicXor(&crc_out[run_block], x);
     };
 
-    // Issue the load side's next step into v and move the load side on.
-    auto load_next = [&](uint4(&v)[8]) -> bool {
-        if (!loading) return false;
-        const int64_t first = row * L.seg + 16 * slot - L.pad + int64_t(lt) * kSegLine;
-#pragma unroll
-        for (int j = 0; j < 8; ++j)
-            v[j] = seg_load(ALT == 1 && j >= 4 ? reinterpret_cast<const char*>(L.alt) : L.src, first + 4 * j * L.seg);
+    // The load side's next step: its base and offset (lane-specific) for loads j = 0..7
+    // at first + j * kSegLine; then the load side moves on.
+    const char* lbase = nullptr;
+    int64_t lfirst = 0;
+    auto load_addr = [&]() {
+        lbase = ALT == 1 && row >= 2 ? reinterpret_cast<const char*>(L.alt) : L.src;
+        lfirst = row * L.seg + 16 * slot - L.pad + int64_t(lt) * kSegStepSeg;
+    };
+    auto load_move = [&]() {
         if (++lt == L.steps) {
             lt = 0;
             loading = units.next(L, lane);
@@ -734,55 +859,60 @@ __device__ __forceinline__ void warp_stream(Units units, const RepTables& tl, co
                 if (lane == 0) ring[lk] = L;
             }
         }
+    };
+    auto load_next = [&](uint4(&v)[8]) -> bool {
+        if (!loading) return false;
+        load_addr();
+#pragma unroll
+        for (int j = 0; j < 8; ++j) v[j] = seg_load(lbase, lfirst + j * kSegLine);
+        load_move();
         return true;
     };
-    // Store the step in v and write it to the line buffer.
-    auto emit = [&](uint4(&v)[8]) {
-        const int64_t first = row * P.seg + 16 * slot - P.pad + int64_t(pt) * kSegLine;
+    // Store, fold and refill one step: for each j, line j is masked (TAIL),
+    // stored, folded into the chains, and its register refilled with the load
+    // side's next step, so the loads go out while the step is folded.
+    auto step = [&](uint4(&v)[8]) -> bool {
+        const int64_t first = row * P.seg + 16 * slot - P.pad + int64_t(pt) * kSegStepSeg;
+        char* sbase = ALT == 2 && row >= 2 ? reinterpret_cast<char*>(P.alt) : P.dst;
         TailMask mask;
         kvsnap_span sp{};
         if (TAIL) {
             sp = spans[P.span];
             mask = TailMask(sp, valid);
         }
+        const bool refill = loading;
+        if (refill) load_addr();
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
-            const int64_t at = first + 4 * j * P.seg;   // the front padding can cover whole segments
+            const int64_t at = first + j * kSegLine;     // the front padding can cover whole segments
             if (TAIL && at >= 0) v[j] = mask.apply(v[j], at, sp, valid);
-            if (STORE && at >= 0) seg_store(ALT == 2 && j >= 4 ? reinterpret_cast<char*>(P.alt) : P.dst, at, v[j]);
-            if (CRC) {
-                const int line = 4 * j + row;
-                buf[line * 8 + (slot ^ (line & 7))] = v[j];
-            }
+            if (STORE && at >= 0) seg_store(sbase, at, v[j]);
+            if (CRC) r.fold(tl, v[j]);
+            if (refill) v[j] = seg_load(lbase, lfirst + j * kSegLine);
         }
-    };
-    // Fold the lane's line of the step just buffered.
-    auto fold = [&]() {
-        __syncwarp();
-        const uint4* mine = buf + lane * 8;
-        uint4 w = mine[slot];
-#pragma unroll 1
-        for (int k = 1; k < 8; ++k) {   // one slot read ahead of the fold
-            const uint4 now = w;
-            w = mine[k ^ slot];
-            r.fold(tl, now);
-        }
-        r.fold(tl, w);
-        __syncwarp();
+        if (refill) load_move();
+        return refill;
     };
     // After a step: at the end of a unit, its CRC share goes out and the next unit comes in.
     auto advance = [&]() {
         if (++pt < P.steps) return;
         if (CRC && !RUNS) {
-            const uint32_t x = gf_mulmod(warp_xor(gf_mulmod(combine_chains(r, t4), place.factor(P.seg, lane))),
-                                         P.shift);
+            const uint32_t h = combine_chains(r, t4);
+            uint32_t x;
+            if (pl.win) {   // by table; the shift row holds the piece's place in its span
+                const uint32_t y = warp_xor(P.seg == pl.seg ? window_mul(pl.win, h) : gf_mulmod(h, place.factor(P.seg, lane)));
+                const int row = (P.span << pl.split) + ((1 << pl.split) - 1 - P.after);
+                x = warp_xor((y >> (31 - lane)) & 1u ? pl.sh[kShiftPitch * row + lane] : 0u);
+            } else {
+                x = gf_mulmod(warp_xor(gf_mulmod(h, place.factor(P.seg, lane, P.after))), P.shift);
+            }
             if (lane == 0) atomicXor(&crc_out[P.block], x);
             r = Chains{};
         }
         if (CRC && RUNS) {
             const uint32_t h = combine_chains(r, t4);
             if (run && P.block == run_block && P.span == run_pos + 1 && P.seg == run_seg) {
-                acc = append.apply(acc, 32 * P.seg - P.pad) ^ h;
+                acc = append.apply(acc, 4 * P.seg - P.pad) ^ h;
             } else {
                 if (run) flush();
                 run = true;
@@ -810,10 +940,7 @@ __device__ __forceinline__ void warp_stream(Units units, const RepTables& tl, co
 #pragma unroll
         for (int d = 0; d < kSegDepth; ++d) {
             if (pending > 0) {                   // slot d holds the oldest step in flight
-                emit(v[d]);
-                --pending;
-                if (load_next(v[d])) ++pending;  // refill before folding, so the loads overlap it
-                if (CRC) fold();
+                if (!step(v[d])) --pending;
                 advance();
             }
         }
@@ -832,14 +959,28 @@ __global__ void __launch_bounds__(kSegThreads, 1) span_kernel_hbm(SpanArgs a) {
     const SegSmem sm(smem, warp, per_cta, RUNS);
     SegUnit* ring = sm.ring;
     uint32_t *t4 = sm.t4, *tx = sm.tx, *tb = sm.tb;
-    uint4* buf = sm.buf;
     const bool crc = a.crc != nullptr;
     // Runs are folded with the first unit's size (a pair: two spans); units of other sizes take the multiply.
     const int64_t first_bytes = (RUNS && a.pairs ? 2 : 1) * a.spans[0].bytes;
     const int64_t span_bytes = first_bytes >= 4 ? first_bytes : 4;
+    Placement pl;
     if (crc) {
         load_seg_tables(tb, t4);
         if (RUNS) load_append_table(tx, span_bytes);
+        if (!RUNS && !TAIL && a.place) {   // the launcher sized shared memory for the placement tables
+            uint32_t* win = reinterpret_cast<uint32_t*>(smem + seg_smem_bytes(per_cta, false) / 16);
+            const kvsnap_span* spans = a.spans;
+            const int split = a.split;
+            const int64_t seg = seg_bytes(spans[0].bytes >> split);   // the windows: the first unit's size
+            build_windows(win, seg);
+            build_shifts(win + kWinWords, a.nspans << split, [spans, split](int r) {
+                const kvsnap_span& sp = spans[r >> split];
+                const int after = (1 << split) - 1 - (r & ((1 << split) - 1));   // pieces after it in its span
+                return after ? gf_mulmod(sp.crc_shift, dev_xpow8n(uint64_t(sp.bytes >> split) * uint64_t(after)))
+                             : sp.crc_shift;
+            });
+            pl = Placement{reinterpret_cast<const char*>(win) + 4 * lane, win + kWinWords, seg, split};
+        }
     }
     __syncthreads();
     if (MODE == kScatter && a.gate && *a.gate) return;
@@ -847,11 +988,11 @@ __global__ void __launch_bounds__(kSegThreads, 1) span_kernel_hbm(SpanArgs a) {
     const AppendBytes append{tx, span_bytes};
     const int64_t w = (int64_t)blockIdx.x * per_cta + warp, warps = (int64_t)gridDim.x * per_cta;
     if (!crc)
-        warp_stream<true, false, TAIL, false>(SpanUnits<MODE, false>(a, w, warps), tl, t4, append, buf, ring, lane,
+        warp_stream<true, false, TAIL, false>(SpanUnits<MODE, false>(a, w, warps), tl, t4, append, ring, lane,
                                               nullptr, a.spans, a.valid);
     else
         warp_stream<true, true, TAIL, RUNS, RUNS ? (MODE == kGather ? 1 : 2) : 0>(
-            SpanUnits<MODE, RUNS>(a, w, warps), tl, t4, append, buf, ring, lane, a.crc, a.spans, a.valid);
+            SpanUnits<MODE, RUNS>(a, w, warps), tl, t4, append, ring, lane, a.crc, a.spans, a.valid, pl);
 }
 
 __global__ void __launch_bounds__(kSegThreads, 1) crc_kernel_hbm(const int64_t* addrs, int64_t n,
@@ -862,14 +1003,13 @@ __global__ void __launch_bounds__(kSegThreads, 1) crc_kernel_hbm(const int64_t* 
     const SegSmem sm(smem, warp, per_cta, false);
     SegUnit* ring = sm.ring;
     uint32_t *t4 = sm.t4, *tx = sm.tx, *tb = sm.tb;     // tx: unused without runs
-    uint4* buf = sm.buf;
     load_seg_tables(tb, t4);
     __syncthreads();
     const RepTables tl{reinterpret_cast<const char*>(tb), 4u * lane};
     const AppendBytes append{tx, kSegPiece};
     const PieceUnits units{addrs, n, block_bytes, (block_bytes + kSegPiece - 1) / kSegPiece, status,
                            (int64_t)blockIdx.x * per_cta + warp, (int64_t)gridDim.x * per_cta};
-    warp_stream<false, true, false, false>(units, tl, t4, append, buf, ring, lane, crc, nullptr, 0);
+    warp_stream<false, true, false, false>(units, tl, t4, append, ring, lane, crc, nullptr, 0);
 }
 
 // CRC32C of whole packed blocks, in pieces of kPiece bytes per warp.
@@ -1291,7 +1431,9 @@ int launch_spans(const kvsnap_span* spans, int nspans, uint64_t block_bytes, con
     return guarded([&] {
         const bool hbm = (vec & KVSNAP_DP_HBM) != 0;
         const bool runs = (vec & KVSNAP_DP_RUNS) != 0, pairs = (vec & KVSNAP_DP_PAIRS) != 0;
-        vec &= ~(KVSNAP_DP_HBM | KVSNAP_DP_RUNS | KVSNAP_DP_PAIRS);
+        const int split = (vec & KVSNAP_DP_SPLIT_MASK) / KVSNAP_DP_SPLIT2;   // log2 of the pieces a span
+        vec &= ~(KVSNAP_DP_HBM | KVSNAP_DP_RUNS | KVSNAP_DP_PAIRS | KVSNAP_DP_SPLIT_MASK);
+        if (split && (!hbm || runs || split > 2)) throw Fail{"split spans need KVSNAP_DP_HBM, without KVSNAP_DP_RUNS"};
         if (n < 0 || nspans <= 0 || !spans) throw Fail{"invalid span table"};
         if (pairs && (!hbm || !runs)) throw Fail{"pairs of spans need KVSNAP_DP_HBM and KVSNAP_DP_RUNS"};
         if (pairs && nspans % 2) throw Fail{"pairs of spans need an even span count"};
@@ -1303,10 +1445,10 @@ int launch_spans(const kvsnap_span* spans, int nspans, uint64_t block_bytes, con
         const int sms = enter_stream(stream);
         cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
         if (crc) check(cudaMemsetAsync(crc, 0, sizeof(uint32_t) * size_t(n), s));
-        SpanArgs a{spans, nspans, blocks, packed, n, valid, crc, gate, status, pairs ? 1 : 0};
+        SpanArgs a{spans, nspans, blocks, packed, n, valid, crc, gate, status, pairs ? 1 : 0, split};
         if (hbm) {
             auto grid_of = [&](int64_t blocks_of_work, int warps) {
-                const int64_t want = (blocks_of_work * nspans + warps - 1) / warps;
+                const int64_t want = ((blocks_of_work * nspans << split) + warps - 1) / warps;
                 return ctas > 0 ? ctas : int(want < sms ? want : sms);
             };
 
@@ -1316,7 +1458,7 @@ int launch_spans(const kvsnap_span* spans, int nspans, uint64_t block_bytes, con
                     body = n - 1;
                     SpanArgs last{spans, nspans, blocks + body, packed + body, 1, valid, crc ? crc + body : nullptr,
                                   gate, status};
-                    configure_once(reinterpret_cast<const void*>(span_kernel_hbm<MODE, true, false>), kSegSmemTotal);
+                    configure_once(reinterpret_cast<const void*>(span_kernel_hbm<MODE, true, false>), kSegSmemMax);
                     span_kernel_hbm<MODE, true, false><<<grid_of(1, kSegWarps), kSegThreads,
                                                          crc ? seg_smem_bytes(kSegWarps, false) : seg_ring_bytes(kSegWarps),
                                                          s>>>(last);
@@ -1327,9 +1469,13 @@ int launch_spans(const kvsnap_span* spans, int nspans, uint64_t block_bytes, con
                 a.n = body;
                 auto kernel = runs ? span_kernel_hbm<MODE, false, true> : span_kernel_hbm<MODE, false, false>;
                 const int warps = runs ? kSegWarps : kSegBulkWarps;
-                configure_once(reinterpret_cast<const void*>(kernel), kSegSmemTotal);
-                kernel<<<grid_of(body, warps), 32 * warps, crc ? seg_smem_bytes(warps, runs) : seg_ring_bytes(warps),
-                         s>>>(a);
+                // Grid-stride units are placed by table when the rows fit beside the line buffers.
+                const int rows = nspans << split;
+                a.place = crc && !runs && rows <= place_rows(warps);
+                const int bytes = !crc ? seg_ring_bytes(warps)
+                                       : seg_smem_bytes(warps, runs) + (a.place ? place_bytes(rows) : 0);
+                configure_once(reinterpret_cast<const void*>(kernel), kSegSmemMax);
+                kernel<<<grid_of(body, warps), 32 * warps, bytes, s>>>(a);
                 check(cudaGetLastError());
             }
             if (crc) finish(crc, expect, n, block_bytes, status, s, kSegUnscale);
@@ -1370,7 +1516,7 @@ extern "C" int kvsnap_dp_crc32c(const int64_t* addrs, int64_t n, uint64_t block_
                                 const uint32_t* expect, uint32_t* status, int vec, int ctas, uintptr_t stream) {
     return guarded([&] {
         const bool hbm = (vec & KVSNAP_DP_HBM) != 0;
-        vec &= ~(KVSNAP_DP_HBM | KVSNAP_DP_RUNS | KVSNAP_DP_PAIRS);   // whole blocks: the hints have no use here
+        vec &= ~(KVSNAP_DP_HBM | KVSNAP_DP_RUNS | KVSNAP_DP_PAIRS | KVSNAP_DP_SPLIT_MASK);   // whole blocks: no use
         if (n < 0 || vec != 16 && vec != 8) throw Fail{"invalid CRC request"};
         if (n == 0) return;
         if (!addrs || !crc_out || block_bytes == 0) throw Fail{"CRC needs addresses, output and a block size"};
@@ -1378,7 +1524,7 @@ extern "C" int kvsnap_dp_crc32c(const int64_t* addrs, int64_t n, uint64_t block_
         cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
         check(cudaMemsetAsync(crc_out, 0, sizeof(uint32_t) * size_t(n), s));
         if (hbm && vec == 16) {
-            configure_once(reinterpret_cast<const void*>(crc_kernel_hbm), kSegSmemTotal);
+            configure_once(reinterpret_cast<const void*>(crc_kernel_hbm), kSegSmemMax);
             const int64_t want = (n * ((int64_t(block_bytes) + kPiece - 1) / kPiece) + kSegWarps - 1) / kSegWarps;
             const int grid = ctas > 0 ? ctas : int(want < sms ? want : sms);
             crc_kernel_hbm<<<grid, kSegThreads, seg_smem_bytes(kSegWarps, false), s>>>(addrs, n, int64_t(block_bytes),

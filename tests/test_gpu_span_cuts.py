@@ -1,13 +1,17 @@
-"""The device-memory kernels with pairs of spans (KVSNAP_DP_PAIRS), against the oracle.
+"""The device-memory kernels with spans cut into other units, against the oracle.
 
-When every span has one size S of 2 or 4 KiB (a TP-8 or TP-16 shard's) and
-the span count is even, the plane folds runs of units that are pairs of
-consecutive spans: each lane owns 2 * S / 32 contiguous packed bytes, lines
-0..15 of a step lie in the pair's first span and lines 16..31 in its second.
-These cases cover both sizes, token- and head-major storage, a ragged last
-block, and one or three CTAs, so that one warp walks many pairs of many
-blocks. The oracle (oracle/oracle.py) gives the packed bytes, the tail
-zeroing, the digests and the restored cache.
+Pairs (KVSNAP_DP_PAIRS): when every span has one size S of 2 or 4 KiB (a TP-8
+or TP-16 shard's) and the span count is even, the plane folds runs of units
+that are pairs of consecutive spans: each lane owns 2 * S / 32 contiguous
+packed bytes, lines 0..15 of a step lie in the pair's first span and lines
+16..31 in its second.
+Splits (KVSNAP_DP_SPLIT2 / SPLIT4): when every span has one size of 32 or
+64 KiB (a Qwen3-8B layer's), units are 16 KiB pieces of a span, and each
+piece's CRC is placed past the span's later pieces.
+These cases cover each cut, token- and head-major storage, a ragged last
+block (which is not split), and one or three CTAs, so that one warp walks many
+units of many blocks. The oracle (oracle/oracle.py) gives the packed bytes,
+the tail zeroing, the digests and the restored cache.
 """
 import numpy as np
 import pytest
@@ -22,10 +26,15 @@ BLOCKS, N = 10, 16
 
 # name: (layers, heads, width in bf16 elements, token-major storage); S = heads * N * width * 2
 SHAPES = {
-    "s4k": (16, 1, 128, False),         # S = 4 KiB (a TP-8 shard's spans): 8 KiB units, 256 B a lane
+    "s4k": (16, 1, 128, False),         # S = 4 KiB (a TP-8 shard's spans): pairs, 8 KiB units, 256 B a lane
     "s4k_tok": (6, 2, 64, True),        # the same size, token-major [B, N, H, C] storage
-    "s2k": (8, 1, 64, False),           # S = 2 KiB: 4 KiB units, one line a lane
+    "s2k": (8, 1, 64, False),           # S = 2 KiB: pairs, 4 KiB units, one line a lane
+    "s32k": (3, 8, 128, True),          # S = 32 KiB (Qwen3-8B, token-major as vLLM stores it): halves
+    "s32k_head": (4, 8, 128, False),    # the same size, head-major
+    "s64k": (2, 16, 128, False),        # S = 64 KiB: quarters
 }
+CUT = {"s4k": "PAIRS", "s4k_tok": "PAIRS", "s2k": "PAIRS", "s32k": "SPLIT2", "s32k_head": "SPLIT2",
+       "s64k": "SPLIT4"}
 
 
 def build(shape):
@@ -47,7 +56,7 @@ def build(shape):
 @pytest.mark.parametrize("shape", sorted(SHAPES))
 @pytest.mark.parametrize("ctas", [0, 1, 3])
 @pytest.mark.parametrize("tokens", [6 * N, 5 * N + 3])
-def test_span_pairs_save_and_restore(shape, ctas, tokens):
+def test_span_cuts_save_and_restore(shape, ctas, tokens):
     from kvsnap_b200 import _abi
     from kvsnap_b200.dataplane import TorchBlockDataPlane
     storages, layout, caches, tensors = build(shape)
@@ -55,7 +64,8 @@ def test_span_pairs_save_and_restore(shape, ctas, tokens):
     try:
         assert plane.block_bytes == layout.block_bytes
         plane.warm_up()
-        assert plane._hbm & _abi.PAIRS and plane._hbm & _abi.RUNS, "2 and 4 KiB spans of one size pair up"
+        assert plane._hbm & getattr(_abi, CUT[shape]), "spans of one size take their cut"
+        assert bool(plane._hbm & _abi.RUNS) == (CUT[shape] == "PAIRS")
         saved = [7, 2, 9, 0, 4, 8][: (tokens + N - 1) // N]
         expected = oracle.pack(storages, layout, saved, tokens)
         size = plane.block_bytes
@@ -105,8 +115,8 @@ def _raw(plane, ids, flags, mode="gather", sources=None):
 
 
 @pytest.mark.parametrize("shape", sorted(SHAPES))
-def test_pairs_match_runs_and_single_spans(shape):
-    """The same bytes and CRCs with pairs, with runs of single spans and with grid-stride spans, both ways."""
+def test_cuts_match_runs_and_single_spans(shape):
+    """The same bytes and CRCs with each cut the spans allow, with runs and with whole spans, both ways."""
     from kvsnap_b200 import _abi
     from kvsnap_b200.dataplane import TorchBlockDataPlane
     storages, layout, caches, tensors = build(shape)
@@ -117,8 +127,14 @@ def test_pairs_match_runs_and_single_spans(shape):
         want = oracle.pack(storages, layout, ids, len(ids) * N)
         crcs = [oracle.crc32c(b) for b in want]
         flat = np.concatenate(want)
-        for name, flags in (("spans", 16 | _abi.HBM), ("runs", 16 | _abi.HBM | _abi.RUNS),
-                            ("pairs", 16 | _abi.HBM | _abi.RUNS | _abi.PAIRS)):
+        size = layout.spans[0].bytes
+        cuts = [("spans", 16 | _abi.HBM), ("runs", 16 | _abi.HBM | _abi.RUNS)]
+        if size in _abi.PAIR_SPAN_BYTES:
+            cuts.append(("pairs", 16 | _abi.HBM | _abi.RUNS | _abi.PAIRS))
+        cuts += [(f"split{k}", 16 | _abi.HBM | flag) for k, flag in ((2, _abi.SPLIT2), (4, _abi.SPLIT4))
+                 if size % (k * 4096) == 0]
+        assert len(cuts) > 2
+        for name, flags in cuts:
             rc, status, out, crc = _raw(plane, ids, flags)
             assert rc == 0 and status == 0, name
             assert out.tobytes() == flat.tobytes() and crc == crcs, name
@@ -133,8 +149,9 @@ def test_pairs_match_runs_and_single_spans(shape):
 
 
 def test_pair_of_spans_of_two_sizes_is_flagged_not_moved():
-    """Under KVSNAP_DP_PAIRS, a pair whose spans differ sets KVSNAP_DP_BAD_PAIR and is not written,
-    while the valid pairs of the same launch are; an odd span count is refused on the host."""
+    """Under KVSNAP_DP_PAIRS, a pair whose spans differ sets KVSNAP_DP_BAD_CUT and is not written,
+    while the valid pairs of the same launch are; an odd span count, or a split with runs, is
+    refused on the host."""
     from kvsnap_b200 import _abi
     from kvsnap_b200.dataplane import TorchBlockDataPlane
 
@@ -153,7 +170,7 @@ def test_pair_of_spans_of_two_sizes_is_flagged_not_moved():
         assert plane._hbm & _abi.RUNS and not plane._hbm & _abi.PAIRS, "spans of two sizes do not pair"
         flags = 16 | _abi.HBM | _abi.RUNS | _abi.PAIRS
         rc, status, out, _ = _raw(plane, [2, 5], flags)
-        assert rc == 0 and status & _abi.BAD_PAIR
+        assert rc == 0 and status & _abi.BAD_CUT
         size = plane.block_bytes
         for i, block in enumerate((2, 5)):
             first = plane.caches["layer.0"][block].contiguous().view(torch.uint8).cpu().numpy().ravel()
@@ -166,5 +183,28 @@ def test_pair_of_spans_of_two_sizes_is_flagged_not_moved():
         plane.warm_up()
         rc, _, _, _ = _raw(plane, [2, 5], 16 | _abi.HBM | _abi.RUNS | _abi.PAIRS)
         assert rc != 0 and b"even" in plane.pool.lib.kvsnap_cuda_error()
+        rc, _, _, _ = _raw(plane, [2, 5], 16 | _abi.HBM | _abi.RUNS | _abi.SPLIT2)
+        assert rc != 0 and b"split" in plane.pool.lib.kvsnap_cuda_error()
+    finally:
+        plane.close()
+
+
+def test_split_that_leaves_padded_pieces_is_flagged_not_moved():
+    """SPLIT2 on 34 KiB spans (17 KiB pieces, not whole lines a lane) sets KVSNAP_DP_BAD_CUT and
+    writes nothing."""
+    from kvsnap_b200 import _abi
+    from kvsnap_b200.dataplane import TorchBlockDataPlane
+    caches = {}
+    for i in range(2):
+        per_block = 8 * N * 136 * 2
+        t = torch.from_numpy(kvgen.random_bytes(99 + i, BLOCKS * per_block)).cuda()
+        caches[f"layer.{i}"] = t.view(torch.bfloat16).as_strided((BLOCKS, 8, N, 136),
+                                                                 (per_block // 2, N * 136, 136, 1))
+    plane = TorchBlockDataPlane(caches, N, 64 << 20)
+    try:
+        plane.warm_up()
+        assert not plane._hbm & (_abi.SPLIT2 | _abi.SPLIT4), "34 KiB spans are not split"
+        rc, status, out, _ = _raw(plane, [4, 1], 16 | _abi.HBM | _abi.SPLIT2)
+        assert rc == 0 and status & _abi.BAD_CUT and not out.any()
     finally:
         plane.close()
