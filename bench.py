@@ -768,7 +768,7 @@ def main():
                                   "the ceiling the whole-job value shares"},
         "roofline": {"bound": "hbm", "kernel": "span_kernel_hbm<gather>: KV -> device staging, tail zero, CRC32C",
                      "achieved": round(gather_gbs, 1), "peak": hbm_peak, "unit": "GB/s",
-                     "frac": round(gather_gbs / hbm_peak, 3), "traffic": 2.367e9,
+                     "frac": round(gather_gbs / hbm_peak, 3), "traffic": 2.366e9,
                      "traffic_note": "ncu dram read+write per launch, profiles/span_kernel_hbm_gather_qwen3-8b_512-blocks.md",
                      "algorithmic_bytes": 2 * session, "ms": round(kernel_ms["gather"], 4),
                      "peak_source": f"{peak_src} hbm_gbs (burst copy)"},

@@ -356,14 +356,15 @@ constexpr int kSegStep = 4 * kSegStepLines * kSegLine;  // bytes a warp moves pe
 // launch may use fewer warps (the kernels read their count from blockDim). On
 // B200, with two steps in flight, twelve warps measured fastest for runs of
 // spans of at most 8 KiB (fewer leave small spans' per-unit work exposed) and
-// for whole-block CRCs, which only read; eight (KVSNAP_SEG_BULK_WARPS) for 16
-// and 32 KiB spans, where 7 or 9 to 12 warps measured 4 to 10 % slower. More
-// than twelve leave each thread too few registers to keep its loads in flight.
+// for whole-block CRCs, which only read; ten (KVSNAP_SEG_BULK_WARPS) for
+// grid-stride units of 16 KiB, where 8, 9, 11 and 12 warps measured 1 to 6 %
+// slower. More than twelve leave each thread too few registers to keep its
+// loads in flight.
 #ifndef KVSNAP_SEG_WARPS
 #define KVSNAP_SEG_WARPS 12
 #endif
 #ifndef KVSNAP_SEG_BULK_WARPS
-#define KVSNAP_SEG_BULK_WARPS 8
+#define KVSNAP_SEG_BULK_WARPS 10
 #endif
 #ifndef KVSNAP_SEG_DEPTH
 #define KVSNAP_SEG_DEPTH 2
