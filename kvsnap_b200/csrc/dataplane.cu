@@ -779,14 +779,34 @@ struct SpanUnits {
 
 // 64 KiB pieces of packed blocks in device memory (the CRC of whole blocks).
 constexpr int64_t kSegPiece = 64 << 10;
+// Warp w of W takes units w, w + W, ..., walked as (block, piece) steps so
+// that no unit costs a 64-bit division. Without `shifts` (the launcher built a
+// shift table) no unit computes its shift either.
 struct PieceUnits {
     const int64_t* addrs;
     int64_t n, block_bytes, pieces;
     uint32_t* status;
-    int64_t u, du;
+    int64_t i, p;        // block and piece of the cursor
+    int64_t di, dp;      // the grid stride, in blocks and pieces
+    bool shifts;
+    __device__ PieceUnits(const int64_t* a, int64_t count, int64_t bytes, uint32_t* st, int64_t w, int64_t warps,
+                          bool with_shifts)
+        : addrs(a), n(count), block_bytes(bytes), pieces((bytes + kSegPiece - 1) / kSegPiece), status(st),
+          shifts(with_shifts) {
+        i = w / pieces;
+        p = w - i * pieces;
+        di = warps / pieces;
+        dp = warps - di * pieces;
+    }
+    __device__ __forceinline__ void step() {
+        i += di;
+        if ((p += dp) >= pieces) {
+            p -= pieces;
+            ++i;
+        }
+    }
     __device__ __forceinline__ bool next(SegUnit& out, int lane) {
-        for (; u < n * pieces; u += du) {
-            const int64_t i = u / pieces, p = u - i * pieces;
+        for (; i < n; step()) {
             const int64_t at = p * kSegPiece, len = min(kSegPiece, block_bytes - at);
             const int64_t base = addrs[i] + at;
             if ((base | len) & 15) {
@@ -799,11 +819,11 @@ struct PieceUnits {
             out.seg = seg_bytes(len);
             out.pad = 4 * out.seg - len;
             out.block = i;
-            out.shift = dev_xpow8n(uint64_t(block_bytes - at - len));
+            out.shift = shifts ? dev_xpow8n(uint64_t(block_bytes - at - len)) : 0u;
             out.after = 0;
             out.steps = int32_t(out.seg / kSegStepSeg);
             out.span = int32_t(p);
-            u += du;
+            step();
             return true;
         }
         return false;
@@ -996,21 +1016,33 @@ __global__ void __launch_bounds__(kSegThreads, 1) span_kernel_hbm(SpanArgs a) {
             SpanUnits<MODE, RUNS>(a, w, warps), tl, t4, append, ring, lane, a.crc, a.spans, a.valid, pl);
 }
 
+// `place`: the launcher sized shared memory for placement tables with a shift row a piece.
 __global__ void __launch_bounds__(kSegThreads, 1) crc_kernel_hbm(const int64_t* addrs, int64_t n,
                                                                  int64_t block_bytes, uint32_t* crc,
-                                                                 uint32_t* status) {
+                                                                 uint32_t* status, int place) {
     extern __shared__ uint4 smem[];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, per_cta = blockDim.x >> 5;
     const SegSmem sm(smem, warp, per_cta, false);
     SegUnit* ring = sm.ring;
     uint32_t *t4 = sm.t4, *tx = sm.tx, *tb = sm.tb;     // tx: unused without runs
     load_seg_tables(tb, t4);
+    Placement pl;
+    const int64_t pieces = (block_bytes + kSegPiece - 1) / kSegPiece;
+    if (place) {   // windows for whole pieces; row p: x^(8 * bytes after piece p in its block)
+        uint32_t* win = reinterpret_cast<uint32_t*>(smem + seg_smem_bytes(per_cta, false) / 16);
+        build_windows(win, seg_bytes(kSegPiece));
+        build_shifts(win + kWinWords, int(pieces), [block_bytes](int p) {
+            const int64_t at = int64_t(p) * kSegPiece;
+            return dev_xpow8n(uint64_t(block_bytes - at - min(kSegPiece, block_bytes - at)));
+        });
+        pl = Placement{reinterpret_cast<const char*>(win) + 4 * lane, win + kWinWords, seg_bytes(kSegPiece), 0};
+    }
     __syncthreads();
     const RepTables tl{reinterpret_cast<const char*>(tb), 4u * lane};
     const AppendBytes append{tx, kSegPiece};
-    const PieceUnits units{addrs, n, block_bytes, (block_bytes + kSegPiece - 1) / kSegPiece, status,
-                           (int64_t)blockIdx.x * per_cta + warp, (int64_t)gridDim.x * per_cta};
-    warp_stream<false, true, false, false>(units, tl, t4, append, ring, lane, crc, nullptr, 0);
+    const PieceUnits units(addrs, n, block_bytes, status, (int64_t)blockIdx.x * per_cta + warp,
+                           (int64_t)gridDim.x * per_cta, !place);
+    warp_stream<false, true, false, false>(units, tl, t4, append, ring, lane, crc, nullptr, 0, pl);
 }
 
 // CRC32C of whole packed blocks, in pieces of kPiece bytes per warp.
@@ -1526,10 +1558,12 @@ extern "C" int kvsnap_dp_crc32c(const int64_t* addrs, int64_t n, uint64_t block_
         check(cudaMemsetAsync(crc_out, 0, sizeof(uint32_t) * size_t(n), s));
         if (hbm && vec == 16) {
             configure_once(reinterpret_cast<const void*>(crc_kernel_hbm), kSegSmemMax);
-            const int64_t want = (n * ((int64_t(block_bytes) + kPiece - 1) / kPiece) + kSegWarps - 1) / kSegWarps;
+            const int64_t pieces = (int64_t(block_bytes) + kSegPiece - 1) / kSegPiece;
+            const int64_t want = (n * pieces + kSegWarps - 1) / kSegWarps;
             const int grid = ctas > 0 ? ctas : int(want < sms ? want : sms);
-            crc_kernel_hbm<<<grid, kSegThreads, seg_smem_bytes(kSegWarps, false), s>>>(addrs, n, int64_t(block_bytes),
-                                                                                       crc_out, status);
+            const int place = pieces <= place_rows(kSegWarps);     // pieces are placed by table
+            const int bytes = seg_smem_bytes(kSegWarps, false) + (place ? place_bytes(int(pieces)) : 0);
+            crc_kernel_hbm<<<grid, kSegThreads, bytes, s>>>(addrs, n, int64_t(block_bytes), crc_out, status, place);
             check(cudaGetLastError());
             finish(crc_out, expect, n, block_bytes, status, s, kSegUnscale);
             return;
