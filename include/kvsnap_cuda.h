@@ -102,8 +102,9 @@ int kvsnap_pool_wait_many(void* pool, int64_t n, const uint64_t* ids);
 #define KVSNAP_DP_BAD_CUT 8u         /* KVSNAP_DP_PAIRS or _SPLIT* met spans that do not cut that way */
 
 /* OR into a `vec` argument when every packed address is device memory: the
-   kernels then give each lane one contiguous segment of a span, move whole
-   128-byte lines coalesced and CRC through per-lane tables (HBM-friendly),
+   kernels then cut each unit into 4 segments, move whole 128-byte lines
+   coalesced, each group of 8 lanes 1 KiB of its segment a step, and CRC each
+   lane's bytes in its registers through per-lane tables (HBM-friendly),
    instead of 16 bytes a lane in 512-byte steps (host-link friendly).
    Needs vec 16. */
 #define KVSNAP_DP_HBM 0x100

@@ -28,6 +28,27 @@ def split_flag(span_bytes):
     return {2: SPLIT2, 4: SPLIT4}.get(span_bytes // SPLIT_PIECE_BYTES, 0) if span_bytes % SPLIT_PIECE_BYTES == 0 else 0
 
 
+def hbm_flags(span_bytes, vec):
+    """The flags a device-to-device gather or scatter of these spans takes beside ``vec``.
+
+    0 unless vec is 16. Otherwise KVSNAP_DP_HBM and the unit cut that measured fastest on B200:
+    spans all of at most RUNS_SPAN_BYTES fold in runs (2 and 4 KiB spans of one size, an even
+    count, in pairs); spans of one size of 32 or 64 KiB move in 16 KiB pieces; others whole.
+    """
+    if vec != 16 or not span_bytes:
+        return 0
+    flags = HBM
+    sizes = set(span_bytes)
+    one_size = next(iter(sizes)) if len(sizes) == 1 else 0
+    if max(span_bytes) <= RUNS_SPAN_BYTES:
+        flags |= RUNS
+        if one_size in PAIR_SPAN_BYTES and len(span_bytes) % 2 == 0:
+            flags |= PAIRS
+    elif one_size:
+        flags |= split_flag(one_size)
+    return flags
+
+
 class Span(C.Structure):
     """``kvsnap_span``: one registered layer view (64 bytes)."""
     _fields_ = [("base", C.c_int64), ("pitch", C.c_int64), ("offset", C.c_int64), ("bytes", C.c_int64),

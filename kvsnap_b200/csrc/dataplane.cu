@@ -324,12 +324,13 @@ __global__ void __launch_bounds__(256) span_kernel(SpanArgs a) {
 // ---- segment-lane kernels, for packed blocks in device memory -------------------
 //
 // When both sides of a copy are HBM, the L1 data pipe (global and shared
-// wavefronts together), not DRAM, bounds a CRC'ing copy. Two things keep its
-// wavefront count per byte near the minimum here:
+// wavefronts together) and the latency of the loads in flight, not DRAM
+// alone, bound a CRC'ing copy. Three things keep the wavefronts per byte low:
 //   * every global load and store moves whole 128-byte lines, 8 lanes a line
 //     (fully coalesced);
-//   * each lane owns one contiguous segment of the unit, so its register runs
-//     straight through its bytes with no jump between steps.
+//   * each lane folds the bytes it loaded, in stream order, so nothing goes
+//     through shared memory but the table lookups;
+//   * the lookups go to per-lane copies of the tables, so none conflicts.
 // A unit of `len` bytes is front-padded with zeros to 4 equal segments of S
 // bytes, S a multiple of 1 KiB (a zero prefix leaves a zero-started raw CRC as
 // is). Lanes 8r..8r+7 own segment r: in step t, load j of lane (r, s) moves
@@ -479,8 +480,7 @@ __device__ __forceinline__ uint32_t mul_x32(const uint32_t* t4, uint32_t r) {
     return t4[768 + (r & 255)] ^ t4[512 + ((r >> 8) & 255)] ^ t4[256 + ((r >> 16) & 255)] ^ t4[r >> 24];
 }
 
-// A lane's chains over its segment, combined: ((c0 x^32 + c1) x^32 + c2) x^32 + c3
-// = raw(segment) * x^96.
+// A lane's four chains, combined: ((c0 x^32 + c1) x^32 + c2) x^32 + c3.
 __device__ __forceinline__ uint32_t combine_chains(const Chains& r, const uint32_t* t4) {
     uint32_t h = mul_x32(t4, r.c[0]) ^ r.c[1];
     h = mul_x32(t4, h) ^ r.c[2];
@@ -651,7 +651,7 @@ __host__ __device__ constexpr int seg_smem_bytes(int warps, bool runs) {
 }
 constexpr int kSegSmemTotal = seg_smem_bytes(kSegWarps, true);
 static_assert(kSegSmemTotal <= 227 * 1024, "segment kernels exceed the shared memory of a CTA");
-// Rows of placement tables a grid-stride CTA of `warps` warps can hold after its line buffers.
+// Rows of placement tables a grid-stride CTA of `warps` warps can hold after its other shared memory.
 __host__ __device__ constexpr int place_rows(int warps) {
     return (kSegCarveBytes - seg_smem_bytes(warps, false) - kWinWords * 4) / (kShiftPitch * 4);
 }
@@ -972,7 +972,8 @@ __device__ __forceinline__ void warp_stream(Units units, const RepTables& tl, co
 // TAIL: every unit belongs to the save's last block, whose token slots from
 // `valid` on are written as zeros. The launcher gives that block a launch of
 // its own, so the common kernel carries none of the masking code.
-// Shared memory: unit rings, then (with a CRC) the tables and line buffers.
+// Shared memory: unit rings, then (with a CRC) the tables, and in the
+// grid-stride path the placement tables when the launcher sized for them.
 template <int MODE, bool TAIL, bool RUNS>
 __global__ void __launch_bounds__(kSegThreads, 1) span_kernel_hbm(SpanArgs a) {
     extern __shared__ uint4 smem[];
@@ -1502,7 +1503,7 @@ int launch_spans(const kvsnap_span* spans, int nspans, uint64_t block_bytes, con
                 a.n = body;
                 auto kernel = runs ? span_kernel_hbm<MODE, false, true> : span_kernel_hbm<MODE, false, false>;
                 const int warps = runs ? kSegWarps : kSegBulkWarps;
-                // Grid-stride units are placed by table when the rows fit beside the line buffers.
+                // Grid-stride units are placed by table when the rows fit within kSegCarveBytes.
                 const int rows = nspans << split;
                 a.place = crc && !runs && rows <= place_rows(warps);
                 const int bytes = !crc ? seg_ring_bytes(warps)

@@ -509,18 +509,9 @@ class TorchBlockDataPlane:
                 raise RuntimeError("packed block size disagrees with the registered layers")
             host = torch.frombuffer(bytearray(bytes(spans)), dtype=torch.uint8)
             self._span_vec = vec
-            # Device-side copies may use the segment-lane HBM kernels; small spans fold in runs,
-            # 2 or 4 KiB spans of one size in pairs; 32 or 64 KiB spans of one size move in
-            # 16 KiB pieces.
-            self._hbm = _abi.HBM if vec == 16 else 0
-            sizes = {layer["bytes"] for layer in self.layers}
-            one_size = sizes.pop() if len(sizes) == 1 else 0
-            if self._hbm and max(layer["bytes"] for layer in self.layers) <= _abi.RUNS_SPAN_BYTES:
-                self._hbm |= _abi.RUNS
-                if one_size in _abi.PAIR_SPAN_BYTES and len(self.layers) % 2 == 0:
-                    self._hbm |= _abi.PAIRS
-            elif self._hbm and one_size:
-                self._hbm |= _abi.split_flag(one_size)
+            # Device-side copies may use the segment-lane HBM kernels, with the unit cut that the
+            # layer sizes allow.
+            self._hbm = _abi.hbm_flags([layer["bytes"] for layer in self.layers], vec)
             self._min_blocks = min(t.shape[0] for t in self.caches.values())
             self._span_table = host.to(self._device())
             # Side streams: restores that read pinned memory in place run on their

@@ -174,6 +174,54 @@ def test_lane_partials_recombine_like_the_kernels():
     assert total ^ init == oracle.crc32c(data.tobytes())
 
 
+@pytest.mark.parametrize("seg,length", [(1024, 4096), (2048, 8192), (1024, 4096 - 640)])
+def test_segment_lanes_recombine_like_the_hbm_kernels(seg, length):
+    """The device-memory kernels' arithmetic, checked on the CPU: a unit front-padded to 4 segments
+    of `seg` bytes; lane (r, s) folds 16-byte slot s of every 128-byte line of segment r into four
+    chains (word k, then the 124 bytes to the same word of the next line); Horner over the chains
+    with x^32, the lane's factor x^(8 * (16 * (7 - s) + seg * (3 - r))), and the XOR over lanes give
+    raw(unit) * x^(8 * 124), the factor the finish step divides out."""
+    rng = np.random.default_rng(seg + length)
+    unit = rng.integers(0, 256, length, dtype=np.uint8).tobytes()
+    padded = bytes(4 * seg - length) + unit
+    line_step, x32 = oracle.xpow8n(128), oracle.xpow8n(4)
+    total = 0
+    for lane in range(32):
+        r, s = lane >> 3, lane & 7
+        chains = [0, 0, 0, 0]
+        for line in range(seg // 128):
+            at = r * seg + line * 128 + 16 * s
+            for k in range(4):
+                word = int.from_bytes(padded[at + 4 * k:at + 4 * k + 4], "little")
+                chains[k] = oracle.gf_mulmod(chains[k] ^ word, line_step)
+        h = oracle.gf_mulmod(oracle.gf_mulmod(oracle.gf_mulmod(chains[0], x32) ^ chains[1], x32) ^ chains[2], x32)
+        h ^= chains[3]
+        total ^= oracle.gf_mulmod(h, oracle.xpow8n(16 * (7 - s) + seg * (3 - r)))
+    raw = ~oracle.crc32c(unit, 0xFFFFFFFF) & 0xFFFFFFFF
+    assert total == oracle.gf_mulmod(raw, oracle.xpow8n(124))
+
+
+def test_hbm_flags_by_model_shape():
+    """The unit cut the plane asks the device-memory kernels for, by registered span sizes."""
+    from kvsnap_b200 import _abi
+    HBM, RUNS, PAIRS, SPLIT2, SPLIT4 = _abi.HBM, _abi.RUNS, _abi.PAIRS, _abi.SPLIT2, _abi.SPLIT4
+    cases = [
+        ([32 << 10] * 72, HBM | SPLIT2),            # Qwen3-8B: 36 layers x K, V of 8 heads
+        ([64 << 10] * 128, HBM | SPLIT4),           # 16 KV heads a rank
+        ([16 << 10] * 128, HBM),                    # Qwen3-32B TP-2 shard
+        ([8 << 10] * 128, HBM | RUNS),              # TP-4 shard
+        ([4 << 10] * 128, HBM | RUNS | PAIRS),      # TP-8 shard
+        ([2 << 10] * 6, HBM | RUNS | PAIRS),
+        ([4 << 10] * 3, HBM | RUNS),                # an odd count does not pair
+        ([4 << 10, 8 << 10], HBM | RUNS),           # sizes differ: runs only
+        ([34816] * 4, HBM),                         # 32 KiB + 2 KiB: no 16 KiB pieces
+        ([32 << 10, 16 << 10], HBM),
+    ]
+    for spans, want in cases:
+        assert _abi.hbm_flags(spans, 16) == want, (spans[:2], len(spans))
+        assert _abi.hbm_flags(spans, 8) == 0
+
+
 def test_runs_coalesce_like_the_reference_copy_count():
     from kvsnap_b200.dataplane import TorchBlockDataPlane
     size = 100
