@@ -67,6 +67,18 @@ def test_every_declared_entry_point_is_exported():
         assert hasattr(io, name), name
 
 
+def test_python_flag_constants_equal_the_header():
+    """Every KVSNAP_DP_* flag and status bit the ctypes layer uses has the header's value."""
+    from kvsnap_b200 import _abi
+    text = (Path(__file__).resolve().parents[1] / "include" / "kvsnap_cuda.h").read_text()
+    defines = {m.group(1): int(m.group(2), 0)
+               for m in re.finditer(r"#define KVSNAP_DP_(\w+) (0x[0-9A-Fa-f]+|\d+)u?\b", text)}
+    for name in ("MISALIGNED", "BAD_BLOCK", "CRC_MISMATCH", "BAD_CUT", "HBM", "RUNS", "PAIRS", "SPLIT2", "SPLIT4"):
+        assert getattr(_abi, name) == defines[name], name
+    assert defines["SPLIT_MASK"] == _abi.SPLIT2 | _abi.SPLIT4
+    assert defines["ABI_VERSION"] == _abi.DP_ABI_VERSION
+
+
 def test_abi_versions_and_span_layout_load_without_a_gpu():
     from kvsnap_b200 import _abi
     from kvsnap_b200.dataplane import _dp, _load
