@@ -356,11 +356,11 @@ constexpr int kSegStep = 4 * kSegStepLines * kSegLine;  // bytes a warp moves pe
 // kSegWarps sizes the register budget and the largest shared-memory layout; a
 // launch may use fewer warps (the kernels read their count from blockDim). On
 // B200, with two steps in flight, twelve warps measured fastest for runs of
-// spans of at most 8 KiB (fewer leave small spans' per-unit work exposed) and
-// for whole-block CRCs, which only read; ten (KVSNAP_SEG_BULK_WARPS) for
-// grid-stride units of 16 KiB, where 8, 9, 11 and 12 warps measured 1 to 6 %
-// slower. More than twelve leave each thread too few registers to keep its
-// loads in flight.
+// spans of at most 8 KiB (fewer leave small spans' per-unit work exposed);
+// ten (KVSNAP_SEG_BULK_WARPS) for grid-stride units of 16 KiB, where 8, 9, 11
+// and 12 warps measured 1 to 6 % slower. More than twelve leave the copying
+// kernels too few registers (at 14 or 16 they spill); the whole-block CRC,
+// which only loads, fits 16 warps in 128 registers (KVSNAP_SEG_CRC_WARPS).
 #ifndef KVSNAP_SEG_WARPS
 #define KVSNAP_SEG_WARPS 12
 #endif
@@ -1018,7 +1018,15 @@ __global__ void __launch_bounds__(kSegThreads, 1) span_kernel_hbm(SpanArgs a) {
 }
 
 // `place`: the launcher sized shared memory for placement tables with a shift row a piece.
-__global__ void __launch_bounds__(kSegThreads, 1) crc_kernel_hbm(const int64_t* addrs, int64_t n,
+#ifndef KVSNAP_SEG_CRC_WARPS
+#define KVSNAP_SEG_CRC_WARPS 16
+#endif
+// Warps of the whole-block CRC, which only loads (its own register budget):
+// 12, 14 and 16 measured 0.69, 0.73 and 0.78 of the HBM copy rate.
+constexpr int kSegCrcWarps = KVSNAP_SEG_CRC_WARPS;
+static_assert(seg_smem_bytes(kSegCrcWarps, false) + kWinWords * 4 <= kSegCarveBytes, "CRC kernel shared memory");
+
+__global__ void __launch_bounds__(32 * kSegCrcWarps, 1) crc_kernel_hbm(const int64_t* addrs, int64_t n,
                                                                  int64_t block_bytes, uint32_t* crc,
                                                                  uint32_t* status, int place) {
     extern __shared__ uint4 smem[];
@@ -1560,11 +1568,12 @@ extern "C" int kvsnap_dp_crc32c(const int64_t* addrs, int64_t n, uint64_t block_
         if (hbm && vec == 16) {
             configure_once(reinterpret_cast<const void*>(crc_kernel_hbm), kSegSmemMax);
             const int64_t pieces = (int64_t(block_bytes) + kSegPiece - 1) / kSegPiece;
-            const int64_t want = (n * pieces + kSegWarps - 1) / kSegWarps;
+            const int64_t want = (n * pieces + kSegCrcWarps - 1) / kSegCrcWarps;
             const int grid = ctas > 0 ? ctas : int(want < sms ? want : sms);
-            const int place = pieces <= place_rows(kSegWarps);     // pieces are placed by table
-            const int bytes = seg_smem_bytes(kSegWarps, false) + (place ? place_bytes(int(pieces)) : 0);
-            crc_kernel_hbm<<<grid, kSegThreads, bytes, s>>>(addrs, n, int64_t(block_bytes), crc_out, status, place);
+            const int place = pieces <= place_rows(kSegCrcWarps);     // pieces are placed by table
+            const int bytes = seg_smem_bytes(kSegCrcWarps, false) + (place ? place_bytes(int(pieces)) : 0);
+            crc_kernel_hbm<<<grid, 32 * kSegCrcWarps, bytes, s>>>(addrs, n, int64_t(block_bytes), crc_out, status,
+                                                                   place);
             check(cudaGetLastError());
             finish(crc_out, expect, n, block_bytes, status, s, kSegUnscale);
             return;
