@@ -236,20 +236,29 @@ int kvsnap_dp_ipc_open(const void* handle, int device, void** ptr);
 int kvsnap_dp_ipc_close(void* ptr);
 
 /*
- * Restore scatter with CRC32C verification that allocates nothing. No
- * counterpart in the reference. For callers that cannot allocate device
- * memory: a serving worker whose KV cache was sized to fill the GPU, or host
- * code that must not enter an allocator that may synchronise the device. The
- * same copy and check as kvsnap_dp_scatter with crc_out and expect, except that
- * the per-block CRC accumulators live in one fixed scratch array inside this
- * library (KVSNAP_DP_STATIC_MAX_BLOCKS × 4 bytes, held on every GPU that loads
- * the library until the process exits). The caller passes inputs and outputs;
- * the result is the cache write and the KVSNAP_DP_CRC_MISMATCH bit in *status.
- * n above the maximum is rejected with an error and nothing is launched. The
- * first call on a device looks up the scratch's device address; make that
- * first call before any stream capture. Every call shares the scratch (it is
- * cleared at the start of each call): calls whose work overlaps on the GPU race
- * and must not be issued concurrently.
+ * Verified restore scatter that allocates nothing. No counterpart in the
+ * reference. For callers that cannot allocate device memory: a serving worker
+ * whose KV cache was sized to fill the GPU has no room left for a CRC buffer,
+ * and host code that must not enter an allocator (which may synchronise the
+ * device) cannot ask for one. The per-block CRC32C accumulators and one gate
+ * word live in one fixed scratch array inside this library,
+ * (KVSNAP_DP_STATIC_MAX_BLOCKS + 64) x 4 bytes, held on every GPU that loads
+ * the library until the process exits. The caller passes inputs and outputs.
+ *
+ * Check before write: every source block's CRC32C is computed and compared
+ * with expect[i] first; the scatter then runs gated on that verdict. On a
+ * mismatch nothing is written to the cache and KVSNAP_DP_CRC_MISMATCH is set
+ * in *status (other bits as kvsnap_dp_scatter sets them). `vec` takes the same
+ * flags as kvsnap_dp_scatter (KVSNAP_DP_HBM and its unit cuts for sources in
+ * device memory). Sources in pinned host memory cross the host link twice,
+ * once for the check and once for the copy.
+ *
+ * n above the maximum is rejected with an error and nothing is launched.
+ * Every call looks up the scratch's device address (cudaGetSymbolAddress, no
+ * allocation); make the first call on a device before any stream capture,
+ * since it may load the module. Every call shares the scratch and clears what
+ * it uses at its start: calls whose work overlaps on the GPU race on it and
+ * must not be issued concurrently.
  */
 #define KVSNAP_DP_STATIC_MAX_BLOCKS 65536
 int kvsnap_dp_scatter_verify_static(const kvsnap_span* spans, int nspans, uint64_t block_bytes,

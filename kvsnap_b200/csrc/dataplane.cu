@@ -1466,11 +1466,12 @@ extern "C" int kvsnap_dp_plan(kvsnap_span* spans, int nspans, uint64_t* block_by
 
 namespace {
 
+// The gather or scatter launches; throws Fail on a bad request or a CUDA error.
 template <int MODE>
-int launch_spans(const kvsnap_span* spans, int nspans, uint64_t block_bytes, const int64_t* blocks,
-                 const int64_t* packed, int64_t n, int32_t valid, uint32_t* crc, const uint32_t* expect,
-                 const uint32_t* gate, uint32_t* status, int vec, int ctas, uintptr_t stream) {
-    return guarded([&] {
+void spans_launch(const kvsnap_span* spans, int nspans, uint64_t block_bytes, const int64_t* blocks,
+                  const int64_t* packed, int64_t n, int32_t valid, uint32_t* crc, const uint32_t* expect,
+                  const uint32_t* gate, uint32_t* status, int vec, int ctas, uintptr_t stream) {
+    {
         const bool hbm = (vec & KVSNAP_DP_HBM) != 0;
         const bool runs = (vec & KVSNAP_DP_RUNS) != 0, pairs = (vec & KVSNAP_DP_PAIRS) != 0;
         const int split = (vec & KVSNAP_DP_SPLIT_MASK) / KVSNAP_DP_SPLIT2;   // log2 of the pieces a span
@@ -1530,6 +1531,16 @@ int launch_spans(const kvsnap_span* spans, int nspans, uint64_t block_bytes, con
             span_kernel<8, MODE><<<grid, 256, 0, s>>>(a);
         check(cudaGetLastError());
         if (crc) finish(crc, expect, n, block_bytes, status, s);
+    }
+}
+
+template <int MODE>
+int launch_spans(const kvsnap_span* spans, int nspans, uint64_t block_bytes, const int64_t* blocks,
+                 const int64_t* packed, int64_t n, int32_t valid, uint32_t* crc, const uint32_t* expect,
+                 const uint32_t* gate, uint32_t* status, int vec, int ctas, uintptr_t stream) {
+    return guarded([&] {
+        spans_launch<MODE>(spans, nspans, block_bytes, blocks, packed, n, valid, crc, expect, gate, status, vec,
+                           ctas, stream);
     });
 }
 
@@ -1554,38 +1565,51 @@ extern "C" int kvsnap_dp_scatter(const kvsnap_span* spans, int nspans, uint64_t 
                                   status, vec, ctas, stream);
 }
 
+namespace {
+
+// CRC32C of n whole packed blocks into crc_out (cleared first), then the finish
+// step. The kernels report bad addresses in `status`; the comparison with
+// `expect` reports into `verdict` (the same word for kvsnap_dp_crc32c).
+void crc_blocks(const int64_t* addrs, int64_t n, uint64_t block_bytes, uint32_t* crc_out, const uint32_t* expect,
+                uint32_t* status, uint32_t* verdict, int vec, int ctas, cudaStream_t s, int sms) {
+    const bool hbm = (vec & KVSNAP_DP_HBM) != 0;
+    vec &= ~(KVSNAP_DP_HBM | KVSNAP_DP_RUNS | KVSNAP_DP_PAIRS | KVSNAP_DP_SPLIT_MASK);   // whole blocks: no use
+    check(cudaMemsetAsync(crc_out, 0, sizeof(uint32_t) * size_t(n), s));
+    if (hbm && vec == 16) {
+        configure_once(reinterpret_cast<const void*>(crc_kernel_hbm), kSegSmemMax);
+        const int64_t pieces = (int64_t(block_bytes) + kSegPiece - 1) / kSegPiece;
+        const int64_t want = (n * pieces + kSegCrcWarps - 1) / kSegCrcWarps;
+        const int grid = ctas > 0 ? ctas : int(want < sms ? want : sms);
+        const int place = pieces <= place_rows(kSegCrcWarps);     // pieces are placed by table
+        const int bytes = seg_smem_bytes(kSegCrcWarps, false) + (place ? place_bytes(int(pieces)) : 0);
+        crc_kernel_hbm<<<grid, 32 * kSegCrcWarps, bytes, s>>>(addrs, n, int64_t(block_bytes), crc_out, status,
+                                                               place);
+        check(cudaGetLastError());
+        finish(crc_out, expect, n, block_bytes, verdict, s, kSegUnscale);
+        return;
+    }
+    const int64_t pieces = (int64_t(block_bytes) + kPiece - 1) / kPiece;
+    const int grid = grid_for(n * pieces, ctas, sms);
+    if (vec == 16)
+        crc_kernel<16><<<grid, 256, 0, s>>>(addrs, n, int64_t(block_bytes), crc_out, status);
+    else
+        crc_kernel<8><<<grid, 256, 0, s>>>(addrs, n, int64_t(block_bytes), crc_out, status);
+    check(cudaGetLastError());
+    finish(crc_out, expect, n, block_bytes, verdict, s);
+}
+
+}  // namespace
+
 extern "C" int kvsnap_dp_crc32c(const int64_t* addrs, int64_t n, uint64_t block_bytes, uint32_t* crc_out,
                                 const uint32_t* expect, uint32_t* status, int vec, int ctas, uintptr_t stream) {
     return guarded([&] {
-        const bool hbm = (vec & KVSNAP_DP_HBM) != 0;
-        vec &= ~(KVSNAP_DP_HBM | KVSNAP_DP_RUNS | KVSNAP_DP_PAIRS | KVSNAP_DP_SPLIT_MASK);   // whole blocks: no use
-        if (n < 0 || vec != 16 && vec != 8) throw Fail{"invalid CRC request"};
+        const int width = vec & ~(KVSNAP_DP_HBM | KVSNAP_DP_RUNS | KVSNAP_DP_PAIRS | KVSNAP_DP_SPLIT_MASK);
+        if (n < 0 || width != 16 && width != 8) throw Fail{"invalid CRC request"};
         if (n == 0) return;
         if (!addrs || !crc_out || block_bytes == 0) throw Fail{"CRC needs addresses, output and a block size"};
         const int sms = enter_stream(stream);
-        cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-        check(cudaMemsetAsync(crc_out, 0, sizeof(uint32_t) * size_t(n), s));
-        if (hbm && vec == 16) {
-            configure_once(reinterpret_cast<const void*>(crc_kernel_hbm), kSegSmemMax);
-            const int64_t pieces = (int64_t(block_bytes) + kSegPiece - 1) / kSegPiece;
-            const int64_t want = (n * pieces + kSegCrcWarps - 1) / kSegCrcWarps;
-            const int grid = ctas > 0 ? ctas : int(want < sms ? want : sms);
-            const int place = pieces <= place_rows(kSegCrcWarps);     // pieces are placed by table
-            const int bytes = seg_smem_bytes(kSegCrcWarps, false) + (place ? place_bytes(int(pieces)) : 0);
-            crc_kernel_hbm<<<grid, 32 * kSegCrcWarps, bytes, s>>>(addrs, n, int64_t(block_bytes), crc_out, status,
-                                                                   place);
-            check(cudaGetLastError());
-            finish(crc_out, expect, n, block_bytes, status, s, kSegUnscale);
-            return;
-        }
-        const int64_t pieces = (int64_t(block_bytes) + kPiece - 1) / kPiece;
-        const int grid = grid_for(n * pieces, ctas, sms);
-        if (vec == 16)
-            crc_kernel<16><<<grid, 256, 0, s>>>(addrs, n, int64_t(block_bytes), crc_out, status);
-        else
-            crc_kernel<8><<<grid, 256, 0, s>>>(addrs, n, int64_t(block_bytes), crc_out, status);
-        check(cudaGetLastError());
-        finish(crc_out, expect, n, block_bytes, status, s);
+        crc_blocks(addrs, n, block_bytes, crc_out, expect, status, status, vec, ctas,
+                   reinterpret_cast<cudaStream_t>(stream), sms);
     });
 }
 
@@ -1673,19 +1697,26 @@ extern "C" int kvsnap_dp_ipc_close(void* ptr) {
     return guarded([&] { check(cudaIpcCloseMemHandle(ptr)); });
 }
 
-// ---- restore scatter with CRC verification into a fixed scratch -------------------------
+// ---- verified restore scatter that allocates nothing -----------------------------------
 //
-// For callers that cannot allocate device memory: the per-block CRC32C
-// accumulators live in this file-scope array instead of a caller buffer.
-// `g_static_crc` is a host-side stand-in in host code: its device address is
-// obtained once per device with cudaGetSymbolAddress (with that device current)
-// and passed to the kernels.
+// For callers that cannot allocate device memory. The per-block CRC32C
+// accumulators and one gate word live in this file-scope array instead of a
+// caller buffer: words [0, kStaticMaxBlocks) hold the CRCs, word kStaticGate
+// the verdict that gates the scatter. In host code `g_static_scratch` is a
+// host-side stand-in, not a device address; every call looks the device
+// address up with cudaGetSymbolAddress, with the stream's device current, and
+// passes that pointer to the kernels.
 constexpr int64_t kStaticMaxBlocks = KVSNAP_DP_STATIC_MAX_BLOCKS;
-__device__ __align__(256) uint32_t g_static_crc[kStaticMaxBlocks];
+constexpr int64_t kStaticGate = kStaticMaxBlocks;
+__device__ __align__(256) uint32_t g_static_scratch[kStaticMaxBlocks + 64];
 
 namespace {
-std::mutex g_static_mutex;
-uint32_t* g_static_ptr[256];   // per device ordinal, set up on first use
+
+// The verdict of the check, copied into the caller's status word after the gated scatter.
+__global__ void report_gate_kernel(const uint32_t* gate, uint32_t* status) {
+    if (threadIdx.x == 0 && *gate) atomicOr(status, *gate);
+}
+
 }  // namespace
 
 extern "C" int kvsnap_dp_scatter_verify_static(const kvsnap_span* spans, int nspans, uint64_t block_bytes,
@@ -1697,25 +1728,22 @@ extern "C" int kvsnap_dp_scatter_verify_static(const kvsnap_span* spans, int nsp
                                                       "scratch holds (KVSNAP_DP_STATIC_MAX_BLOCKS)"};
         if (!expect || !status) throw Fail{"kvsnap_dp_scatter_verify_static needs expected CRCs and a status word"};
         if (n == 0) return;
-        int device = 0;
-        if (stream)
-            check(cudaStreamGetDevice(reinterpret_cast<cudaStream_t>(stream), &device));
-        else
-            check(cudaGetDevice(&device));
-        if (device < 0 || device >= 256) throw Fail{"device ordinal out of range"};
-        uint32_t* scratch = nullptr;
-        {
-            std::lock_guard<std::mutex> lock(g_static_mutex);
-            if (!g_static_ptr[device]) {
-                check(cudaSetDevice(device));
-                void* ptr = nullptr;
-                check(cudaGetSymbolAddress(&ptr, g_static_crc));
-                g_static_ptr[device] = static_cast<uint32_t*>(ptr);
-            }
-            scratch = g_static_ptr[device];
-        }
-        if (launch_spans<kScatter>(spans, nspans, block_bytes, blocks, sources, n, 0, scratch, expect, nullptr,
-                                   status, vec, ctas, stream) < 0)
-            throw Fail{kvsnap_cuda_error()};
+        if (!spans || nspans <= 0 || !sources || !blocks || block_bytes == 0)
+            throw Fail{"kvsnap_dp_scatter_verify_static needs spans, sources, block ids and a block size"};
+        const int sms = enter_stream(stream);   // the stream's device is current from here on
+        cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+        void* address = nullptr;
+        check(cudaGetSymbolAddress(&address, g_static_scratch));
+        uint32_t* scratch = static_cast<uint32_t*>(address);
+        uint32_t* gate = scratch + kStaticGate;
+        // 1. CRC32C of every source block into the scratch; a mismatch sets the gate.
+        check(cudaMemsetAsync(gate, 0, sizeof(uint32_t), s));
+        crc_blocks(sources, n, block_bytes, scratch, expect, status, gate, vec, ctas, s, sms);
+        // 2. The scatter, which writes nothing when the gate is set.
+        spans_launch<kScatter>(spans, nspans, block_bytes, blocks, sources, n, 0, nullptr, nullptr, gate, status, vec,
+                               ctas, stream);
+        // 3. The verdict into the caller's status.
+        report_gate_kernel<<<1, 32, 0, s>>>(gate, status);
+        check(cudaGetLastError());
     });
 }

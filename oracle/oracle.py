@@ -258,11 +258,16 @@ def digests(blocks) -> list:
 
 def dedup(blocks) -> tuple:
     """Distinct blobs and per-block segments (``store.py:625-628``): returns (unique ids, segments)."""
+    return dedup_digests(digests(blocks), [len(b) for b in blocks])
+
+
+def dedup_digests(block_digests, lengths) -> tuple:
+    """``dedup`` from per-block ``(content id, CRC32C)`` already computed: a payload dict keyed by
+    content id keeps the first block of each (``store.py:625-628``, ``volatile.py:254-279``)."""
     unique, segments = {}, []
-    for index, (key, checksum) in enumerate(digests(blocks)):
+    for index, ((key, checksum), length) in enumerate(zip(block_digests, lengths)):
         unique.setdefault(key, index)
-        segments.append(dict(blob_id=key, offset=0, length=len(blocks[index]), first_block=index, nblocks=1,
-                             crc32c=checksum))
+        segments.append(dict(blob_id=key, offset=0, length=length, first_block=index, nblocks=1, crc32c=checksum))
     return list(unique), segments
 
 

@@ -129,3 +129,26 @@ def test_unit_cut_flags_are_consistent(spans, vec):
         assert one and not flags & _abi.RUNS
         pieces = 2 if flags & _abi.SPLIT2 else 4
         assert spans[0] == pieces * _abi.SPLIT_PIECE_BYTES
+
+
+def test_full_size_generators_reproduce_the_fixture_stream():
+    """The GPU fill (torch int64 splitmix64) and the lazy host slices give kvgen.random_bytes' bytes exactly,
+    so the full-size GPU tests feed the CUDA path and the oracle the same cache."""
+    import torch
+    import kvgen
+    seed, nbytes = 28011, (1 << 18) + 24
+    want = kvgen.random_bytes(seed, nbytes)
+    buf = torch.empty(nbytes, dtype=torch.uint8)
+    kvgen.fill_random(buf, seed, chunk_words=1 << 12)
+    assert np.array_equal(buf.numpy(), want)
+    lazy = kvgen.LazyBytes(seed, nbytes)
+    for start, stop in [(0, 8), (3, 1000), (4096, 8192), (nbytes - 13, nbytes), (77, 77), (0, nbytes)]:
+        assert np.array_equal(lazy[start:stop], want[start:stop])
+
+
+def test_dedup_from_precomputed_digests_is_the_dedup_rule():
+    import kvgen
+    blocks = [kvgen.random_bytes(s, 4096) for s in (1, 2, 1, 3, 2)]
+    unique, segments = oracle.dedup(blocks)
+    assert oracle.dedup_digests(oracle.digests(blocks), [len(b) for b in blocks]) == (unique, segments)
+    assert len(unique) == 3 and [s["first_block"] for s in segments] == [0, 1, 2, 3, 4]

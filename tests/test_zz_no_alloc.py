@@ -1,16 +1,24 @@
-"""The restore scatter that allocates nothing (kvsnap_dp_scatter_verify_static), against the one that does.
+"""The verified restore scatter that allocates nothing (kvsnap_dp_scatter_verify_static), against the one that does.
 
 Some callers of this data plane cannot allocate device memory: a serving worker
 whose KV cache was sized to fill the GPU has no room for a CRC buffer, and host
 code that must not enter an allocator that may synchronise the device cannot
-call one. For them the library keeps the per-block CRC accumulators in a fixed
-scratch array of its own. This test calls that entry point through the C ABI
-and checks that it leaves the same cache bytes and the same verdict as
-kvsnap_dp_scatter given a caller-allocated CRC buffer, on two calls in a row
-(the scratch keeps the previous call's contents, so each call must clear it),
-that a bad checksum is caught the same way, and that a request beyond the
-scratch's size is refused before anything runs. This file sorts last so that a
-run stopping at the first failure has already run every other test.
+call one. For them the library keeps the per-block CRC accumulators and the
+verdict that gates the copy in a fixed scratch array of its own. This test
+calls that entry point through the C ABI and checks, for packed blocks in
+pinned host memory (the host-link kernels) and in device memory (the
+segment-lane HBM kernels, with the plane's unit cut):
+
+* on two calls in a row (the scratch keeps the previous call's contents, so
+  each call must clear it) it leaves the same cache bytes and the same status
+  as kvsnap_dp_scatter given a caller-allocated CRC buffer, and the oracle's;
+* a bad checksum gives the same status as kvsnap_dp_scatter, but, because the
+  check runs before the copy, the cache is left exactly as it was;
+* a clean call after a failing one succeeds;
+* a request beyond the scratch's size is refused before anything runs.
+
+This file sorts last so that a run stopping at the first failure has already
+run every other test.
 """
 import ctypes as C
 
@@ -29,7 +37,8 @@ def _i32(values):
     return torch.tensor([v - (1 << 32) if v >= 1 << 31 else v for v in values], dtype=torch.int32, device="cuda")
 
 
-def test_static_scratch_scatter_matches_the_allocating_entry_point():
+@pytest.mark.parametrize("where", ["pinned", "device"])
+def test_static_scratch_scatter_matches_the_allocating_entry_point(where):
     from kvsnap_b200 import _abi
     from kvsnap_b200.dataplane import TorchBlockDataPlane, _dp
     case, storages, layout = golden_case("qwen3_8b_5d")
@@ -43,7 +52,14 @@ def test_static_scratch_scatter_matches_the_allocating_entry_point():
         snapshot = plane.pool.reserve(n * size)
         for i, block in enumerate(packed):
             C.memmove(snapshot.pointer + i * size, block.ctypes.data, size)
-        sources = torch.tensor([snapshot.pointer + i * size for i in range(n)], dtype=torch.int64, device="cuda")
+        if where == "pinned":
+            base, vec = snapshot.pointer, 16
+        else:
+            staged = torch.empty(n * size, dtype=torch.uint8, device="cuda")
+            staged.copy_(torch.from_numpy(np.concatenate(packed)))
+            base, vec = staged.data_ptr(), 16 | plane._hbm
+            assert vec & _abi.HBM
+        sources = torch.tensor([base + i * size for i in range(n)], dtype=torch.int64, device="cuda")
         blocks = torch.tensor(case["restored"], dtype=torch.int64, device="cuda")
         good = _i32([oracle.crc32c(b) for b in packed])
         bad = _i32([oracle.crc32c(b) ^ (1 if i == 2 else 0) for i, b in enumerate(packed)])
@@ -61,7 +77,8 @@ def test_static_scratch_scatter_matches_the_allocating_entry_point():
             crc = torch.empty(n, dtype=torch.int32, device="cuda")
             status = torch.zeros(1, dtype=torch.int32, device="cuda")
             assert lib.kvsnap_dp_scatter(spans.data_ptr(), nspans, size, sources.data_ptr(), blocks.data_ptr(), n,
-                                         crc.data_ptr(), expect.data_ptr(), 0, status.data_ptr(), 16, 0, stream) == 0
+                                         crc.data_ptr(), expect.data_ptr(), 0, status.data_ptr(), vec, 0,
+                                         stream) == 0
             torch.cuda.synchronize()
             return host_bytes(tensors), int(status.item())
 
@@ -70,7 +87,7 @@ def test_static_scratch_scatter_matches_the_allocating_entry_point():
             status = torch.zeros(1, dtype=torch.int32, device="cuda")
             assert lib.kvsnap_dp_scatter_verify_static(spans.data_ptr(), nspans, size, sources.data_ptr(),
                                                        blocks.data_ptr(), n, expect.data_ptr(), status.data_ptr(),
-                                                       16, 0, stream) == 0
+                                                       vec, 0, stream) == 0
             torch.cuda.synchronize()
             return host_bytes(tensors), int(status.item())
 
@@ -84,16 +101,19 @@ def test_static_scratch_scatter_matches_the_allocating_entry_point():
             assert all(np.array_equal(kv_b[k], expected_cache[k]) for k in kv_b)
         for _ in range(2):
             _, status_a = allocating(bad)
-            _, status_b = static(bad)
+            kv_b, status_b = static(bad)
             assert status_a == status_b == _abi.CRC_MISMATCH
-        _, status_b = static(good)           # a clean call after a failing one
+            # Checked before the copy: the cache still holds what it held before the call.
+            assert all(np.array_equal(kv_b[k], storages[k]) for k in kv_b)
+        kv_b, status_b = static(good)        # a clean call after a failing one
         assert status_b == 0
+        assert all(np.array_equal(kv_b[k], expected_cache[k]) for k in kv_b)
 
         status = torch.zeros(1, dtype=torch.int32, device="cuda")
         too_many = _abi.STATIC_MAX_BLOCKS + 1
         assert lib.kvsnap_dp_scatter_verify_static(spans.data_ptr(), nspans, size, sources.data_ptr(),
                                                    blocks.data_ptr(), too_many, good.data_ptr(), status.data_ptr(),
-                                                   16, 0, stream) == -1
+                                                   vec, 0, stream) == -1
         assert "KVSNAP_DP_STATIC_MAX_BLOCKS" in lib.kvsnap_cuda_error().decode()
         snapshot.close()
     finally:
