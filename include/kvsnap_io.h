@@ -28,13 +28,16 @@ uint32_t kvsnap_crc32c(const void* data, size_t size);
 int kvsnap_pwrite_all(int fd, const void* data, size_t size, int64_t offset, int durable);
 /* Read exactly size bytes at offset; EIO at end of file (reference io.cpp:71-81). */
 int kvsnap_pread_all(int fd, void* data, size_t size, int64_t offset);
-/* A pool of `workers` (1..64) I/O threads admitting at most max_bytes in
-   flight; NULL on bad arguments (reference io.cpp:130-133). */
+/* A transfer pool that runs at most `workers` (1..64) transfers and at most
+   max_bytes at once; NULL on bad arguments (reference io.cpp:130-133, which
+   runs them on that many worker threads). Here each transfer runs on its
+   caller's thread once admitted: the call waits for its result either way. */
 void* kvsnap_io_pool_create(size_t workers, size_t max_bytes);
 void kvsnap_io_pool_destroy(void* pool);
-/* Run one pread (write=0) or pwrite (write=1) on the pool and wait for it:
-   EINVAL for bad arguments, EMSGSIZE above the pool's byte limit, ECANCELED
-   when the pool stops first (reference io.cpp:135-154). */
+/* Run one pread (write=0) or pwrite (write=1) through the pool and wait for
+   it: EINVAL for bad arguments, EMSGSIZE above the pool's byte limit,
+   ECANCELED when the pool is destroyed before admitting it (reference
+   io.cpp:135-154). Destroying the pool waits for admitted transfers. */
 int kvsnap_io_pool_transfer(void* pool, int fd, void* data, size_t size, int64_t offset, int write, int durable);
 
 #ifdef __cplusplus

@@ -7,17 +7,14 @@
 //     a byte table where SSE4.2 is absent. Same values as the reference
 //     (io.cpp:16-47), pinned by tests/test_io_native.py;
 //   * pread / pwrite loops with EINTR, short-transfer and EOF handling;
-//   * a bounded worker pool that admits at most a byte budget in flight.
+//   * a transfer pool that runs at most `workers` transfers and a byte budget
+//     at once, each on its caller's thread.
 #include <cerrno>
 #include <condition_variable>
 #include <cstdint>
 #include <cstring>
-#include <deque>
-#include <future>
-#include <memory>
 #include <mutex>
-#include <thread>
-#include <vector>
+#include <new>
 
 #include <unistd.h>
 
@@ -118,156 +115,117 @@ extern "C" uint32_t kvsnap_crc32c_extend(const void* data, size_t size, uint32_t
 extern "C" uint32_t kvsnap_crc32c(const void* data, size_t size) { return kvsnap_crc32c_extend(data, size, 0); }
 
 namespace {
-bool bad_range(size_t size, int64_t offset) {
-    return offset < 0 || size > static_cast<uint64_t>(INT64_MAX - offset);
+
+// Every byte of [offset, offset + size) moved by positional reads or writes,
+// resuming after signals and short transfers. A read that meets end of file, or
+// a write that makes no progress, is EIO; other failures return their errno.
+// A negative offset, or a range past INT64_MAX, is EINVAL before any call.
+template <bool kWrite>
+int move_all(int fd, char* bytes, size_t size, int64_t offset) {
+    if (offset < 0 || size > static_cast<uint64_t>(INT64_MAX - offset)) return EINVAL;
+    size_t moved = 0;
+    while (moved < size) {
+        const off_t at = static_cast<off_t>(offset + static_cast<int64_t>(moved));
+        const ssize_t n = kWrite ? pwrite(fd, bytes + moved, size - moved, at) : pread(fd, bytes + moved, size - moved, at);
+        if (n > 0) {
+            moved += static_cast<size_t>(n);
+        } else if (n == 0) {
+            return EIO;
+        } else if (errno != EINTR) {
+            return errno;
+        }
+    }
+    return 0;
 }
+
+int sync_data(int fd) {
+    for (;;) {
+        if (fdatasync(fd) == 0) return 0;
+        if (errno != EINTR) return errno;
+    }
+}
+
 }  // namespace
 
 extern "C" int kvsnap_pwrite_all(int fd, const void* data, size_t size, int64_t offset, int durable) {
-    if (bad_range(size, offset)) return EINVAL;
-    const char* p = static_cast<const char*>(data);
-    for (size_t done = 0; done < size;) {
-        ssize_t n = pwrite(fd, p + done, size - done, offset + static_cast<int64_t>(done));
-        if (n < 0) {
-            if (errno == EINTR) continue;
-            return errno;
-        }
-        if (n == 0) return EIO;
-        done += static_cast<size_t>(n);
-    }
-    if (durable) {
-        int rc;
-        do rc = fdatasync(fd);
-        while (rc < 0 && errno == EINTR);
-        if (rc < 0) return errno;
-    }
-    return 0;
+    const int rc = move_all<true>(fd, const_cast<char*>(static_cast<const char*>(data)), size, offset);
+    return rc || !durable ? rc : sync_data(fd);
 }
 
 extern "C" int kvsnap_pread_all(int fd, void* data, size_t size, int64_t offset) {
-    if (bad_range(size, offset)) return EINVAL;
-    char* p = static_cast<char*>(data);
-    for (size_t done = 0; done < size;) {
-        ssize_t n = pread(fd, p + done, size - done, offset + static_cast<int64_t>(done));
-        if (n < 0) {
-            if (errno == EINTR) continue;
-            return errno;
-        }
-        if (n == 0) return EIO;   // end of file before `size` bytes
-        done += static_cast<size_t>(n);
-    }
-    return 0;
+    return move_all<false>(fd, static_cast<char*>(data), size, offset);
 }
 
 namespace {
 
-struct Request {
-    int fd = -1, write = 0, durable = 0;
-    void* data = nullptr;
-    size_t size = 0;
-    int64_t offset = 0;
-    std::promise<int> result;
-};
-
-class Workers {
+// The transfer pool. Its C ABI is synchronous: a caller hands over one read or
+// write and waits for its result. So no work is handed to other threads: each
+// caller runs its own transfer once the gate admits it, and the gate bounds
+// what the pool allows at once: `slots` transfers and `budget` bytes in
+// flight. Destroying the gate turns away every waiter (ECANCELED) and waits
+// for the transfers already admitted.
+class Gate {
   public:
-    Workers(size_t count, size_t budget) : budget_(budget) {
-        try {
-            for (size_t i = 0; i < count; ++i) threads_.emplace_back([this] { serve(); });
-        } catch (...) {
-            stop();
-            throw;
-        }
-    }
-    ~Workers() { stop(); }
+    Gate(size_t slots, size_t budget) : free_slots_(slots), budget_(budget), room_(budget) {}
 
-    int submit(int fd, void* data, size_t size, int64_t offset, int write, int durable) {
-        auto request = std::make_shared<Request>();
-        request->fd = fd;
-        request->data = data;
-        request->size = size;
-        request->offset = offset;
-        request->write = write;
-        request->durable = durable;
-        std::future<int> done = request->result.get_future();
-        {
-            std::unique_lock<std::mutex> lock(mutex_);
-            room_.wait(lock, [&] { return stopping_ || size <= budget_ - in_flight_; });
-            if (stopping_) return ECANCELED;
-            in_flight_ += size;
-            queue_.push_back(std::move(request));
-        }
-        ready_.notify_one();
-        return done.get();
+    ~Gate() {
+        std::unique_lock<std::mutex> hold(mu_);
+        closing_ = true;
+        changed_.notify_all();
+        changed_.wait(hold, [&] { return running_ == 0 && waiting_ == 0; });
     }
 
     size_t budget() const { return budget_; }
 
-  private:
-    void serve() {
-        for (;;) {
-            std::shared_ptr<Request> request;
-            {
-                std::unique_lock<std::mutex> lock(mutex_);
-                ready_.wait(lock, [&] { return stopping_ || !queue_.empty(); });
-                if (queue_.empty()) return;   // stopping and drained
-                request = std::move(queue_.front());
-                queue_.pop_front();
-            }
-            int rc = request->write
-                         ? kvsnap_pwrite_all(request->fd, request->data, request->size, request->offset,
-                                             request->durable)
-                         : kvsnap_pread_all(request->fd, request->data, request->size, request->offset);
-            {
-                std::lock_guard<std::mutex> lock(mutex_);
-                in_flight_ -= request->size;
-            }
-            room_.notify_all();
-            request->result.set_value(rc);
-        }
-    }
-
-    void stop() {
+    int run(int fd, char* bytes, size_t size, int64_t offset, bool write, bool durable) {
         {
-            std::lock_guard<std::mutex> lock(mutex_);
-            stopping_ = true;
+            std::unique_lock<std::mutex> hold(mu_);
+            ++waiting_;
+            changed_.wait(hold, [&] { return closing_ || (free_slots_ > 0 && size <= room_); });
+            --waiting_;
+            if (closing_) {
+                changed_.notify_all();
+                return ECANCELED;
+            }
+            --free_slots_;
+            room_ -= size;
+            ++running_;
         }
-        ready_.notify_all();
-        room_.notify_all();
-        for (auto& t : threads_)
-            if (t.joinable()) t.join();
+        const int rc = write ? kvsnap_pwrite_all(fd, bytes, size, offset, durable)
+                             : kvsnap_pread_all(fd, bytes, size, offset);
+        {
+            std::lock_guard<std::mutex> hold(mu_);
+            ++free_slots_;
+            room_ += size;
+            --running_;
+        }
+        changed_.notify_all();
+        return rc;
     }
 
+  private:
+    std::mutex mu_;
+    std::condition_variable changed_;
+    size_t free_slots_;
     const size_t budget_;
-    size_t in_flight_ = 0;
-    bool stopping_ = false;
-    std::mutex mutex_;
-    std::condition_variable ready_, room_;
-    std::deque<std::shared_ptr<Request>> queue_;
-    std::vector<std::thread> threads_;
+    size_t room_;
+    size_t running_ = 0, waiting_ = 0;
+    bool closing_ = false;
 };
 
 }  // namespace
 
 extern "C" void* kvsnap_io_pool_create(size_t workers, size_t max_bytes) {
-    if (workers == 0 || workers > 64 || max_bytes == 0) return nullptr;
-    try {
-        return new Workers(workers, max_bytes);
-    } catch (...) {
-        return nullptr;
-    }
+    if (workers < 1 || workers > 64 || max_bytes == 0) return nullptr;
+    return new (std::nothrow) Gate(workers, max_bytes);
 }
 
-extern "C" void kvsnap_io_pool_destroy(void* pool) { delete static_cast<Workers*>(pool); }
+extern "C" void kvsnap_io_pool_destroy(void* pool) { delete static_cast<Gate*>(pool); }
 
 extern "C" int kvsnap_io_pool_transfer(void* pool, int fd, void* data, size_t size, int64_t offset, int write,
                                        int durable) {
     if (!pool || (!data && size) || (write != 0 && write != 1)) return EINVAL;
-    Workers* w = static_cast<Workers*>(pool);
-    if (size > w->budget()) return EMSGSIZE;
-    try {
-        return w->submit(fd, data, size, offset, write, durable);
-    } catch (...) {
-        return ENOMEM;
-    }
+    Gate* gate = static_cast<Gate*>(pool);
+    if (size > gate->budget()) return EMSGSIZE;
+    return gate->run(fd, static_cast<char*>(data), size, offset, write == 1, durable != 0);
 }

@@ -190,13 +190,25 @@ class DigestCache:
         return len(self._entries)
 
 
+def _nonnegative(*values):
+    if min(values) < 0:
+        raise ValueError("negative copy argument")
+
+
 class CudaPool:
-    """A pinned host arena with one copy stream, over the C ABI v2 (reference dataplane.py:38-131)."""
+    """A pinned host arena and its copy stream, owned through the C ABI v2 (reference dataplane.py:38-131).
+
+    Every entry point refuses a pool inherited across fork or already closed,
+    and runs under the pool's re-entrant lock, so a close waits for an
+    operation in progress. The Python allocation objects are kept until the
+    native pool has drained, because the native side may still be copying for
+    them; a close that cannot drain the copy stream raises and leaves the
+    pool, its allocations and their tensor owners intact.
+    """
 
     def __init__(self, capacity_bytes: int, device: int = 0, library=None):
         self._pid = os.getpid()
         self._lock = threading.RLock()
-        # Python owners of allocations the native pool may still be copying; see close().
         self._allocations = {}
         self.lib = _load(library)
         self.abi_version = self.lib.kvsnap_pool_abi_version()
@@ -205,46 +217,56 @@ class CudaPool:
         self.device = device
         self.handle = self.lib.kvsnap_pool_create(capacity_bytes, device)
         if not self.handle:
-            raise RuntimeError(self.lib.kvsnap_cuda_error().decode())
+            raise RuntimeError(self._error())
+
+    def _error(self):
+        return self.lib.kvsnap_cuda_error().decode()
+
+    def _not_forked(self):
+        if self._pid != os.getpid():
+            raise RuntimeError("CUDA pools must not be inherited across fork")
+
+    def _native(self, entry, *args):
+        """Pool entry point ``entry`` on this pool's handle; a negative result raises with the library's message."""
+        result = getattr(self.lib, entry)(self.handle, *args)
+        if result < 0:
+            raise RuntimeError(self._error())
+        return result
 
     def check(self, result):
         if result < 0:
-            raise RuntimeError(self.lib.kvsnap_cuda_error().decode())
+            raise RuntimeError(self._error())
         return result
-
-    def reserve(self, size):
-        with self.operation():
-            ident, ptr = C.c_uint64(), C.c_void_p()
-            if self.lib.kvsnap_pool_reserve(self.handle, size, C.byref(ident), C.byref(ptr)) < 0:
-                message = self.lib.kvsnap_cuda_error().decode()
-                if "pinned capacity exhausted" in message:
-                    raise PinnedCapacityError(message)
-                raise RuntimeError(message)
-            allocation = PinnedAllocation(self, ident.value, ptr.value, size)
-            self._allocations[ident.value] = allocation
-            return allocation
 
     @contextmanager
     def operation(self):
-        if self._pid != os.getpid():
-            raise RuntimeError("CUDA pools must not be inherited across fork")
+        self._not_forked()
         with self._lock:
             if not self.handle:
                 raise RuntimeError("pool closed")
             yield
 
+    def reserve(self, size):
+        ident, pointer = C.c_uint64(), C.c_void_p()
+        with self.operation():
+            if self.lib.kvsnap_pool_reserve(self.handle, size, C.byref(ident), C.byref(pointer)) < 0:
+                message = self._error()
+                full = "pinned capacity exhausted" in message
+                raise PinnedCapacityError(message) if full else RuntimeError(message)
+            allocation = PinnedAllocation(self, ident.value, pointer.value, size)
+            self._allocations[allocation.ident] = allocation
+        return allocation
+
     def close(self):
-        if self._pid != os.getpid():
-            raise RuntimeError("CUDA pools must not be inherited across fork")
+        self._not_forked()
         with self._lock:
-            if self.handle:
-                self.check(self.lib.kvsnap_pool_close_checked(self.handle))
-                self.handle = None
-                for allocation in self._allocations.values():
-                    allocation.closed = True
-                    if hasattr(allocation, "_tensor_references"):
-                        allocation._tensor_references.clear()
-                self._allocations.clear()
+            if not self.handle:
+                return
+            self._native("kvsnap_pool_close_checked")     # raises, keeping everything, when the drain fails
+            self.handle = None
+            for allocation in self._allocations.values():
+                allocation._retire()
+            self._allocations = {}
 
     def copy_many(self, entries, *, to_host, stream=0):
         """Queue copies ``(allocation, offset, device_ptr, size)`` in order on ``stream`` in one native call.
@@ -254,53 +276,53 @@ class CudaPool:
         allocation's completion event covers all of them (kvsnap_pool_copy_many).
         """
         with self.operation():
-            n = len(entries)
-            if n == 0:
+            if not entries:
                 return
             for allocation, offset, device_ptr, size in entries:
-                if allocation.pool is not self:
-                    raise ValueError("allocation belongs to another pool")
-                allocation._open()
-                if min(offset, device_ptr, size, stream) < 0:
-                    raise ValueError("negative copy argument")
-            arrays = [(C.c_uint64 * n)(*column) for column in
-                      zip(*((a.ident, offset, ptr, size) for a, offset, ptr, size in entries))]
-            self.check(self.lib.kvsnap_pool_copy_many(self.handle, n, *arrays, int(bool(to_host)), stream))
+                self._owns(allocation)
+                _nonnegative(offset, device_ptr, size, stream)
+            columns = zip(*((a.ident, offset, ptr, size) for a, offset, ptr, size in entries))
+            arrays = [(C.c_uint64 * len(entries))(*column) for column in columns]
+            self._native("kvsnap_pool_copy_many", len(entries), *arrays, int(bool(to_host)), stream)
 
     def wait_many(self, allocations):
         """``wait`` for each allocation, in one native call (kvsnap_pool_wait_many)."""
         with self.operation():
             allocations = list(allocations)
             for allocation in allocations:
-                if allocation.pool is not self:
-                    raise ValueError("allocation belongs to another pool")
-                allocation._open()
+                self._owns(allocation)
             if allocations:
                 ids = (C.c_uint64 * len(allocations))(*(a.ident for a in allocations))
-                self.check(self.lib.kvsnap_pool_wait_many(self.handle, len(allocations), ids))
+                self._native("kvsnap_pool_wait_many", len(allocations), ids)
+
+    def _owns(self, allocation):
+        if allocation.pool is not self:
+            raise ValueError("allocation belongs to another pool")
+        allocation._open()
 
     def stream_handle(self) -> int:
         """The copy stream's handle (borrowed; valid while the pool is open)."""
-        with self.operation():
-            handle = C.c_size_t()
-            self.check(self.lib.kvsnap_pool_copy_stream(self.handle, C.byref(handle)))
-            if not handle.value:
-                raise RuntimeError("native copy stream handle is invalid")
-            return handle.value
+        with self.borrow_copy_stream() as handle:
+            return handle
 
     @contextmanager
     def borrow_copy_stream(self):
         """Borrow the copy stream's handle; the context excludes a concurrent close (reference dataplane.py:110-131)."""
         with self.operation():
             handle = C.c_size_t()
-            self.check(self.lib.kvsnap_pool_copy_stream(self.handle, C.byref(handle)))
+            self._native("kvsnap_pool_copy_stream", C.byref(handle))
             if not handle.value:
                 raise RuntimeError("native copy stream handle is invalid")
             yield handle.value
 
 
 class PinnedAllocation:
-    """One reservation in a :class:`CudaPool` (reference dataplane.py:134-211)."""
+    """One reservation in a :class:`CudaPool`: pinned bytes and the id its copies are fenced under
+    (reference dataplane.py:134-211).
+
+    Callers may hang the tensors a copy still reads on ``_tensor_references``;
+    they are let go once the allocation is waited for or retired.
+    """
 
     def __init__(self, pool, ident, pointer, size):
         self.pool, self.ident, self.pointer, self.size = pool, ident, pointer, size
@@ -310,72 +332,77 @@ class PinnedAllocation:
         if self.closed or not self.pool.handle:
             raise RuntimeError("pinned allocation closed")
 
+    def _drop_owners(self):
+        owners = getattr(self, "_tensor_references", None)
+        if owners is not None:
+            owners.clear()
+
+    def _retire(self):
+        self.closed = True
+        self._drop_owners()
+
     @contextmanager
     def operation(self):
         with self.pool.operation():
             self._open()
             yield
 
+    def _native(self, entry, *args):
+        return self.pool._native(entry, self.ident, *args)
+
     def copy(self, device_ptr, size, offset=0, *, to_host, producer_stream=0):
         with self.operation():
-            if min(size, offset, device_ptr, producer_stream) < 0:
-                raise ValueError("negative copy argument")
-            self.pool.check(self.pool.lib.kvsnap_pool_copy(
-                self.pool.handle, self.ident, offset, device_ptr, size, int(bool(to_host)), producer_stream))
+            _nonnegative(size, offset, device_ptr, producer_stream)
+            self._native("kvsnap_pool_copy", offset, device_ptr, size, int(bool(to_host)), producer_stream)
 
     def copy_2d(self, device_ptr, device_pitch, host_offset, host_pitch, width, height, *,
                 to_host, producer_stream=0):
         """``height`` rows of ``width`` bytes between strided device and host memory."""
         with self.operation():
-            if min(device_ptr, device_pitch, host_offset, host_pitch, width, height, producer_stream) < 0:
-                raise ValueError("negative copy argument")
-            self.pool.check(self.pool.lib.kvsnap_pool_copy_2d(
-                self.pool.handle, self.ident, host_offset, host_pitch, device_ptr, device_pitch,
-                width, height, int(bool(to_host)), producer_stream))
+            _nonnegative(device_ptr, device_pitch, host_offset, host_pitch, width, height, producer_stream)
+            self._native("kvsnap_pool_copy_2d", host_offset, host_pitch, device_ptr, device_pitch, width, height,
+                         int(bool(to_host)), producer_stream)
 
     def copy_on(self, device_ptr, size, offset=0, *, to_host, stream):
         """Like :meth:`copy`, queued on ``stream`` instead of the pool's copy stream (no producer fence)."""
         with self.operation():
-            if min(size, offset, device_ptr, stream) < 0:
-                raise ValueError("negative copy argument")
-            self.pool.check(self.pool.lib.kvsnap_pool_copy_on(
-                self.pool.handle, self.ident, offset, device_ptr, size, int(bool(to_host)), stream))
+            _nonnegative(size, offset, device_ptr, stream)
+            self._native("kvsnap_pool_copy_on", offset, device_ptr, size, int(bool(to_host)), stream)
 
     def mark(self, stream=0):
         """Fence work queued so far on ``stream`` (0: the pool's copy stream) under this allocation's
         wait/ready/release: kernels that read or write the allocation in place run there, and
         marking after them makes the allocation's lifetime cover them."""
         with self.operation():
-            self.pool.check(self.pool.lib.kvsnap_pool_mark(self.pool.handle, self.ident, stream))
+            self._native("kvsnap_pool_mark", stream)
 
     def wait(self):
         with self.operation():
-            self.pool.check(self.pool.lib.kvsnap_pool_wait(self.pool.handle, self.ident))
-            if hasattr(self, "_tensor_references"):
-                self._tensor_references.clear()
+            self._native("kvsnap_pool_wait")
+            self._drop_owners()
 
     def ready(self):
         with self.operation():
-            return bool(self.pool.check(self.pool.lib.kvsnap_pool_ready(self.pool.handle, self.ident)))
+            return bool(self._native("kvsnap_pool_ready"))
+
+    def _settled(self, offset, size, what):
+        """Wait for the allocation's copies; then the address of bytes [offset, offset + size) of it."""
+        self.wait()
+        if type(offset) is not int or type(size) is not int or offset < 0 or size < 0 or offset + size > self.size:
+            raise ValueError(f"pinned {what} outside allocation")
+        return self.pointer + offset
 
     def read(self):
         with self.operation():
-            self.wait()
-            return C.string_at(self.pointer, self.size)
+            return C.string_at(self._settled(0, self.size, "read"), self.size)
 
     def read_range(self, offset, size):
         with self.operation():
-            self.wait()
-            if type(offset) is not int or type(size) is not int or offset < 0 or size < 0 or offset + size > self.size:
-                raise ValueError("pinned read outside allocation")
-            return C.string_at(self.pointer + offset, size)
+            return C.string_at(self._settled(offset, size, "read"), size)
 
     def zero(self, offset, size):
         with self.operation():
-            self.wait()
-            if offset < 0 or size < 0 or offset + size > self.size:
-                raise ValueError("pinned zero outside allocation")
-            C.memset(self.pointer + offset, 0, size)
+            C.memset(self._settled(offset, size, "zero"), 0, size)
 
     def write(self, data):
         with self.operation():
@@ -385,15 +412,13 @@ class PinnedAllocation:
             C.memmove(self.pointer, data, self.size)
 
     def close(self):
-        if self.pool._pid != os.getpid():
-            raise RuntimeError("CUDA pools must not be inherited across fork")
-        with self.pool._lock:
-            if not self.closed and self.pool.handle:
-                self.pool.check(self.pool.lib.kvsnap_pool_release(self.pool.handle, self.ident))
-            self.closed = True
-            self.pool._allocations.pop(self.ident, None)
-            if hasattr(self, "_tensor_references"):
-                self._tensor_references.clear()
+        pool = self.pool
+        pool._not_forked()
+        with pool._lock:
+            if not self.closed and pool.handle:
+                self._native("kvsnap_pool_release")
+            pool._allocations.pop(self.ident, None)
+            self._retire()
 
 
 def _split_paged(caches, block_size):
@@ -412,6 +437,32 @@ def _split_paged(caches, block_size):
         else:
             views[name] = tensor
     return views
+
+
+def _layer_record(name, tensor, block_size, device):
+    """The reference's record of one registered layer view, after its checks (reference dataplane.py:230-247).
+
+    Every view lives on the one CUDA ``device``. A view is ``[blocks, heads, tokens, width]`` with ``block_size`` tokens and
+    contiguous width. Its per-block axes may be permuted in storage (vLLM's
+    ``[blocks, tokens, heads, width]`` seen as BHNC) but must tile one dense
+    span: taken in order of stride, each axis longer than 1 has the stride
+    of the product of the smaller ones. Blocks may be further apart than a
+    span, never closer. The record keeps the actual shape, dtype and strides.
+    """
+    if tensor.device != device or tensor.device.type != "cuda":
+        raise ValueError("one CUDA device required")
+    shape, strides = tuple(tensor.shape), tuple(tensor.stride()) if tensor.ndim else ()
+    if tensor.ndim != 4 or shape[2] != block_size or strides[3] != 1:
+        raise ValueError(f"unsupported KV layout for {name}: need dense [B,H,N,C] blocks with contiguous C")
+    span = 1
+    for stride, size in sorted((strides[axis], shape[axis]) for axis in (1, 2, 3) if shape[axis] > 1):
+        if stride != span:
+            raise ValueError(f"unsupported KV layout for {name}: block has holes or overlapping axes")
+        span *= size
+    if strides[0] < span:
+        raise ValueError(f"unsupported KV layout for {name}: overlapping blocks")
+    return {"name": name, "shape": list(shape[1:]), "dtype": str(tensor.dtype), "stride": list(strides[1:]),
+            "bytes": shape[1] * shape[2] * shape[3] * tensor.element_size()}
 
 
 def _u32(values):
@@ -448,25 +499,8 @@ class TorchBlockDataPlane:
         self.torch = torch
         self.caches = dict(sorted(_split_paged(caches, block_size).items()))
         self.block_size = block_size
-        self.layers = []
         device = next(iter(self.caches.values())).device
-        for name, tensor in self.caches.items():
-            if tensor.device != device or tensor.device.type != "cuda":
-                raise ValueError("one CUDA device required")
-            if tensor.ndim != 4 or tensor.shape[2] != block_size or tensor.stride(3) != 1:
-                raise ValueError(f"unsupported KV layout for {name}: need dense [B,H,N,C] blocks with contiguous C")
-            # A block must be one dense span: its H/N axes may be permuted (vLLM's
-            # LBNHC storage seen as BHNC) but may not leave holes or overlap.
-            dense = 1
-            for stride, size in sorted((tensor.stride(i), tensor.shape[i]) for i in (1, 2, 3) if tensor.shape[i] > 1):
-                if stride != dense:
-                    raise ValueError(f"unsupported KV layout for {name}: block has holes or overlapping axes")
-                dense *= size
-            if tensor.stride(0) < dense:
-                raise ValueError(f"unsupported KV layout for {name}: overlapping blocks")
-            self.layers.append({"name": name, "shape": list(tensor.shape[1:]),
-                                "dtype": str(tensor.dtype), "stride": list(tensor.stride()[1:]),
-                                "bytes": tensor[0].numel() * tensor.element_size()})
+        self.layers = [_layer_record(name, tensor, block_size, device) for name, tensor in self.caches.items()]
         self.block_bytes = sum(layer["bytes"] for layer in self.layers)
         self.save_mode = save_mode or self.save_mode
         self.restore_mode = restore_mode or self.restore_mode

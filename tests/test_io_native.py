@@ -13,6 +13,7 @@ import shutil
 import subprocess
 import tempfile
 import threading
+import time
 from pathlib import Path
 
 import pytest
@@ -49,6 +50,8 @@ def faulty(tmp_path_factory):
     handle = _abi.declare(C.CDLL(str(lib)), _abi.IO_API)
     handle.io_fault.argtypes, handle.io_fault.restype = [C.c_int] * 4, None
     handle.io_calls.argtypes, handle.io_calls.restype = [C.c_int], C.c_int
+    handle.io_stall.argtypes, handle.io_stall.restype = [C.c_int], None
+    handle.io_inside.restype = handle.io_peak.restype = C.c_int
     return handle
 
 
@@ -183,6 +186,76 @@ def test_worker_pool_arguments_budget_and_concurrency(io, tmpfile):
         io.kvsnap_io_pool_destroy(pool)
 
 
+def _until(predicate, seconds=5.0):
+    deadline = time.monotonic() + seconds
+    while not predicate():
+        if time.monotonic() > deadline:
+            return False
+        time.sleep(0.01)
+    return True
+
+
+@pytest.mark.parametrize("slots, budget, expect", [(2, 1 << 20, 2), (8, 3 * 4096, 3)])
+def test_transfer_pool_runs_at_most_its_slots_and_bytes_at_once(faulty, tmpfile, slots, budget, expect):
+    """kvsnap_io_pool_create's limits: `workers` transfers and `max_bytes` in flight (reference io.cpp:130-154)."""
+    pool = faulty.kvsnap_io_pool_create(slots, budget)
+    fd = tmpfile.fileno()
+    blocks = [kvgen.random_bytes(40 + i, 4096).tobytes() for i in range(6)]
+    results = [None] * 6
+
+    def write(i):
+        results[i] = faulty.kvsnap_io_pool_transfer(pool, fd, blocks[i], 4096, i * 4096, 1, 0)
+
+    faulty.io_peak()
+    faulty.io_stall(1)
+    threads = [threading.Thread(target=write, args=(i,)) for i in range(6)]
+    try:
+        for t in threads:
+            t.start()
+        assert _until(lambda: faulty.io_inside() == expect)
+        time.sleep(0.2)
+        assert faulty.io_inside() == expect          # the rest wait for a slot or for bytes
+    finally:
+        faulty.io_stall(0)
+        for t in threads:
+            t.join(10)
+    assert results == [0] * 6 and faulty.io_peak() == expect
+    back = C.create_string_buffer(6 * 4096)
+    assert faulty.kvsnap_pread_all(fd, back, 6 * 4096, 0) == 0
+    assert back.raw == b"".join(blocks)
+    faulty.kvsnap_io_pool_destroy(pool)
+
+
+def test_destroying_the_transfer_pool_cancels_waiters_and_waits_for_running(faulty, tmpfile):
+    pool = faulty.kvsnap_io_pool_create(1, 1 << 20)
+    fd = tmpfile.fileno()
+    data = kvgen.random_bytes(7, 4096).tobytes()
+    results = {}
+
+    def write(key):
+        results[key] = faulty.kvsnap_io_pool_transfer(pool, fd, data, 4096, 0, 1, 0)
+
+    faulty.io_stall(1)
+    running = threading.Thread(target=write, args=("running",))
+    waiting = threading.Thread(target=write, args=("waiting",))
+    destroy = threading.Thread(target=faulty.kvsnap_io_pool_destroy, args=(pool,))
+    try:
+        running.start()
+        assert _until(lambda: faulty.io_inside() == 1)
+        waiting.start()
+        time.sleep(0.1)
+        destroy.start()
+        assert _until(lambda: "waiting" in results)
+        assert results["waiting"] == errno.ECANCELED
+        time.sleep(0.1)
+        assert destroy.is_alive() and "running" not in results     # the admitted transfer holds the pool
+    finally:
+        faulty.io_stall(0)
+        for t in (running, waiting, destroy):
+            t.join(10)
+    assert results["running"] == 0 and not destroy.is_alive()
+
+
 def test_native_io_wrapper_round_trip(tmpfile):
     from kvsnap_b200.native_io import get_io_backend
     from kvsnap_b200.crc32c import crc32c
@@ -205,3 +278,36 @@ def test_native_io_wrapper_round_trip(tmpfile):
         backend.pread_all(fd, 10, 10 ** 9)
     with pytest.raises(ValueError):
         get_io_backend("python")
+
+
+def test_native_io_pieces_close_and_fork_rules(tmpfile):
+    """NativeIO's own contract (reference native_io.py:51-151): transfers above the byte budget go in pieces,
+    a closed backend and one inherited across fork refuse work, and close is idempotent."""
+    from unittest.mock import patch
+    from kvsnap_b200.native_io import NativeIO, resolve_io_library
+    backend = NativeIO(resolve_io_library(), workers=3, queue_bytes=4096)
+    fd = tmpfile.fileno()
+    data = kvgen.random_bytes(99, 3 * 4096 + 123).tobytes()
+    backend.pwrite_all(fd, bytearray(data), 5)
+    assert backend.pread_all(fd, len(data), 5) == data
+    target = C.create_string_buffer(len(data))
+    backend.pread_into(fd, C.addressof(target), len(data), 5)
+    backend.pwrite_from(fd, C.addressof(target), len(data), 5 + len(data))
+    assert backend.pread_all(fd, 2 * len(data), 5) == data + data
+    assert backend.crc32c(memoryview(data)) == oracle.crc32c(data)
+    for bad in ((-1, 0), (1, -1), (2**62, 2**62), (1.0, 0)):
+        with pytest.raises(ValueError, match="invalid I/O range"):
+            backend.pread_all(fd, *bad)
+    with pytest.raises(ValueError, match="capacity"):
+        NativeIO(resolve_io_library(), workers=0)
+    with patch("os.getpid", return_value=os.getpid() + 1):
+        with pytest.raises(RuntimeError, match="fork"):
+            backend.pread_all(fd, 4, 0)
+        backend.close()                       # a child leaves the parent's pool alone
+    assert backend.handle
+    backend.close()
+    backend.close()
+    with pytest.raises(RuntimeError, match="closed"):
+        backend.pread_all(fd, 4, 0)
+    with pytest.raises(RuntimeError, match="closed"):
+        backend.crc32c(b"x")
