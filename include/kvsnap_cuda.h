@@ -129,6 +129,11 @@ int kvsnap_pool_wait_many(void* pool, int64_t n, const uint64_t* ids);
 #define KVSNAP_DP_SPLIT2 0x800
 #define KVSNAP_DP_SPLIT4 0x1000
 #define KVSNAP_DP_SPLIT_MASK 0x1800
+/* With KVSNAP_DP_HBM and crc_out: add this call's share of each block's CRC
+   to crc_out as it stands (not cleared first) and leave it raw (no finish
+   step). A save that moves each block in several calls, a range of spans at
+   a time, ends with kvsnap_dp_crc32c_finish. */
+#define KVSNAP_DP_CRC_ACCUMULATE 0x2000
 
 /*
  * One registered layer view, i.e. one span of every packed block. A packed
@@ -198,6 +203,37 @@ int kvsnap_dp_crc32c(const int64_t* addrs, int64_t n, uint64_t block_bytes, uint
    big-endian bytes at out + 32 * i, the bytes of hashlib.sha256(block).digest()
    (the store's content id, store.py:623). One lane hashes one block. */
 int kvsnap_dp_sha256(const int64_t* addrs, int64_t n, uint64_t block_bytes, uint8_t* out, uintptr_t stream);
+
+/* The same hash, one part of every block at a time, so that the bytes of only
+   one part need to be in device memory at once. Call it for parts in order:
+   bytes [done_bytes, done_bytes + part_bytes) of each block of total_bytes,
+   that part starting at addrs[i]. state holds 8 words a block between calls
+   (n * 32 bytes, device memory): the first part (done_bytes 0) starts from
+   the SHA-256 initial value, later ones from state. Parts before the last
+   must be whole 64-byte chunks; the last part (done_bytes + part_bytes ==
+   total_bytes) pads and writes the digests to out as kvsnap_dp_sha256 does,
+   the others write state. */
+int kvsnap_dp_sha256_part(const int64_t* addrs, int64_t n, uint64_t part_bytes, uint64_t done_bytes,
+                          uint64_t total_bytes, uint32_t* state, uint8_t* out, uintptr_t stream);
+
+/* Land one column of n packed blocks from a device slot where each block goes:
+   bytes [0, len) at src + i * src_stride are copied to targets[i] + offset,
+   for i < n. Targets may be pinned host memory (written over the host link by
+   the SMs, one 4 KiB piece a warp step) or device memory. No counterpart in
+   the reference: its save copies whole chunks with cudaMemcpyAsync
+   (kvsnap/connector/dataplane.py:418-427); a bounded save's columns are too
+   small for the copy engine (256 KiB copies to scattered per-block targets ran
+   at 30 GB/s on B200, this kernel at 52.6 with 16 CTAs). src, src_stride,
+   offset, len and every target must be multiples of 16 bytes: a block that
+   is not sets KVSNAP_DP_MISALIGNED in *status and is skipped. `ctas` 0 picks 16. */
+int kvsnap_dp_land(const void* src, int64_t src_stride, const int64_t* targets, int64_t offset, int64_t n,
+                   int64_t len, uint32_t* status, int ctas, uintptr_t stream);
+
+/* Finish raw CRC accumulators that KVSNAP_DP_HBM gathers or scatters left
+   under KVSNAP_DP_CRC_ACCUMULATE: crc[i] becomes block i's CRC32C; with
+   expect not NULL, mismatches set KVSNAP_DP_CRC_MISMATCH in *status. */
+int kvsnap_dp_crc32c_finish(uint32_t* crc, const uint32_t* expect, int64_t n, uint64_t block_bytes,
+                            uint32_t* status, uintptr_t stream);
 
 /*
  * The reference restore kernel's exact interface (copy_kernel.py:43-49): all

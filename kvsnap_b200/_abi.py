@@ -20,6 +20,7 @@ RUNS_SPAN_BYTES = 8 << 10
 PAIRS = 0x400           # with RUNS: spans all of one size in PAIR_SPAN_BYTES, an even count: units of two spans
 PAIR_SPAN_BYTES = (2 << 10, 4 << 10)
 SPLIT2, SPLIT4 = 0x800, 0x1000   # with HBM, without RUNS: units of 1/2 or 1/4 of a span
+CRC_ACCUMULATE = 0x2000          # with HBM: add to the CRC accumulators, leave them raw (kvsnap_dp_crc32c_finish)
 SPLIT_PIECE_BYTES = 16 << 10     # the unit size the plane splits large spans of one size into
 
 
@@ -94,6 +95,9 @@ DP_API = {
     "kvsnap_dp_scatter": ([_P, C.c_int, _U64, _P, _P, _I64, _P, _P, _P, _P, C.c_int, C.c_int, _SZ], C.c_int),
     "kvsnap_dp_crc32c": ([_P, _I64, _U64, _P, _P, _P, C.c_int, C.c_int, _SZ], C.c_int),
     "kvsnap_dp_sha256": ([_P, _I64, _U64, _P, _SZ], C.c_int),
+    "kvsnap_dp_sha256_part": ([_P, _I64, _U64, _U64, _U64, _P, _P, _SZ], C.c_int),
+    "kvsnap_dp_crc32c_finish": ([_P, _P, _I64, _U64, _P, _SZ], C.c_int),
+    "kvsnap_dp_land": ([_P, _I64, _P, _I64, _I64, _I64, _P, C.c_int, _SZ], C.c_int),
     "kvsnap_dp_copy_host_blocks": ([_P, _P, _I64, _P, _P, _P, _P, _I64, C.c_int, _SZ], C.c_int),
     "kvsnap_dp_regroup": ([_P, _P, C.c_int, _P, C.c_int, _P, _I64, _P, C.c_int, _SZ], C.c_int),
     "kvsnap_dp_device_alloc": ([_SZ, C.c_int, C.POINTER(C.c_void_p)], C.c_int),

@@ -1160,10 +1160,39 @@ __device__ __forceinline__ void sha256_words(const unsigned char* p, bool aligne
 // their integer issue rate bounds the hash time, so the compress warp gets a
 // sub-partition to itself. The two warps hand ring slots over with named
 // barriers (bar.arrive / bar.sync, 64 threads): both run the same number of
-// chunks, so every wait is matched.
-constexpr int kShaPairs = 2;          // warp pairs a CTA
-constexpr int kShaSlots = 3;          // ring slots a pair
+// chunks, so every wait is matched. The schedule warp keeps the loads of the
+// next kShaPrefetch chunks in flight, so that its loads (from device memory,
+// or over the host link for blocks in pinned memory) do not hold the rounds up.
+//
+// A launch hashes one part of every block: bytes [done, done + part) of a
+// block of `total` bytes, starting at addrs[i]. The first part starts from the
+// initial hash value, later ones from the 8 state words the previous part
+// left; the last part pads (with the whole block's bit length) and writes the
+// digest. A whole-block hash is the one part [0, total).
+#ifndef KVSNAP_SHA_SLOTS
+#define KVSNAP_SHA_SLOTS 3
+#endif
+#ifndef KVSNAP_SHA_PREFETCH
+#define KVSNAP_SHA_PREFETCH 1
+#endif
+#ifndef KVSNAP_SHA_PAIRS
+#define KVSNAP_SHA_PAIRS 2
+#endif
+constexpr int kShaPairs = KVSNAP_SHA_PAIRS;       // warp pairs a CTA
+constexpr int kShaSlots = KVSNAP_SHA_SLOTS;       // ring slots a pair
+constexpr int kShaPrefetch = KVSNAP_SHA_PREFETCH; // chunks a schedule lane has loads in flight for
 constexpr int kShaSlotWords = 64 * 32;
+static_assert(1 + 2 * kShaSlots * kShaPairs <= 16, "a CTA has 16 named barriers, and barrier 0 is __syncthreads'");
+
+struct ShaPart {
+    const int64_t* addrs;    // where each block's part starts
+    int64_t n;
+    int64_t part;            // bytes of each block in this part
+    int64_t total;           // bytes of a whole block (the length the padding records)
+    int first, last;         // the part starts / ends the blocks
+    uint32_t* state;         // 8 words a block between parts
+    uint8_t* out;            // 32 bytes a block, written by the last part
+};
 
 __device__ __forceinline__ void named_arrive(int id) { asm volatile("bar.arrive %0, 64;" ::"r"(id) : "memory"); }
 __device__ __forceinline__ void named_sync(int id) { asm volatile("bar.sync %0, 64;" ::"r"(id) : "memory"); }
@@ -1177,8 +1206,17 @@ __device__ __forceinline__ uint32_t fadd(uint32_t a, uint32_t one, uint32_t c) {
     return d;
 }
 
-__global__ void __launch_bounds__(64 * kShaPairs) sha256_kernel(const int64_t* addrs, int64_t n,
-                                                               int64_t block_bytes, uint8_t* out, uint32_t one) {
+__device__ __forceinline__ void be_words(const uint4 (&v)[4], uint32_t w[16]) {
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        w[4 * k + 0] = be32(v[k].x);
+        w[4 * k + 1] = be32(v[k].y);
+        w[4 * k + 2] = be32(v[k].z);
+        w[4 * k + 3] = be32(v[k].w);
+    }
+}
+
+__global__ void __launch_bounds__(64 * kShaPairs) sha256_kernel(ShaPart a, uint32_t one) {
     extern __shared__ uint32_t ring[];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int pair = warp >> 1;
@@ -1186,57 +1224,60 @@ __global__ void __launch_bounds__(64 * kShaPairs) sha256_kernel(const int64_t* a
     // within a CTA the compress warps sit on sub-partitions 0 and 2.
     const bool compress = (warp & 1) == 0;
     const int64_t first = ((int64_t)blockIdx.x * kShaPairs + pair) * 32;
-    if (first >= n) return;                          // the whole pair idles together
+    if (first >= a.n) return;                        // the whole pair idles together
     const int64_t i = first + lane;
-    const bool live = i < n;
+    const bool live = i < a.n;
     uint32_t* slots = ring + pair * kShaSlots * kShaSlotWords;
     const int full_id = 1 + pair * 2 * kShaSlots;    // barrier ids: FULL[s], EMPTY[s] per pair
     const int empty_id = full_id + kShaSlots;
-    const int64_t full = block_bytes / 64;
-    const int rest = int(block_bytes - full * 64);
-    const int64_t chunks = full + (rest < 56 ? 1 : 2);
+    const int64_t full = a.part / 64;
+    const int rest = int(a.part - full * 64);
+    const int64_t chunks = full + (a.last ? (rest < 56 ? 1 : 2) : 0);
 
     if (!compress) {
-        const unsigned char* p = reinterpret_cast<const unsigned char*>(addrs[live ? i : n - 1]);
+        const unsigned char* p = reinterpret_cast<const unsigned char*>(a.addrs[live ? i : a.n - 1]);
         const bool aligned = (reinterpret_cast<uintptr_t>(p) & 15) == 0;
-        const uint64_t bits = uint64_t(block_bytes) * 8;
+        const uint64_t bits = uint64_t(a.total) * 8;
         const uint4* q = reinterpret_cast<const uint4*>(p);
-        uint4 next[4];
-        if (aligned && full > 0) {
+        uint4 next[kShaPrefetch][4];
+        if (aligned) {
 #pragma unroll
-            for (int k = 0; k < 4; ++k) next[k] = __ldcs(q + k);
+            for (int u = 0; u < kShaPrefetch; ++u)
+                if (u < full) {
+#pragma unroll
+                    for (int k = 0; k < 4; ++k) next[u][k] = __ldcs(q + 4 * u + k);
+                }
         }
-        for (int64_t c = 0; c < chunks; ++c) {
-            const int s = int(c % kShaSlots);
-            uint32_t w[16];
-            if (aligned && c < full) {
-                // This chunk's words, then the next chunk's loads in flight under the expansion.
+        for (int64_t base = 0; base < chunks; base += kShaPrefetch) {
 #pragma unroll
-                for (int k = 0; k < 4; ++k) {
-                    w[4 * k + 0] = be32(next[k].x);
-                    w[4 * k + 1] = be32(next[k].y);
-                    w[4 * k + 2] = be32(next[k].z);
-                    w[4 * k + 3] = be32(next[k].w);
-                }
-                if (c + 1 < full) {
+            for (int u = 0; u < kShaPrefetch; ++u) {
+                const int64_t c = base + u;
+                if (c >= chunks) break;
+                uint32_t w[16];
+                if (aligned && c < full) {
+                    // This chunk's words, then the loads of the chunk kShaPrefetch on in flight under the expansion.
+                    be_words(next[u], w);
+                    if (c + kShaPrefetch < full) {
 #pragma unroll
-                    for (int k = 0; k < 4; ++k) next[k] = __ldcs(q + 4 * (c + 1) + k);
+                        for (int k = 0; k < 4; ++k) next[u][k] = __ldcs(q + 4 * (c + kShaPrefetch) + k);
+                    }
+                } else {
+                    sha256_words(p, aligned, c, full, rest, bits, w);
                 }
-            } else {
-                sha256_words(p, aligned, c, full, rest, bits, w);
+                const int s = int(c % kShaSlots);
+                if (c >= kShaSlots) named_sync(empty_id + s);
+                uint32_t* slot = slots + s * kShaSlotWords + lane;
+#pragma unroll
+                for (int t = 0; t < 64; ++t) {
+                    if (t >= 16) {
+                        const uint32_t x = w[(t + 1) & 15], y = w[(t + 14) & 15];
+                        w[t & 15] += (rotr(x, 7) ^ rotr(x, 18) ^ (x >> 3)) + w[(t + 9) & 15] +
+                                     (rotr(y, 17) ^ rotr(y, 19) ^ (y >> 10));
+                    }
+                    slot[t * 32] = w[t & 15] + kSha256K[t];
+                }
+                named_arrive(full_id + s);
             }
-            if (c >= kShaSlots) named_sync(empty_id + s);
-            uint32_t* slot = slots + s * kShaSlotWords + lane;
-#pragma unroll
-            for (int t = 0; t < 64; ++t) {
-                if (t >= 16) {
-                    const uint32_t x = w[(t + 1) & 15], y = w[(t + 14) & 15];
-                    w[t & 15] += (rotr(x, 7) ^ rotr(x, 18) ^ (x >> 3)) + w[(t + 9) & 15] +
-                                 (rotr(y, 17) ^ rotr(y, 19) ^ (y >> 10));
-                }
-                slot[t * 32] = w[t & 15] + kSha256K[t];
-            }
-            named_arrive(full_id + s);
         }
         // Match the compress warp's last releases, so every barrier generation completes.
         for (int64_t c = chunks > kShaSlots ? chunks - kShaSlots : 0; c < chunks; ++c)
@@ -1244,24 +1285,31 @@ __global__ void __launch_bounds__(64 * kShaPairs) sha256_kernel(const int64_t* a
         return;
     }
     uint32_t h[8] = {0x6a09e667, 0xbb67ae85, 0x3c6ef372, 0xa54ff53a, 0x510e527f, 0x9b05688c, 0x1f83d9ab, 0x5be0cd19};
+    if (!a.first && live) {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) h[j] = a.state[8 * i + j];
+    }
     for (int64_t c = 0; c < chunks; ++c) {
         const int s = int(c % kShaSlots);
         named_sync(full_id + s);
         const uint32_t* slot = slots + s * kShaSlotWords + lane;
-        uint32_t a = h[0], b = h[1], cc = h[2], d = h[3], e = h[4], f = h[5], g = h[6], k = h[7];
+        uint32_t a0 = h[0], b = h[1], cc = h[2], d = h[3], e = h[4], f = h[5], g = h[6], k = h[7];
 #pragma unroll
         for (int t = 0; t < 64; ++t) {
-            // The round, reassociated so the new e is one add after Sigma1 and Ch:
-            // e' = (d + h + W + K) + Sigma1(e) + Ch(e,f,g), with d + h + W + K
-            // formed off the critical path from values known rounds earlier.
-            const uint32_t hk = fadd(k, one, slot[t * 32]);
-            const uint32_t dhk = fadd(d, one, hk);
+            // The round, reassociated so the new e is one three-input add after
+            // Sigma1 and Ch: e' = (d + h + W + K) + Sigma1(e) + Ch(e,f,g), with
+            // d + h + W + K formed off the critical path from values known rounds
+            // earlier. T1 = (h + W + K) + Ch + Sigma1 goes to the FMA pipe, beside
+            // the rotations on the ALU; placing e' there too lengthened the chain
+            // (34.8 and 36.2 ms a session instead of 33.9 in a variant sweep).
+            const uint32_t hk = k + slot[t * 32];
+            const uint32_t dhk = d + hk;
             const uint32_t ch = (e & f) ^ (~e & g);
             const uint32_t s1 = rotr(e, 6) ^ rotr(e, 11) ^ rotr(e, 25);
-            const uint32_t e_new = fadd(s1, one, fadd(ch, one, dhk));
+            const uint32_t e_new = dhk + ch + s1;
             const uint32_t t1 = fadd(s1, one, fadd(ch, one, hk));
-            const uint32_t s0 = rotr(a, 2) ^ rotr(a, 13) ^ rotr(a, 22);
-            const uint32_t maj = (a & b) ^ (a & cc) ^ (b & cc);
+            const uint32_t s0 = rotr(a0, 2) ^ rotr(a0, 13) ^ rotr(a0, 22);
+            const uint32_t maj = (a0 & b) ^ (a0 & cc) ^ (b & cc);
             const uint32_t a_new = t1 + s0 + maj;
             k = g;
             g = f;
@@ -1269,16 +1317,55 @@ __global__ void __launch_bounds__(64 * kShaPairs) sha256_kernel(const int64_t* a
             e = e_new;
             d = cc;
             cc = b;
-            b = a;
-            a = a_new;
+            b = a0;
+            a0 = a_new;
         }
         named_arrive(empty_id + s);
-        h[0] += a; h[1] += b; h[2] += cc; h[3] += d; h[4] += e; h[5] += f; h[6] += g; h[7] += k;
+        h[0] += a0; h[1] += b; h[2] += cc; h[3] += d; h[4] += e; h[5] += f; h[6] += g; h[7] += k;
     }
-    if (live) {
-        uint32_t* o = reinterpret_cast<uint32_t*>(out + 32 * i);
+    if (!live) return;
+    if (a.last) {
+        uint32_t* o = reinterpret_cast<uint32_t*>(a.out + 32 * i);
 #pragma unroll
         for (int j = 0; j < 8; ++j) o[j] = be32(h[j]);
+    } else {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) a.state[8 * i + j] = h[j];
+    }
+}
+
+// ---- landing a column of packed blocks -------------------------------------------
+//
+// The bounded staged save moves each block a column at a time, so its copies
+// to the targets are small (a few hundred KiB each). The SMs store them
+// instead of the copy engine: a warp moves one 4 KiB piece of one block a step,
+// 16 bytes a lane, eight loads in flight before the eight stores.
+__global__ void __launch_bounds__(256) land_kernel(const char* src, int64_t stride, const int64_t* targets,
+                                                   int64_t offset, int64_t n, int64_t len, uint32_t* status) {
+    const int lane = threadIdx.x & 31;
+    const int64_t pieces = (len + 4095) / 4096;
+    const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
+    for (int64_t u = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); u < n * pieces; u += warps) {
+        const int64_t i = u / pieces, p = u - i * pieces;
+        const int64_t target = targets[i] + offset;
+        if (target & 15) {
+            if (lane == 0 && p == 0) flag(status, KVSNAP_DP_MISALIGNED);
+            continue;
+        }
+        const char* from = src + i * stride + p * 4096;
+        char* to = reinterpret_cast<char*>(target) + p * 4096;
+        const int64_t left = len - p * 4096;
+        uint4 v[8];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+            const int64_t at = int64_t(k * 32 + lane) * 16;
+            if (at < left) v[k] = __ldcs(reinterpret_cast<const uint4*>(from + at));
+        }
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+            const int64_t at = int64_t(k * 32 + lane) * 16;
+            if (at < left) __stcs(reinterpret_cast<uint4*>(to + at), v[k]);
+        }
     }
 }
 
@@ -1475,7 +1562,9 @@ void spans_launch(const kvsnap_span* spans, int nspans, uint64_t block_bytes, co
         const bool hbm = (vec & KVSNAP_DP_HBM) != 0;
         const bool runs = (vec & KVSNAP_DP_RUNS) != 0, pairs = (vec & KVSNAP_DP_PAIRS) != 0;
         const int split = (vec & KVSNAP_DP_SPLIT_MASK) / KVSNAP_DP_SPLIT2;   // log2 of the pieces a span
-        vec &= ~(KVSNAP_DP_HBM | KVSNAP_DP_RUNS | KVSNAP_DP_PAIRS | KVSNAP_DP_SPLIT_MASK);
+        const bool accumulate = (vec & KVSNAP_DP_CRC_ACCUMULATE) != 0;
+        vec &= ~(KVSNAP_DP_HBM | KVSNAP_DP_RUNS | KVSNAP_DP_PAIRS | KVSNAP_DP_SPLIT_MASK | KVSNAP_DP_CRC_ACCUMULATE);
+        if (accumulate && (!hbm || expect)) throw Fail{"KVSNAP_DP_CRC_ACCUMULATE needs KVSNAP_DP_HBM and no expect"};
         if (split && (!hbm || runs || split > 2)) throw Fail{"split spans need KVSNAP_DP_HBM, without KVSNAP_DP_RUNS"};
         if (n < 0 || nspans <= 0 || !spans) throw Fail{"invalid span table"};
         if (pairs && (!hbm || !runs)) throw Fail{"pairs of spans need KVSNAP_DP_HBM and KVSNAP_DP_RUNS"};
@@ -1487,7 +1576,7 @@ void spans_launch(const kvsnap_span* spans, int nspans, uint64_t block_bytes, co
         if (expect && !crc) throw Fail{"verifying needs a CRC output"};
         const int sms = enter_stream(stream);
         cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-        if (crc) check(cudaMemsetAsync(crc, 0, sizeof(uint32_t) * size_t(n), s));
+        if (crc && !accumulate) check(cudaMemsetAsync(crc, 0, sizeof(uint32_t) * size_t(n), s));
         SpanArgs a{spans, nspans, blocks, packed, n, valid, crc, gate, status, pairs ? 1 : 0, split};
         if (hbm) {
             auto grid_of = [&](int64_t blocks_of_work, int warps) {
@@ -1521,7 +1610,7 @@ void spans_launch(const kvsnap_span* spans, int nspans, uint64_t block_bytes, co
                 kernel<<<grid_of(body, warps), 32 * warps, bytes, s>>>(a);
                 check(cudaGetLastError());
             }
-            if (crc) finish(crc, expect, n, block_bytes, status, s, kSegUnscale);
+            if (crc && !accumulate) finish(crc, expect, n, block_bytes, status, s, kSegUnscale);
             return;
         }
         const int grid = grid_for(n * nspans, ctas, sms);
@@ -1613,21 +1702,68 @@ extern "C" int kvsnap_dp_crc32c(const int64_t* addrs, int64_t n, uint64_t block_
     });
 }
 
+namespace {
+
+void sha_launch(const int64_t* addrs, int64_t n, uint64_t part, uint64_t done, uint64_t total, uint32_t* state,
+                uint8_t* out, uintptr_t stream) {
+    if (n < 0 || done > total || part > total - done) throw Fail{"invalid digest request"};
+    if (n == 0) return;
+    const bool last = done + part == total;
+    if (!addrs) throw Fail{"digests need addresses"};
+    if (!last && (part % 64 || !state)) throw Fail{"a digest part before the last needs whole 64-byte chunks and a state"};
+    if (done && (done % 64 || !state)) throw Fail{"a digest part after the first needs a state at a chunk boundary"};
+    if (last && !out) throw Fail{"digests need an output"};
+    if (last && (reinterpret_cast<uintptr_t>(out) & 3)) throw Fail{"digest output must be 4-byte aligned"};
+    if (state && (reinterpret_cast<uintptr_t>(state) & 3)) throw Fail{"digest state must be 4-byte aligned"};
+    enter_stream(stream);
+    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    constexpr int smem = kShaPairs * kShaSlots * kShaSlotWords * int(sizeof(uint32_t));
+    configure_once(reinterpret_cast<const void*>(sha256_kernel), smem);
+    const ShaPart a{addrs, n, int64_t(part), int64_t(total), done == 0, last, state, out};
+    const int64_t per_cta = 32 * kShaPairs;
+    sha256_kernel<<<int((n + per_cta - 1) / per_cta), 64 * kShaPairs, smem, s>>>(a, 1u);
+    check(cudaGetLastError());
+}
+
+}  // namespace
+
 extern "C" int kvsnap_dp_sha256(const int64_t* addrs, int64_t n, uint64_t block_bytes, uint8_t* out,
                                 uintptr_t stream) {
+    return guarded([&] { sha_launch(addrs, n, block_bytes, 0, block_bytes, nullptr, out, stream); });
+}
+
+extern "C" int kvsnap_dp_sha256_part(const int64_t* addrs, int64_t n, uint64_t part_bytes, uint64_t done_bytes,
+                                     uint64_t total_bytes, uint32_t* state, uint8_t* out, uintptr_t stream) {
+    return guarded([&] { sha_launch(addrs, n, part_bytes, done_bytes, total_bytes, state, out, stream); });
+}
+
+extern "C" int kvsnap_dp_land(const void* src, int64_t src_stride, const int64_t* targets, int64_t offset,
+                              int64_t n, int64_t len, uint32_t* status, int ctas, uintptr_t stream) {
     return guarded([&] {
-        if (n < 0) throw Fail{"invalid digest request"};
-        if (n == 0) return;
-        if (!addrs || !out) throw Fail{"digests need addresses and an output"};
-        if (reinterpret_cast<uintptr_t>(out) & 3) throw Fail{"digest output must be 4-byte aligned"};
-        enter_stream(stream);
-        cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-        constexpr int smem = kShaPairs * kShaSlots * kShaSlotWords * int(sizeof(uint32_t));
-        configure_once(reinterpret_cast<const void*>(sha256_kernel), smem);
-        const int64_t per_cta = 32 * kShaPairs;
-        sha256_kernel<<<int((n + per_cta - 1) / per_cta), 64 * kShaPairs, smem, s>>>(addrs, n,
-                                                                                    int64_t(block_bytes), out, 1u);
+        if (n < 0 || len < 0 || offset < 0 || src_stride < 0) throw Fail{"invalid landing request"};
+        if (n == 0 || len == 0) return;
+        if (!src || !targets) throw Fail{"landing needs a source and targets"};
+        if (n > 1 && src_stride < len) throw Fail{"landing source blocks overlap (stride below the length)"};
+        if ((reinterpret_cast<uintptr_t>(src) | uint64_t(src_stride) | uint64_t(offset) | uint64_t(len)) & 15)
+            throw Fail{"landing needs 16-byte aligned sources, strides, offsets and lengths"};
+        const int sms = enter_stream(stream);
+        const int64_t pieces = n * ((len + 4095) / 4096);
+        const int64_t want = (pieces + 7) / 8;
+        const int grid = ctas > 0 ? ctas : int(want < 16 ? want : (16 < sms ? 16 : sms));
+        land_kernel<<<grid, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+            static_cast<const char*>(src), src_stride, targets, offset, n, len, status);
         check(cudaGetLastError());
+    });
+}
+
+extern "C" int kvsnap_dp_crc32c_finish(uint32_t* crc, const uint32_t* expect, int64_t n, uint64_t block_bytes,
+                                       uint32_t* status, uintptr_t stream) {
+    return guarded([&] {
+        if (n < 0) throw Fail{"invalid CRC finish request"};
+        if (n == 0) return;
+        if (!crc) throw Fail{"CRC finish needs the accumulators"};
+        enter_stream(stream);
+        finish(crc, expect, n, block_bytes, status, reinterpret_cast<cudaStream_t>(stream), kSegUnscale);
     });
 }
 

@@ -465,9 +465,47 @@ def _layer_record(name, tensor, block_size, device):
             "bytes": shape[1] * shape[2] * shape[3] * tensor.element_size()}
 
 
+def column_plan(span_bytes, n, slot_bytes):
+    """How a staged save moves through device slots of ``slot_bytes`` when its blocks do not fit at once.
+
+    Every block of a group is moved a column at a time: a column is a run of
+    consecutive spans, the same for every block, so a slot holds that column
+    of ``group`` blocks, each ``stride`` bytes apart. Columns end at a multiple
+    of 64 bytes into the block (SHA-256 goes in 64-byte chunks), except the
+    last, and are about ``slot_bytes / n`` bytes, at least one span. Returns
+    ``(group, stride, columns)``, each column ``(first span, end span, byte
+    offset in the block, bytes)``; ``group * stride <= slot_bytes`` unless one
+    column of one block is larger than a slot.
+    """
+    if n <= 0 or not span_bytes:
+        raise ValueError("a column plan needs blocks and spans")
+    target = max(64, slot_bytes // n // 64 * 64)
+    columns, first, offset, size = [], 0, 0, 0
+    for s, nbytes in enumerate(span_bytes):
+        if size and size + nbytes > target and offset % 64 == 0:
+            columns.append((first, s, offset - size, size))
+            first, size = s, 0
+        size += nbytes
+        offset += nbytes
+    columns.append((first, len(span_bytes), offset - size, size))
+    stride = (max(c[3] for c in columns) + 15) // 16 * 16
+    group = max(1, min(n, slot_bytes // stride))
+    return group, stride, columns
+
+
 def _u32(values):
     """Python ints in [0, 2**32) as the int32 bit patterns a torch int32 tensor holds."""
     return [v - (1 << 32) if v >= 1 << 31 else v for v in values]
+
+
+class _SaveJob:
+    """One save's state: what it moves, and the device buffers its digests still read."""
+
+    def __init__(self, block_ids, targets, valid, hashed, known, digests):
+        self.block_ids, self.targets, self.valid = block_ids, targets, valid
+        self.hashed, self.known, self.digests = hashed, known, digests
+        self.status = self.crc = self.digest = self.side = self.keep = None
+        self.rehash_from = []
 
 
 class TorchBlockDataPlane:
@@ -485,14 +523,24 @@ class TorchBlockDataPlane:
     scatters them from there (the default: copy engines in both directions at
     once reach about twice what one direction does, SM reads of host memory
     beside a copy do not); ``"direct"`` has the scatter kernel read pinned
-    blocks in place. A restore with ``expected_crc32c`` stages every block, so
-    the check completes before any KV byte changes.
+    blocks in place. A restore with ``expected_crc32c`` checks every block
+    before any KV byte changes.
+
+    ``staging_bytes`` bounds the device memory one call stages through (512
+    MiB by default; the engine's KV cache owns the rest of the GPU): a save
+    whose packed blocks exceed it moves through a ring of ``staging_slots``
+    device slots a column of spans at a time; a verified restore that exceeds
+    it checks the CRCs over the pinned blocks first and then restores through
+    the two-slot chunk ring; ``digest`` hashes the pinned blocks in place. A
+    restore's chunk ring holds two ``chunk_bytes`` chunks.
     """
 
     save_mode = "staged"
     restore_mode = "staged"
+    staging_slots = 4
 
-    def __init__(self, caches, block_size, capacity_bytes, *, save_mode=None, restore_mode=None, ctas=0):
+    def __init__(self, caches, block_size, capacity_bytes, *, save_mode=None, restore_mode=None, ctas=0,
+                 staging_bytes=512 << 20):
         import torch
         if not caches:
             raise ValueError("empty KV cache registration")
@@ -507,6 +555,9 @@ class TorchBlockDataPlane:
         if self.save_mode not in ("staged", "direct") or self.restore_mode not in ("staged", "direct"):
             raise ValueError("save_mode and restore_mode are 'staged' or 'direct'")
         self.ctas = ctas
+        if type(staging_bytes) is not int or staging_bytes < (1 << 20):
+            raise ValueError("staging_bytes must be an int of at least 1 MiB")
+        self.staging_bytes = staging_bytes
         # Kernels that read or write pinned memory in place are bound by the host
         # link, which 16-32 CTAs already saturate; the rest of the GPU stays free
         # for the engine and the SHA-256 kernel.
@@ -770,6 +821,12 @@ class TorchBlockDataPlane:
                                 progress.append((done, (n - last) * size))
                         for allocation in {id(a): a for a, _ in sources}.values():
                             allocation.mark(kernels.cuda_stream)
+                    elif verified and n * size > self.staging_bytes:
+                        # Larger than the staging bound: check every block where it lies, then the chunk ring.
+                        vec = self._vec_for(addresses)
+                        table = torch.tensor(addresses, dtype=torch.int64).pin_memory().to(device, non_blocking=True)
+                        self._verify(table, n, expected_crc32c, status, vec, self.host_ctas)
+                        launches, done = self._staged_chunks(sources, ids, n, per_launch, status, progress)
                     elif verified:
                         stage = torch.empty(n * size, dtype=torch.uint8, device=device)
                         stage.record_stream(copies)
@@ -853,14 +910,16 @@ class TorchBlockDataPlane:
                 progress.append((done, (n - last) * size))
         return launches, done
 
-    def _verify(self, table, n, expected, status, vec):
-        """CRC32C of the staged blocks (table[:n]) against ``expected``; raises before any scatter is queued."""
+    def _verify(self, table, n, expected, status, vec, ctas=None):
+        """CRC32C of the blocks at table[:n] (device staging, or pinned memory read over the host link) against
+        ``expected``; raises before any scatter is queued."""
         torch = self.torch
         lib = _dp(self.pool.lib)
         crc = torch.empty(n, dtype=torch.int32, device=table.device)
         expect = torch.tensor(_u32(expected), dtype=torch.int32).pin_memory().to(table.device, non_blocking=True)
         self._check(lib.kvsnap_dp_crc32c(table.data_ptr(), n, self.block_bytes, crc.data_ptr(), expect.data_ptr(),
-                                         status.data_ptr(), vec, self.ctas, torch.cuda.current_stream().cuda_stream))
+                                         status.data_ptr(), vec, self.ctas if ctas is None else ctas,
+                                         torch.cuda.current_stream().cuda_stream))
         flags = int(status.item())          # synchronises the copy stream
         if flags & _abi.CRC_MISMATCH:
             got = [v & 0xFFFFFFFF for v in crc.tolist()]
@@ -881,19 +940,26 @@ class TorchBlockDataPlane:
         are written as zeros, so a snapshot never carries stale KV. Returns the
         number of device-to-host copies (staged mode: one per run of adjacent
         targets in one allocation, per ``chunk_bytes`` of blocks) or of kernel
-        launches (direct mode).
+        launches (direct mode; and, above ``staging_bytes``, the column
+        landings).
 
         ``digests``: a list that receives ``(sha256 hex, crc32c)`` for each
         packed block, the store's content id and checksum, computed on the GPU
         from the same bytes the targets receive. A :class:`PendingDigests`
         instead returns as soon as the targets are written (the point at which
         the connector may free the GPU blocks) while the SHA-256 kernel still
-        runs; its ``result()`` waits for it and returns the list.
+        runs; its ``result()`` waits for it and returns the list. The targets
+        must stay allocated until then.
 
         ``cache`` (a :class:`DigestCache`) with ``generations[i]`` for each
         block: full blocks found in the cache are not hashed again (their
         CRC32C, computed by the gather anyway, must equal the cached one), and
         every full block's digest is stored for the next save.
+
+        Device staging is bounded by ``staging_bytes``: a session that does not
+        fit moves through a ring of device slots a column (a run of spans of
+        every block) at a time, the SHA-256 of each block carried from column
+        to column.
         """
         torch = self.torch
         self._validate_ids(block_ids)
@@ -902,19 +968,16 @@ class TorchBlockDataPlane:
             raise ValueError("block count does not cover computed tokens")
         if not block_ids:
             return 0
-        spans = self._spans()
-        stream = self._scatter_targets()
-        lib = _dp(self.pool.lib)
-        device = self._device()
-        n, size = len(block_ids), self.block_bytes
-        valid = num_kv_tokens % self.block_size
-        per_chunk = max(1, min(n, chunk_bytes // size))
         if (cache is None) != (generations is None):
             raise ValueError("a digest cache needs one generation per block, and generations a cache")
-        if generations is not None and len(generations) != n:
+        if generations is not None and len(generations) != len(block_ids):
             raise ValueError("one generation per block is required")
         if cache is not None and digests is None:
             raise ValueError("a digest cache serves digests: pass digests= as well")
+        spans = self._spans()
+        stream = self._scatter_targets()
+        n, size = len(block_ids), self.block_bytes
+        valid = num_kv_tokens % self.block_size
         # Full blocks only: the last block's tail slots are zeroed and change with the next token.
         full = n if valid == 0 else n - 1
         known = {}
@@ -923,97 +986,241 @@ class TorchBlockDataPlane:
                 entry = cache.get(block_ids[i], generations[i])
                 if entry is not None:
                     known[i] = entry
-        hashed = [i for i in range(n) if i not in known]
-        direct = self.save_mode == "direct" and digests is None
-        copies = 0
+        job = _SaveJob(block_ids, targets, valid, [i for i in range(n) if i not in known], known, digests is not None)
         with torch.cuda.stream(stream):
-            status = torch.zeros(1, dtype=torch.int32, device=device)
-            crc = torch.empty(n, dtype=torch.int32, device=device) if digests is not None else None
-            if direct:
-                for allocation, offset in targets:
-                    allocation._open()
-                    if offset < 0 or offset + size > allocation.size:
-                        raise ValueError("save target outside its allocation")
-                write_to = [a.pointer + o for a, o in targets]
-            else:
-                stage = torch.empty(n * size, dtype=torch.uint8, device=device)
-                write_to = [stage.data_ptr() + i * size for i in range(n)]
-            vec = self._vec_for(write_to)
-            if not direct and vec == 16:
-                vec |= self._hbm
-            table = torch.tensor(list(block_ids) + write_to, dtype=torch.int64).pin_memory().to(
-                device, non_blocking=True)
+            job.status = torch.zeros(1, dtype=torch.int32, device=self._device())
+            job.crc = torch.zeros(n, dtype=torch.int32, device=self._device()) if job.digests else None
             try:
-                if direct:
-                    for first in range(0, n, per_chunk):
-                        last = min(n, first + per_chunk)
-                        self._check(lib.kvsnap_dp_gather(
-                            spans.data_ptr(), len(self.layers), size, table[first:].data_ptr(),
-                            table[n + first:].data_ptr(), last - first, valid if last == n else 0, 0,
-                            status.data_ptr(), vec, self.host_ctas, stream.cuda_stream))
-                        copies += 1
-                    for allocation in {id(a): a for a, _ in targets}.values():
-                        allocation.mark()
+                if self.save_mode == "direct" and not job.digests:
+                    copies = self._save_direct(job, spans, chunk_bytes)
+                elif n * size <= self.staging_bytes or self._span_vec != 16:
+                    copies = self._save_whole(job, spans, chunk_bytes)
                 else:
-                    self._check(lib.kvsnap_dp_gather(
-                        spans.data_ptr(), len(self.layers), size, table.data_ptr(), table[n:].data_ptr(), n, valid,
-                        crc.data_ptr() if crc is not None else 0, status.data_ptr(), vec, self.ctas,
-                        stream.cuda_stream))
-                    if digests is not None:
-                        side = self._sha_stream()
-                        addresses = table[n:] if not known else torch.tensor(
-                            [write_to[i] for i in hashed], dtype=torch.int64).pin_memory().to(device, non_blocking=True)
-                        digest = self._sha256_after(stage, addresses, len(hashed), stream, side)
-                    entries = []
-                    for first in range(0, n, per_chunk):
-                        for i, j in self._runs(targets, first, min(n, first + per_chunk), size):
-                            allocation, offset = targets[i]
-                            entries.append((allocation, offset, stage.data_ptr() + i * size, (j - i) * size))
-                    self.pool.copy_many(entries, to_host=True)
-                    copies += len(entries)
+                    copies = self._save_columns(job)
                 done = torch.cuda.Event()
                 done.record()
             except BaseException:
                 stream.synchronize()
+                if job.side is not None:
+                    job.side.synchronize()
                 raise
         done.synchronize()
         self.pool.wait_many({id(a): a for a, _ in targets}.values())
-        self._status_error(status)
-        if digests is not None:
+        self._status_error(job.status)
+        if job.digests:
             finished = torch.cuda.Event()
-            finished.record(side)
+            finished.record(job.side)
             pending = digests if isinstance(digests, PendingDigests) else PendingDigests()
             keys = [(block_ids[i], generations[i]) for i in range(full)] if cache is not None else []
-            pending._bind(finished, lambda: self._digests(crc, digest, hashed, known, stage, write_to, cache, keys))
+            pending._bind(finished, lambda: self._digests(job, cache, keys))
             if not isinstance(digests, PendingDigests):
                 digests.extend(pending.result())
         return copies
 
-    def _digests(self, crc, digest, hashed, known, stage, write_to, cache, keys):
-        """The save's ``(sha256 hex, crc32c)`` list, once its SHA-256 kernel has finished.
+    def _save_direct(self, job, spans, chunk_bytes):
+        """The gather kernel writes the pinned targets in place over the host link."""
+        torch = self.torch
+        lib = _dp(self.pool.lib)
+        stream = self._copy_stream
+        n, size = len(job.block_ids), self.block_bytes
+        for allocation, offset in job.targets:
+            allocation._open()
+            if offset < 0 or offset + size > allocation.size:
+                raise ValueError("save target outside its allocation")
+        write_to = [a.pointer + o for a, o in job.targets]
+        vec = self._vec_for(write_to)
+        table = torch.tensor(list(job.block_ids) + write_to, dtype=torch.int64).pin_memory().to(
+            self._device(), non_blocking=True)
+        per_chunk = max(1, min(n, chunk_bytes // size))
+        launches = 0
+        for first in range(0, n, per_chunk):
+            last = min(n, first + per_chunk)
+            self._check(lib.kvsnap_dp_gather(
+                spans.data_ptr(), len(self.layers), size, table[first:].data_ptr(), table[n + first:].data_ptr(),
+                last - first, job.valid if last == n else 0, 0, job.status.data_ptr(), vec, self.host_ctas,
+                stream.cuda_stream))
+            launches += 1
+        for allocation in {id(a): a for a, _ in job.targets}.values():
+            allocation.mark()
+        return launches
 
-        Blocks served from ``cache`` must have kept their CRC32C; one that has
-        not is hashed now from the staging buffer, which is still alive.
+    def _save_whole(self, job, spans, chunk_bytes):
+        """Every block gathered into device staging at once; the copy engine lands it, SHA-256 reads it in place."""
+        torch = self.torch
+        lib = _dp(self.pool.lib)
+        stream = self._copy_stream
+        n, size = len(job.block_ids), self.block_bytes
+        stage = torch.empty(n * size, dtype=torch.uint8, device=self._device())
+        write_to = [stage.data_ptr() + i * size for i in range(n)]
+        vec = self._vec_for(write_to)
+        if vec == 16:
+            vec |= self._hbm
+        table = torch.tensor(list(job.block_ids) + write_to, dtype=torch.int64).pin_memory().to(
+            self._device(), non_blocking=True)
+        self._check(lib.kvsnap_dp_gather(
+            spans.data_ptr(), len(self.layers), size, table.data_ptr(), table[n:].data_ptr(), n, job.valid,
+            job.crc.data_ptr() if job.crc is not None else 0, job.status.data_ptr(), vec, self.ctas,
+            stream.cuda_stream))
+        if job.digests:
+            job.side = self._sha_stream()
+            addresses = table[n:] if len(job.hashed) == n else torch.tensor(
+                [write_to[i] for i in job.hashed], dtype=torch.int64).pin_memory().to(self._device(), non_blocking=True)
+            job.digest = self._sha256_after(stage, addresses, len(job.hashed), stream, job.side)
+        job.keep = stage
+        job.rehash_from = write_to
+        per_chunk = max(1, min(n, chunk_bytes // size))
+        entries = []
+        for first in range(0, n, per_chunk):
+            for i, j in self._runs(job.targets, first, min(n, first + per_chunk), size):
+                allocation, offset = job.targets[i]
+                entries.append((allocation, offset, stage.data_ptr() + i * size, (j - i) * size))
+        self.pool.copy_many(entries, to_host=True)
+        return len(entries)
+
+    def _save_columns(self, job):
+        """A save larger than ``staging_bytes``: a ring of device slots, one column of a group of blocks a slot.
+
+        For each (group, column): the gather writes the column of every block
+        of the group into a free slot (CRC shares accumulate per block), a
+        landing kernel stores it at each target's column offset in pinned
+        memory (columns are too small for the copy engine to run at the link
+        rate), and the SHA-256 kernel advances every block's hash over it from
+        the state the previous column left. A slot is reused once it has
+        landed and its hash part is done, so device memory stays within
+        ``staging_bytes`` while all blocks hash at once. Needs 16-byte aligned
+        spans and targets (the CRC shares of the segment kernels accumulate
+        across calls; the landing stores are 16 bytes).
         """
         torch = self.torch
-        crcs = [v & 0xFFFFFFFF for v in crc.cpu().tolist()]
-        raw = digest.cpu().numpy().tobytes()
+        lib = _dp(self.pool.lib)
+        stream = self._copy_stream
+        device = self._device()
+        n, size = len(job.block_ids), self.block_bytes
+        slots = self.staging_slots
+        group, stride, columns, tables, flags = self._columns(n)
+        slot_bytes = group * stride
+        with self.pool.operation():
+            # The pool lock keeps every target open until the kernels writing it are fenced under it.
+            for allocation, offset in job.targets:
+                allocation._open()
+                if offset < 0 or offset + size > allocation.size:
+                    raise RuntimeError("copy outside pinned allocation")
+            targets = [a.pointer + o for a, o in job.targets]
+            if any(t % 16 for t in targets):
+                raise ValueError("packed blocks must be 16-byte aligned for a bounded save")
+            ring = torch.empty(slots * slot_bytes, dtype=torch.uint8, device=device)
+            base = ring.data_ptr()
+            groups = [(g0, min(n, g0 + group)) for g0 in range(0, n, group)]
+            hashed_in = [[i for i in job.hashed if g0 <= i < g1] for g0, g1 in groups]
+            # One upload: block ids, target addresses, each slot's block addresses, and for a group whose
+            # blocks are not all hashed, per slot the addresses of those that are.
+            host = list(job.block_ids) + targets
+            slot_at = len(host)
+            host += [base + r * slot_bytes + k * stride for r in range(slots) for k in range(group)]
+            own_table = {}
+            if job.digests:
+                for g, (g0, g1) in enumerate(groups):
+                    if hashed_in[g] and hashed_in[g] != list(range(g0, g1)):
+                        for r in range(slots):
+                            own_table[g, r] = len(host)
+                            host += [base + r * slot_bytes + (i - g0) * stride for i in hashed_in[g]]
+            table = torch.tensor(host, dtype=torch.int64).pin_memory().to(device, non_blocking=True)
+            words = table.data_ptr()
+            state = None
+            if job.digests:
+                job.side = self._sha_stream()
+                ring.record_stream(job.side)
+                table.record_stream(job.side)
+                # The hash parts write these on the side stream after this call returns: allocated there, and
+                # held by the job until its digests are read, so no other allocation can take them meanwhile.
+                with torch.cuda.stream(job.side):
+                    job.digest = torch.empty(max(1, len(job.hashed)) * 32, dtype=torch.uint8, device=device)
+                    state = torch.empty(max(1, len(job.hashed)) * 8, dtype=torch.int32, device=device)
+            launches, hashed_before, unit = 0, 0, 0
+            read = []          # per unit: the event after which its slot's hash part is done, or None
+            for g, (g0, g1) in enumerate(groups):
+                for j, (s0, s1, offset, nbytes) in enumerate(columns):
+                    r = unit % slots
+                    slot = base + r * slot_bytes
+                    slot_table = words + 8 * (slot_at + r * group)
+                    if unit >= slots and read[unit - slots] is not None:
+                        stream.wait_event(read[unit - slots])
+                    self._check(lib.kvsnap_dp_gather(
+                        tables[j].data_ptr(), s1 - s0, size, words + 8 * g0, slot_table, g1 - g0,
+                        job.valid if g1 == n else 0, job.crc.data_ptr() + 4 * g0 if job.crc is not None else 0,
+                        job.status.data_ptr(), flags[j], self.ctas, stream.cuda_stream))
+                    self._check(lib.kvsnap_dp_land(slot, stride, words + 8 * (n + g0), offset, g1 - g0, nbytes,
+                                                   job.status.data_ptr(), 0, stream.cuda_stream))
+                    launches += 1
+                    event = None
+                    if job.digests and hashed_in[g]:
+                        gathered = torch.cuda.Event()
+                        gathered.record(stream)
+                        job.side.wait_event(gathered)
+                        at = words + 8 * own_table[g, r] if (g, r) in own_table else slot_table
+                        last = j == len(columns) - 1
+                        self._check(lib.kvsnap_dp_sha256_part(
+                            at, len(hashed_in[g]), nbytes, offset, size, state.data_ptr() + 32 * hashed_before,
+                            job.digest.data_ptr() + 32 * hashed_before if last else 0, job.side.cuda_stream))
+                        event = torch.cuda.Event()
+                        event.record(job.side)
+                    read.append(event)
+                    unit += 1
+                hashed_before += len(hashed_in[g])
+            if job.crc is not None:
+                self._check(lib.kvsnap_dp_crc32c_finish(job.crc.data_ptr(), 0, n, size, job.status.data_ptr(),
+                                                        stream.cuda_stream))
+            for allocation in {id(a): a for a, _ in job.targets}.values():
+                allocation.mark()
+        job.keep = (ring, table, state)
+        job.rehash_from = targets
+        return launches
+
+    def _columns(self, n):
+        """The column plan for saves of n blocks, with each column's device span table and kernel flags."""
+        plans = self.__dict__.setdefault("_column_plans", {})
+        if n not in plans:
+            span_bytes = [layer["bytes"] for layer in self.layers]
+            group, stride, columns = column_plan(span_bytes, n, self.staging_bytes // self.staging_slots)
+            host = (_abi.Span * len(self.layers)).from_buffer_copy(self._span_table.cpu().numpy().tobytes())
+            tables, flags = [], []
+            for s0, s1, offset, _ in columns:
+                part = (_abi.Span * (s1 - s0))()
+                for k in range(s1 - s0):
+                    part[k] = host[s0 + k]
+                    part[k].offset -= offset                 # packed offsets from the column's start
+                tables.append(self.torch.frombuffer(bytearray(bytes(part)), dtype=self.torch.uint8).to(self._device()))
+                vec = 16 if self._span_vec == 16 and stride % 16 == 0 else 8
+                flags.append(vec | (_abi.hbm_flags(span_bytes[s0:s1], vec) | _abi.CRC_ACCUMULATE if vec == 16 else 0))
+            plans[n] = (group, stride, columns, tables, flags)
+        return plans[n]
+
+    def _digests(self, job, cache, keys):
+        """The save's ``(sha256 hex, crc32c)`` list, once its SHA-256 kernels have finished.
+
+        Blocks served from ``cache`` must have kept their CRC32C; one that has
+        not is hashed now, from wherever the save left its packed bytes
+        (device staging, or the pinned targets).
+        """
+        torch = self.torch
+        crcs = [v & 0xFFFFFFFF for v in job.crc.cpu().tolist()]
+        raw = job.digest.cpu().numpy().tobytes() if job.hashed else b""
         out = [None] * len(crcs)
-        for k, i in enumerate(hashed):
+        for k, i in enumerate(job.hashed):
             out[i] = (raw[32 * k:32 * k + 32].hex(), crcs[i])
-        stale = [i for i, (sha, c) in known.items() if c != crcs[i]]
-        for i, entry in known.items():
+        stale = [i for i, (sha, c) in job.known.items() if c != crcs[i]]
+        for i, entry in job.known.items():
             out[i] = (entry[0], crcs[i])
         if cache is not None:
-            cache.hits += len(known) - len(stale)
-            cache.misses += len(keys) - len(known)
+            cache.hits += len(job.known) - len(stale)
+            cache.misses += len(keys) - len(job.known)
             cache.rejected += len(stale)
         if stale:
             lib = _dp(self.pool.lib)
             stream = self._sha_stream()
-            device = stage.device
+            device = self._device()
             with torch.cuda.stream(stream):
-                addresses = torch.tensor([write_to[i] for i in stale], dtype=torch.int64, device=device)
+                addresses = torch.tensor([job.rehash_from[i] for i in stale], dtype=torch.int64, device=device)
                 fresh = torch.empty(len(stale) * 32, dtype=torch.uint8, device=device)
                 self._check(lib.kvsnap_dp_sha256(addresses.data_ptr(), len(stale), self.block_bytes,
                                                  fresh.data_ptr(), stream.cuda_stream))
@@ -1024,6 +1231,7 @@ class TorchBlockDataPlane:
         if cache is not None:
             for i, key in enumerate(keys):
                 cache.put(key[0], key[1], out[i])
+        job.keep = None
         return out
 
     def _sha_stream(self):
@@ -1072,17 +1280,22 @@ class TorchBlockDataPlane:
                 if offset < 0 or offset + size > allocation.size:
                     raise ValueError("digest source outside its allocation")
             with torch.cuda.stream(stream):
-                stage = torch.empty(n * size, dtype=torch.uint8, device=device)
-                self.pool.copy_many([(sources[i][0], sources[i][1], stage.data_ptr() + i * size, (j - i) * size)
-                                     for i, j in self._runs(sources, 0, n, size)], to_host=False)
-                addresses = torch.tensor([stage.data_ptr() + i * size for i in range(n)],
-                                         dtype=torch.int64).pin_memory().to(device, non_blocking=True)
+                if n * size <= self.staging_bytes:
+                    stage = torch.empty(n * size, dtype=torch.uint8, device=device)
+                    self.pool.copy_many([(sources[i][0], sources[i][1], stage.data_ptr() + i * size, (j - i) * size)
+                                         for i, j in self._runs(sources, 0, n, size)], to_host=False)
+                    where = [stage.data_ptr() + i * size for i in range(n)]
+                    vec, ctas = ((16 | _abi.HBM) if size % 16 == 0 else 8), self.ctas
+                else:
+                    # Beyond the staging bound the kernels read the pinned blocks in place over the host link.
+                    where = [a.pointer + o for a, o in sources]
+                    vec, ctas = self._vec_for(where), self.host_ctas
+                addresses = torch.tensor(where, dtype=torch.int64).pin_memory().to(device, non_blocking=True)
                 crc = torch.empty(n, dtype=torch.int32, device=device)
                 status = torch.zeros(1, dtype=torch.int32, device=device)
                 out = torch.empty(n * 32, dtype=torch.uint8, device=device)
-                vec = (16 | _abi.HBM) if size % 16 == 0 else 8
                 self._check(lib.kvsnap_dp_crc32c(addresses.data_ptr(), n, size, crc.data_ptr(), 0,
-                                                 status.data_ptr(), vec, self.ctas, stream.cuda_stream))
+                                                 status.data_ptr(), vec, ctas, stream.cuda_stream))
                 self._check(lib.kvsnap_dp_sha256(addresses.data_ptr(), n, size, out.data_ptr(), stream.cuda_stream))
             stream.synchronize()
         self._status_error(status)

@@ -73,7 +73,8 @@ def test_python_flag_constants_equal_the_header():
     text = (Path(__file__).resolve().parents[1] / "include" / "kvsnap_cuda.h").read_text()
     defines = {m.group(1): int(m.group(2), 0)
                for m in re.finditer(r"#define KVSNAP_DP_(\w+) (0x[0-9A-Fa-f]+|\d+)u?\b", text)}
-    for name in ("MISALIGNED", "BAD_BLOCK", "CRC_MISMATCH", "BAD_CUT", "HBM", "RUNS", "PAIRS", "SPLIT2", "SPLIT4"):
+    for name in ("MISALIGNED", "BAD_BLOCK", "CRC_MISMATCH", "BAD_CUT", "HBM", "RUNS", "PAIRS", "SPLIT2", "SPLIT4",
+                 "CRC_ACCUMULATE"):
         assert getattr(_abi, name) == defines[name], name
     assert defines["SPLIT_MASK"] == _abi.SPLIT2 | _abi.SPLIT4
     assert defines["ABI_VERSION"] == _abi.DP_ABI_VERSION
@@ -246,3 +247,24 @@ def test_runs_coalesce_like_the_reference_copy_count():
             ours += len(list(TorchBlockDataPlane._runs(targets, first, min(len(targets), first + per), size)))
         keyed = [(id(x), o) for x, o in targets]
         assert ours == oracle.save_copy_count(keyed, size, chunk_blocks * size)
+
+
+@pytest.mark.parametrize("spans, n, slot", [([32768] * 72, 512, 128 << 20), ([4096] * 128, 2048, 128 << 20),
+                                            ([32768] * 72, 8192, 128 << 20), ([8192, 8192, 48, 16, 4096] * 3, 9, 4096),
+                                            ([1 << 20] * 4, 64, 1 << 20), ([16] * 40, 3, 64)])
+def test_column_plan_covers_every_block_byte_in_sha_chunks(spans, n, slot):
+    """The staged save's column plan: consecutive spans, whole 64-byte chunks before the last column,
+    every byte once, and a slot's group of columns within the slot unless a single column is larger."""
+    from kvsnap_b200.dataplane import column_plan
+    group, stride, columns = column_plan(spans, n, slot)
+    assert columns[0][0] == 0 and columns[-1][1] == len(spans)
+    offset = 0
+    for (s0, s1, at, nbytes), nxt in zip(columns, columns[1:] + [None]):
+        assert s1 > s0 and at == offset and nbytes == sum(spans[s0:s1])
+        offset += nbytes
+        if nxt is not None:
+            assert nxt[0] == s1 and offset % 64 == 0
+    assert offset == sum(spans)
+    assert stride % 16 == 0 and stride >= max(c[3] for c in columns)
+    assert 1 <= group <= n
+    assert group * stride <= slot or group == 1
