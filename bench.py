@@ -303,7 +303,8 @@ class Engine:
         self.chunk = max(1, (64 << 20) // plane.block_bytes)
         self.n = len(save_ids)
         self.size = plane.block_bytes
-        self.ctas = ctas
+        # As the API launches them: beside SHA-256 kernels, the device-memory kernels leave their SMs free.
+        self.ctas = ctas or plane.hbm_ctas
         self.restore_mode = restore_mode
         dev = plane._device()
         n, size = self.n, self.size

@@ -538,6 +538,7 @@ class TorchBlockDataPlane:
     save_mode = "staged"
     restore_mode = "staged"
     staging_slots = 4
+    sha_sms = 16
 
     def __init__(self, caches, block_size, capacity_bytes, *, save_mode=None, restore_mode=None, ctas=0,
                  staging_bytes=512 << 20):
@@ -563,6 +564,22 @@ class TorchBlockDataPlane:
         # for the engine and the SHA-256 kernel.
         self.host_ctas = ctas or 32
         self.pool = CudaPool(capacity_bytes, device.index)
+
+    @property
+    def hbm_ctas(self):
+        """CTAs of a device-memory gather, scatter or CRC launch.
+
+        Those kernels' CTAs each take most of an SM's shared memory, so one
+        cannot start on an SM where a SHA-256 CTA (of this save or another
+        session's) runs: launched on every SM, a gather or scatter would wait
+        for that hash, tens of milliseconds, to finish. Unless ``ctas`` was
+        given, they leave ``sha_sms`` SMs to the hashes.
+        """
+        if self.ctas:
+            return self.ctas
+        if getattr(self, "_sm_count", None) is None:
+            self._sm_count = self.torch.cuda.get_device_properties(self._device()).multi_processor_count
+        return max(1, self._sm_count - self.sha_sms)
 
     # ---- registration-time tables ------------------------------------------------------------
 
@@ -847,7 +864,7 @@ class TorchBlockDataPlane:
                             last = min(n, first + per_launch)
                             self._check(lib.kvsnap_dp_scatter(
                                 spans.data_ptr(), len(self.layers), size, table[first:].data_ptr(),
-                                ids[first:].data_ptr(), last - first, 0, 0, 0, status.data_ptr(), vec, self.ctas,
+                                ids[first:].data_ptr(), last - first, 0, 0, 0, status.data_ptr(), vec, self.hbm_ctas,
                                 kernels.cuda_stream))
                             launches += 1
                             done = torch.cuda.Event()
@@ -901,7 +918,7 @@ class TorchBlockDataPlane:
             kernels.wait_event(landed)
             self._check(lib.kvsnap_dp_scatter(
                 spans.data_ptr(), len(self.layers), size, table[slot * depth:].data_ptr(), ids[first:].data_ptr(),
-                last - first, 0, 0, 0, status.data_ptr(), vec, self.ctas, kernels.cuda_stream))
+                last - first, 0, 0, 0, status.data_ptr(), vec, self.hbm_ctas, kernels.cuda_stream))
             launches += 1
             done = torch.cuda.Event()
             done.record(kernels)
@@ -918,7 +935,7 @@ class TorchBlockDataPlane:
         crc = torch.empty(n, dtype=torch.int32, device=table.device)
         expect = torch.tensor(_u32(expected), dtype=torch.int32).pin_memory().to(table.device, non_blocking=True)
         self._check(lib.kvsnap_dp_crc32c(table.data_ptr(), n, self.block_bytes, crc.data_ptr(), expect.data_ptr(),
-                                         status.data_ptr(), vec, self.ctas if ctas is None else ctas,
+                                         status.data_ptr(), vec, self.hbm_ctas if ctas is None else ctas,
                                          torch.cuda.current_stream().cuda_stream))
         flags = int(status.item())          # synchronises the copy stream
         if flags & _abi.CRC_MISMATCH:
@@ -1059,7 +1076,7 @@ class TorchBlockDataPlane:
             self._device(), non_blocking=True)
         self._check(lib.kvsnap_dp_gather(
             spans.data_ptr(), len(self.layers), size, table.data_ptr(), table[n:].data_ptr(), n, job.valid,
-            job.crc.data_ptr() if job.crc is not None else 0, job.status.data_ptr(), vec, self.ctas,
+            job.crc.data_ptr() if job.crc is not None else 0, job.status.data_ptr(), vec, self.hbm_ctas,
             stream.cuda_stream))
         if job.digests:
             job.side = self._sha_stream()
@@ -1148,7 +1165,7 @@ class TorchBlockDataPlane:
                     self._check(lib.kvsnap_dp_gather(
                         tables[j].data_ptr(), s1 - s0, size, words + 8 * g0, slot_table, g1 - g0,
                         job.valid if g1 == n else 0, job.crc.data_ptr() + 4 * g0 if job.crc is not None else 0,
-                        job.status.data_ptr(), flags[j], self.ctas, stream.cuda_stream))
+                        job.status.data_ptr(), flags[j], self.hbm_ctas, stream.cuda_stream))
                     self._check(lib.kvsnap_dp_land(slot, stride, words + 8 * (n + g0), offset, g1 - g0, nbytes,
                                                    job.status.data_ptr(), 0, stream.cuda_stream))
                     launches += 1
@@ -1285,7 +1302,7 @@ class TorchBlockDataPlane:
                     self.pool.copy_many([(sources[i][0], sources[i][1], stage.data_ptr() + i * size, (j - i) * size)
                                          for i, j in self._runs(sources, 0, n, size)], to_host=False)
                     where = [stage.data_ptr() + i * size for i in range(n)]
-                    vec, ctas = ((16 | _abi.HBM) if size % 16 == 0 else 8), self.ctas
+                    vec, ctas = ((16 | _abi.HBM) if size % 16 == 0 else 8), self.hbm_ctas
                 else:
                     # Beyond the staging bound the kernels read the pinned blocks in place over the host link.
                     where = [a.pointer + o for a, o in sources]
