@@ -61,6 +61,8 @@ def parse():
     p.add_argument("--ctas", type=int, default=0, help="CTAs for the data-plane kernels (0: library default)")
     p.add_argument("--restore-mode", choices=["direct", "staged"], default="staged")
     p.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    p.add_argument("--no-shard", action="store_true",
+                   help="skip the sharded (BASELINE config 5) and regroup sub-objects of the session line")
     p.add_argument("--explore", type=str, default="", help="write a per-phase / CTA sweep breakdown to this path")
     p.add_argument("--seed", type=int, default=0)
     p.add_argument("--workload", choices=["session", "disk", "reshard", "rotation", "kernels"], default="session",
@@ -462,6 +464,61 @@ def check_session(plane, save_ids, restore_ids, tokens):
     return True
 
 
+def reference_gpu(caches, save_ids, restore_ids, tokens, reps=5):
+    """The reference's own GPU data plane on this GPU, the same cache and session as ours.
+
+    kvsnap's stock ``TorchBlockDataPlane`` (installed under baseline/_ref with
+    its CUDA pool): the save gathers with torch ``index_select`` + ``cat`` a
+    64 MiB chunk at a time and copies each chunk to pinned memory, then zeroes
+    the last block's tail on the host (kvsnap/connector/dataplane.py:388-437);
+    the restore is its Triton kernel reading pinned memory
+    (kvsnap/connector/copy_kernel.py:23-49). Timed on the host around each call
+    (both wait for their copies), one session at a time, one pinned buffer for
+    the session (the disk tier's target). Returns a dict, or the reason it
+    could not run.
+    """
+    import torch
+    ref = ROOT / "baseline" / "_ref"
+    if not (ref / "kvsnap" / "_native").is_dir():
+        return {"unavailable": "the reference is not installed under baseline/_ref"}
+    if str(ref) not in sys.path:
+        sys.path.append(str(ref))
+    saved_env = os.environ.pop("KVSNAP_CUDA_LIBRARY", None)
+    try:
+        from kvsnap.connector import dataplane as theirs
+        from kvsnap_b200.dataplane import _split_paged
+        plane = theirs.TorchBlockDataPlane(_split_paged(caches, BLOCK), BLOCK, (len(save_ids) + 4) *
+                                           sum(t[0].numel() * 2 for t in caches.values()) + (64 << 20))
+    except Exception as exc:                                      # noqa: BLE001 - reported, not fatal
+        return {"unavailable": f"{type(exc).__name__}: {exc}"[:200]}
+    finally:
+        if saved_env is not None:
+            os.environ["KVSNAP_CUDA_LIBRARY"] = saved_env
+    try:
+        plane.warm_up()
+        n, size = len(save_ids), plane.block_bytes
+        with plane.staging(n) as snap:
+            targets = [(snap, i * size) for i in range(n)]
+            saves, restores = [], []
+            for _ in range(reps + 1):
+                torch.cuda.synchronize()
+                t0 = time.perf_counter()
+                plane.save_gather(save_ids, targets, tokens)
+                saves.append((time.perf_counter() - t0) * 1e3)
+                t0 = time.perf_counter()
+                plane.load_scatter(restore_ids, targets)
+                restores.append((time.perf_counter() - t0) * 1e3)
+        save_ms, restore_ms = statistics.median(saves[1:]), statistics.median(restores[1:])
+        return {"save_ms": round(save_ms, 3), "restore_ms": round(restore_ms, 3),
+                "save_gbs": round(n * size / save_ms / 1e6, 2), "restore_gbs": round(n * size / restore_ms / 1e6, 2),
+                "how": "kvsnap TorchBlockDataPlane from baseline/_ref: torch index_select+cat and cudaMemcpyAsync "
+                       "save, Triton restore kernel; one session at a time, one pinned buffer"}
+    except Exception as exc:                                      # noqa: BLE001
+        return {"unavailable": f"{type(exc).__name__}: {exc}"[:200]}
+    finally:
+        plane.close()
+
+
 # ---- the reference's CPU path ----------------------------------------------------------------------
 
 def reference_cpu(seconds, sample_blocks, threads, layers=LAYERS):
@@ -720,6 +777,8 @@ def main():
             t0 = time.perf_counter()
             plane.load_scatter(restore_ids, places)
             restore_times.append((time.perf_counter() - t0) * 1e3)
+    # The reference's own GPU path on the same GPU, cache and session, one session at a time.
+    ref_gpu = reference_gpu(caches, save_ids, restore_ids, args.tokens)
     restore_ms = max_over_ranks(statistics.median(restore_times), world)
     save_ms = max_over_ranks(statistics.median(save_times), world)
     save_digests_ms = max_over_ranks(statistics.median(digest_times), world)
@@ -782,17 +841,93 @@ def main():
         "gpu_launches": engine.launches_per_step * args.steps,
         "clocks": clock_info,
         "parity": {"restored_equals_saved": digests_ok, "host_hash_sample": True},
+        "reference_gpu": dict(ref_gpu, ours_save_ms=round(save_ms, 3), ours_restore_ms=round(restore_ms, 3),
+                              note="both until the packed blocks are in pinned memory (save) or in the cache "
+                                   "(restore); ours also computes CRC32C on the way and SHA-256 after"),
     }
     if cpu is not None:
         line["cpu_baseline"] = cpu
-    if rank == 0:
-        print(json.dumps(line), flush=True)
     for snap in engine.snapshot:
         snap.close()
     plane.close()
+    del engine, plane, caches
+    torch.cuda.synchronize()
+    torch.cuda.empty_cache()
+    if not args.no_shard:
+        # Benchmark configuration 5 on the same ranks: every rank's own TP-N shard, then (an even N) the
+        # regroup of a TP-N snapshot restored at TP-N/2 over NVLink.
+        line["sharded"] = measure_sharded(args, world, rank, device, box_duplex)
+        if world >= 2 and world % 2 == 0:
+            line["reshard"] = measure_reshard(args, world, rank, device)
+    if rank == 0:
+        print(json.dumps(line), flush=True)
     if world > 1:
         import torch.distributed as dist
         dist.destroy_process_group()
+
+
+def measure_sharded(args, world, rank, device, box_duplex):
+    """Benchmark configuration 5: each rank's TP-N shard of a 32768-token Qwen3-32B session, all ranks at once.
+
+    A rank holds 64 layers of 8/N KV heads (TP-N, kvsnap/connector/vllm.py:9-14)
+    in a pool of 4160 blocks and saves and restores its 2048-block shard
+    through the API, one pinned buffer a session, with content ids and CRCs
+    from the GPU: no collective touches the data path. Times are the median of
+    a few sessions, max over ranks; box figures are all ranks' bytes over that.
+    """
+    import numpy as np
+    import torch
+    from kvsnap_b200.dataplane import PendingDigests, TorchBlockDataPlane
+    layers, heads, n, pool = 64, 8 // world, 2048, 2 * 2048 + 64
+    gen = torch.Generator(device=device)
+    caches = {}
+    for i in range(layers):
+        gen.manual_seed(args.seed * 1000 + 700 + i + 100 * rank)
+        t = torch.empty((2, pool, BLOCK, heads, HEAD_DIM), dtype=torch.bfloat16, device=device)
+        t.normal_(generator=gen)
+        caches[f"model.layers.{i}.self_attn.attn"] = t
+    size = layers * 2 * BLOCK * heads * HEAD_DIM * 2
+    plane = TorchBlockDataPlane(caches, BLOCK, n * size + (64 << 20), ctas=args.ctas)
+    plane.warm_up()
+    order = np.random.Generator(np.random.PCG64(args.seed + 29)).permutation(pool - 1) + 1
+    save_ids, restore_ids = [int(b) for b in order[:n]], [int(b) for b in order[n:2 * n]]
+    saves, digests, restores = [], [], []
+    with plane.staging(n) as snapshot:
+        targets = [(snapshot, i * size) for i in range(n)]
+        for rep in range(4):
+            torch.cuda.synchronize()
+            barrier(world)
+            t0 = time.perf_counter()
+            pending = PendingDigests()
+            plane.save_gather(save_ids, targets, n * BLOCK, digests=pending)
+            t1 = time.perf_counter()
+            pending.result()
+            t2 = time.perf_counter()
+            barrier(world)
+            t3 = time.perf_counter()
+            plane.load_scatter(restore_ids, targets)
+            t4 = time.perf_counter()
+            if rep:                                          # the first is a warm-up
+                saves.append(t1 - t0)
+                digests.append(t2 - t0)
+                restores.append(t4 - t3)
+    plane.close()
+    del plane, caches
+    torch.cuda.synchronize()
+    torch.cuda.empty_cache()
+    save_s = max_over_ranks(statistics.median(saves), world)
+    digest_s = max_over_ranks(statistics.median(digests), world)
+    restore_s = max_over_ranks(statistics.median(restores), world)
+    shard = n * size
+    return {"config": f"qwen3-32b 32768-token session, TP-{world} shard a rank (BASELINE config 5)",
+            "layers": layers, "kv_heads_per_rank": heads, "blocks": n, "shard_bytes_per_rank": shard,
+            "save_ms": round(save_s * 1e3, 3), "save_digests_ms": round(digest_s * 1e3, 3),
+            "restore_ms": round(restore_s * 1e3, 3),
+            "save_gbs_per_gpu": round(shard / save_s / 1e9, 2), "restore_gbs_per_gpu": round(shard / restore_s / 1e9, 2),
+            "save_gbs_box": round(world * shard / save_s / 1e9, 2),
+            "restore_gbs_box": round(world * shard / restore_s / 1e9, 2),
+            "box_duplex_gbs": round(box_duplex, 2),
+            "note": "one session at a time a rank, all ranks at once; the box's ranks share its host link"}
 
 
 def run_kernels(args, world, rank, device):
@@ -1007,7 +1142,7 @@ def blob_phase(plane, sources, digests, restored, n, size, args):
     return out
 
 
-def run_reshard(args, world, rank, device):
+def measure_reshard(args, world, rank, device):
     """Benchmark configuration 5's regroup: a TP-(2T) Qwen3-32B snapshot restored at TP-T over NVLink.
 
     World size W (torchrun, one GPU a rank): the snapshot was saved at TP=W (one
@@ -1081,19 +1216,33 @@ def run_reshard(args, world, rank, device):
     worst = torch.tensor([med["total_s"], med.get("kernel_ms", 0.0), med["stage_s"]], dtype=torch.float64,
                          device=device)
     dist.all_reduce(worst, op=dist.ReduceOp.MAX)
-    if rank == 0:
-        moved = plan.dst_tp * n * size
-        print(json.dumps({
-            "workload": f"TP-{plan.src_tp} -> TP-{plan.dst_tp} regroup restore, qwen3-32b shape, 32768 tokens",
-            "n_gpus": world, "blocks": n, "shard_bytes_per_rank": n * shard, "dest_bytes_per_rank": n * size,
-            "total_ms": round(worst[0].item() * 1e3, 3), "regroup_kernel_ms": round(worst[1].item(), 3),
-            "stage_ms": round(worst[2].item() * 1e3, 3),
-            "regroup_kernel_gbs_per_dest_rank": round(n * size / (worst[1].item() / 1e3) / 1e9, 1),
-            "box_restored_gbs": round(moved / worst[0].item() / 1e9, 2),
-            "bit_exact_samples": bool(flags.item() == 1.0)}), flush=True)
+    moved = plan.dst_tp * n * size
+    result = {
+        "workload": f"TP-{plan.src_tp} -> TP-{plan.dst_tp} regroup restore, qwen3-32b shape, 32768 tokens",
+        "n_gpus": world, "blocks": n, "shard_bytes_per_rank": n * shard, "dest_bytes_per_rank": n * size,
+        "total_ms": round(worst[0].item() * 1e3, 3), "regroup_kernel_ms": round(worst[1].item(), 3),
+        "stage_ms": round(worst[2].item() * 1e3, 3),
+        "regroup_kernel_gbs_per_dest_rank": round(n * size / (worst[1].item() / 1e3) / 1e9, 1),
+        "box_restored_gbs": round(moved / worst[0].item() / 1e9, 2),
+        "bit_exact_samples": bool(flags.item() == 1.0),
+        "limit": "stage: every source rank's shard over the box's shared host link; kernel: peer reads over NVLink"}
     snapshot.close()
     plane.close()
+    del plane, caches, noise
+    torch.cuda.synchronize()
+    torch.cuda.empty_cache()
+    return result
+
+
+def run_reshard(args, world, rank, device):
+    """``--workload reshard``: the regroup alone, its line printed by rank 0."""
+    import torch.distributed as dist
+    result = measure_reshard(args, world, rank, device)
+    if rank == 0:
+        print(json.dumps(result), flush=True)
     dist.destroy_process_group()
+
+
 
 
 def run_rotation(args, world, rank, device):

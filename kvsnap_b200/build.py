@@ -9,11 +9,15 @@
 * ``_io_native.so``: host CRC32C and the pread/pwrite pool (csrc/io.cpp,
   include/kvsnap_io.h), g++.
 
-A library is rebuilt when any of its sources or headers is newer than it.
+A library is rebuilt unless the stamp beside it (``<library>.stamp``) holds
+the SHA-256 of exactly the sources, headers and compiler command it would be
+built from now: a prebuilt library from other sources is never reused because
+of its timestamp.
 """
 from __future__ import annotations
 
 import argparse
+import hashlib
 import os
 import shutil
 import subprocess
@@ -39,11 +43,22 @@ def _nvcc() -> str:
     return found
 
 
-def _stale(target: Path, sources) -> bool:
-    if not target.is_file():
-        return True
-    built = target.stat().st_mtime
-    return any(p.stat().st_mtime > built for p in sources)
+def _recipe(sources, command) -> str:
+    """The SHA-256 of what a library is built from: each input's name and bytes, then the command."""
+    digest = hashlib.sha256()
+    for path in sources:
+        digest.update(path.name.encode() + b"\0" + path.read_bytes() + b"\0")
+    digest.update(" ".join(map(str, command)).encode())
+    return digest.hexdigest()
+
+
+def _stamp(target: Path) -> Path:
+    return target.with_name(target.name + ".stamp")
+
+
+def _stale(target: Path, recipe: str) -> bool:
+    stamp = _stamp(target)
+    return not target.is_file() or not stamp.is_file() or stamp.read_text().strip() != recipe
 
 
 def _run(cmd):
@@ -52,28 +67,29 @@ def _run(cmd):
         raise RuntimeError(f"build failed: {' '.join(map(str, cmd))}\n{result.stdout}\n{result.stderr}")
 
 
-def build_cuda(force: bool = False) -> Path:
-    sources = [CSRC / "pool.cpp", CSRC / "dataplane.cu"]
-    deps = sources + [CSRC / "kvsnap_internal.h", INCLUDE / "kvsnap_cuda.h"]
-    if force or _stale(CUDA_LIB, deps):
+def _build(target: Path, sources, deps, compiler, flags, force: bool) -> Path:
+    """Compile ``sources`` into ``target`` unless its stamp matches this recipe; then write the stamp."""
+    command = [*flags, *map(str, sources)]
+    recipe = _recipe(sources + deps, [Path(compiler).name, *command])
+    if force or _stale(target, recipe):
         NATIVE.mkdir(parents=True, exist_ok=True)
-        tmp = CUDA_LIB.with_suffix(".so.tmp")
-        _run([_nvcc(), *ARCH, "-O3", "-lineinfo", "-std=c++17", "-shared", "-Xcompiler", "-fPIC",
-              "-Xcompiler", "-Wall", "-cudart", "static", f"-I{INCLUDE}", f"-I{CSRC}",
-              *map(str, sources), "-o", str(tmp)])
-        os.replace(tmp, CUDA_LIB)
-    return CUDA_LIB
+        tmp = target.with_suffix(".so.tmp")
+        _run([compiler, *command, "-o", str(tmp)])
+        os.replace(tmp, target)
+        _stamp(target).write_text(recipe + "\n")
+    return target
+
+
+def build_cuda(force: bool = False) -> Path:
+    flags = [*ARCH, "-O3", "-lineinfo", "-std=c++17", "-shared", "-Xcompiler", "-fPIC", "-Xcompiler", "-Wall",
+             "-cudart", "static", f"-I{INCLUDE}", f"-I{CSRC}"]
+    return _build(CUDA_LIB, [CSRC / "pool.cpp", CSRC / "dataplane.cu"],
+                  [CSRC / "kvsnap_internal.h", INCLUDE / "kvsnap_cuda.h"], _nvcc(), flags, force)
 
 
 def build_io(force: bool = False) -> Path:
-    sources = [CSRC / "io.cpp"]
-    if force or _stale(IO_LIB, sources + [INCLUDE / "kvsnap_io.h"]):
-        NATIVE.mkdir(parents=True, exist_ok=True)
-        tmp = IO_LIB.with_suffix(".so.tmp")
-        _run([os.environ.get("CXX", "g++"), "-std=c++17", "-O3", "-shared", "-fPIC", "-pthread", "-Wall",
-              "-Wextra", "-Werror", f"-I{INCLUDE}", *map(str, sources), "-o", str(tmp)])
-        os.replace(tmp, IO_LIB)
-    return IO_LIB
+    flags = ["-std=c++17", "-O3", "-shared", "-fPIC", "-pthread", "-Wall", "-Wextra", "-Werror", f"-I{INCLUDE}"]
+    return _build(IO_LIB, [CSRC / "io.cpp"], [INCLUDE / "kvsnap_io.h"], os.environ.get("CXX", "g++"), flags, force)
 
 
 def build(force: bool = False) -> None:

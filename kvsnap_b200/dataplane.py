@@ -152,6 +152,14 @@ class DigestCache:
     every save (kvsnap/store/store.py:616-629, connector/volatile.py:141-151)
     and lists "hashing only the blocks a turn changed" as its next step.
     Least recently used entries go first beyond ``capacity``.
+
+    What the cache trusts: the generation is the guarantee that a block's bytes
+    are unchanged; the CRC32C comparison only catches a caller that broke that
+    contract. A block that changed without a new generation and whose new bytes
+    happen to have the same CRC32C (one chance in 2**32 a block) would be given
+    the old content id, and a content-addressed store would file it under
+    another block's bytes. Callers that cannot keep the generation contract
+    should not pass a cache: then every block is hashed.
     """
 
     def __init__(self, capacity: int = 1 << 20):
@@ -537,7 +545,7 @@ class TorchBlockDataPlane:
 
     save_mode = "staged"
     restore_mode = "staged"
-    staging_slots = 4
+    staging_slots = 8
     sha_sms = 16
 
     def __init__(self, caches, block_size, capacity_bytes, *, save_mode=None, restore_mode=None, ctas=0,
@@ -575,11 +583,15 @@ class TorchBlockDataPlane:
         for that hash, tens of milliseconds, to finish. Unless ``ctas`` was
         given, they leave ``sha_sms`` SMs to the hashes.
         """
+        return self._grid_beside(0)
+
+    def _grid_beside(self, hashed_blocks):
+        """``hbm_ctas``, leaving at least the SMs a hash of ``hashed_blocks`` blocks occupies (64 blocks an SM)."""
         if self.ctas:
             return self.ctas
         if getattr(self, "_sm_count", None) is None:
             self._sm_count = self.torch.cuda.get_device_properties(self._device()).multi_processor_count
-        return max(1, self._sm_count - self.sha_sms)
+        return max(1, self._sm_count - max(self.sha_sms, (hashed_blocks + 63) // 64))
 
     # ---- registration-time tables ------------------------------------------------------------
 
@@ -1165,7 +1177,7 @@ class TorchBlockDataPlane:
                     self._check(lib.kvsnap_dp_gather(
                         tables[j].data_ptr(), s1 - s0, size, words + 8 * g0, slot_table, g1 - g0,
                         job.valid if g1 == n else 0, job.crc.data_ptr() + 4 * g0 if job.crc is not None else 0,
-                        job.status.data_ptr(), flags[j], self.hbm_ctas, stream.cuda_stream))
+                        job.status.data_ptr(), flags[j], self._grid_beside(len(job.hashed)), stream.cuda_stream))
                     self._check(lib.kvsnap_dp_land(slot, stride, words + 8 * (n + g0), offset, g1 - g0, nbytes,
                                                    job.status.data_ptr(), 0, stream.cuda_stream))
                     launches += 1

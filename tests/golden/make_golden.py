@@ -1,9 +1,9 @@
 """Generate tests/golden/golden.json by running the REFERENCE kvsnap data plane on the CPU.
 
-    python tests/golden/make_golden.py [--reference <kvsnap source tree>]
+    python tests/golden/make_golden.py --reference <kvsnap source tree>
 
-Needs the reference source tree (read-only) and ``make -C oracle`` (which
-compiles the reference's own ``csrc/dataplane/io.cpp`` into
+Needs the reference source tree (read-only) and ``make -C oracle REF=<tree>``
+(which compiles the reference's own ``csrc/dataplane/io.cpp`` into
 ``oracle/_ref/libkvsnap_io_ref.so``). Everything recorded here is produced by
 the reference's code, never by this repository's product:
 
@@ -213,7 +213,7 @@ def save_case(dataplane, crc32c, caches, block_size, saved, restored, tokens, ch
 
 def main():
     parser = argparse.ArgumentParser()
-    parser.add_argument("--reference", default="/root/reference")
+    parser.add_argument("--reference", required=True, help="the kvsnap source tree (read-only)")
     parser.add_argument("--out", default=str(Path(__file__).resolve().parent / "golden.json"))
     args = parser.parse_args()
     ref_io = REPO / "oracle/_ref/libkvsnap_io_ref.so"
