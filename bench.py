@@ -487,8 +487,9 @@ def reference_gpu(caches, save_ids, restore_ids, tokens, reps=5):
     try:
         from kvsnap.connector import dataplane as theirs
         from kvsnap_b200.dataplane import _split_paged
-        plane = theirs.TorchBlockDataPlane(_split_paged(caches, BLOCK), BLOCK, (len(save_ids) + 4) *
-                                           sum(t[0].numel() * 2 for t in caches.values()) + (64 << 20))
+        block_bytes = sum(2 * t[0, 0].numel() * t.element_size() for t in caches.values())   # K and V
+        plane = theirs.TorchBlockDataPlane(_split_paged(caches, BLOCK), BLOCK,
+                                           (len(save_ids) + 4) * block_bytes + (64 << 20))
     except Exception as exc:                                      # noqa: BLE001 - reported, not fatal
         return {"unavailable": f"{type(exc).__name__}: {exc}"[:200]}
     finally:
@@ -706,6 +707,7 @@ def main():
         s1.record(engine.copy)
         torch.cuda.synchronize()
         kernel_ms[name] = max_over_ranks(s0.elapsed_time(s1) / 10, world)
+    del fn                                               # a bound method of the engine: it holds the cache
 
     # End to end through the public API, host tier (one pinned allocation per block), with the
     # connector's threads: two save workers (vllm.py:202) and one load worker (vllm.py:203). Session k
@@ -851,8 +853,7 @@ def main():
         snap.close()
     plane.close()
     del engine, plane, caches
-    torch.cuda.synchronize()
-    torch.cuda.empty_cache()
+    release_device_memory()
     if not args.no_shard:
         # Benchmark configuration 5 on the same ranks: every rank's own TP-N shard, then (an even N) the
         # regroup of a TP-N snapshot restored at TP-N/2 over NVLink.
@@ -864,6 +865,18 @@ def main():
     if world > 1:
         import torch.distributed as dist
         dist.destroy_process_group()
+
+
+def release_device_memory():
+    """Hand a finished workload's device memory back: its plane, pool and allocations refer to one another,
+    so they go at a collection, and then the caching allocator returns the blocks to the device."""
+    import gc
+    import torch
+    gc.collect()
+    torch.cuda.synchronize()
+    torch.cuda.empty_cache()
+    free, total = torch.cuda.mem_get_info()
+    log(f"device memory free {free / 2**30:.1f} of {total / 2**30:.1f} GiB")
 
 
 def measure_sharded(args, world, rank, device, box_duplex):
@@ -913,8 +926,7 @@ def measure_sharded(args, world, rank, device, box_duplex):
                 restores.append(t4 - t3)
     plane.close()
     del plane, caches
-    torch.cuda.synchronize()
-    torch.cuda.empty_cache()
+    release_device_memory()
     save_s = max_over_ranks(statistics.median(saves), world)
     digest_s = max_over_ranks(statistics.median(digests), world)
     restore_s = max_over_ranks(statistics.median(restores), world)
@@ -1229,8 +1241,7 @@ def measure_reshard(args, world, rank, device):
     snapshot.close()
     plane.close()
     del plane, caches, noise
-    torch.cuda.synchronize()
-    torch.cuda.empty_cache()
+    release_device_memory()
     return result
 
 
