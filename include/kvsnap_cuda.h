@@ -91,6 +91,26 @@ int kvsnap_pool_copy_many(void* pool, int64_t n, const uint64_t* ids, const uint
 /* Extension: kvsnap_pool_wait for each of n allocations, in one call. */
 int kvsnap_pool_wait_many(void* pool, int64_t n, const uint64_t* ids);
 
+/* Extension for the cross-owner host tier (replaces the socket copy of
+   kvsnap/connector/vllm.py:524-534 and connector/volatile.py:87-138): a pool
+   whose arena is POSIX shared memory named `name` (one path component that
+   starts with '/', created with mode 0600, so only this user's processes open
+   it), registered with CUDA as pinned and mapped memory. It behaves as
+   kvsnap_pool_create's; destroying it unlinks the name, and the mappings other
+   processes made stay valid until they close them. NULL on error (a name
+   already in use included). */
+void* kvsnap_pool_create_shared(size_t capacity, int device, const char* name);
+/* Extension: the arena's first byte and its capacity, so an owner can tell
+   other processes where an allocation lies in its shared arena. */
+int kvsnap_pool_arena(void* pool, void** base, size_t* capacity);
+/* Map another process's shared arena read-only into this one and register it
+   with CUDA (pinned, mapped, read-only) on `device`, so that its blocks serve
+   as restore sources in place: *base and *size receive the mapping. */
+int kvsnap_shared_open(const char* name, int device, void** base, size_t* size);
+/* Unregister and unmap a mapping from kvsnap_shared_open. The caller first
+   waits for every copy and kernel that reads it. */
+int kvsnap_shared_close(void* base, size_t size);
+
 /* ---- 2. data-plane kernels --------------------------------------------------- */
 
 #define KVSNAP_DP_ABI_VERSION 1

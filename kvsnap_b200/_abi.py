@@ -85,6 +85,10 @@ POOL_EXTRA = {
     "kvsnap_pool_copy_on": ([_P, C.c_uint64, _SZ, _P, _SZ, C.c_int, _SZ], C.c_int),
     "kvsnap_pool_copy_many": ([_P, C.c_int64, _P, _P, _P, _P, C.c_int, _SZ], C.c_int),
     "kvsnap_pool_wait_many": ([_P, C.c_int64, _P], C.c_int),
+    "kvsnap_pool_create_shared": ([_SZ, C.c_int, C.c_char_p], _P),
+    "kvsnap_pool_arena": ([_P, C.POINTER(C.c_void_p), C.POINTER(C.c_size_t)], C.c_int),
+    "kvsnap_shared_open": ([C.c_char_p, C.c_int, C.POINTER(C.c_void_p), C.POINTER(C.c_size_t)], C.c_int),
+    "kvsnap_shared_close": ([_P, _SZ], C.c_int),
 }
 
 DP_API = {

@@ -13,7 +13,14 @@
 // fake runtime (tests/native/fake_cudart.h) and drive its failure paths on a CPU.
 #include <cuda_runtime_api.h>
 
+#include <fcntl.h>
+#include <sys/mman.h>
+#include <sys/stat.h>
+#include <unistd.h>
+
+#include <cerrno>
 #include <cstdint>
+#include <cstring>
 #include <map>
 #include <vector>
 #include <memory>
@@ -51,6 +58,8 @@ struct Arena {
     char* base = nullptr;
     size_t capacity = 0;
     int device = 0;
+    std::string shared;          // the POSIX shared-memory name of a shared arena, else empty
+    bool registered = false;     // the shared mapping is registered with CUDA
     cudaStream_t stream = nullptr;
     std::map<uint64_t, Slot> slots;
     std::map<size_t, size_t> used;   // live ranges, offset -> size, in address order
@@ -66,7 +75,14 @@ struct Arena {
         for (auto& kv : slots)
             if (kv.second.done) cudaEventDestroy(kv.second.done);
         if (stream) cudaStreamDestroy(stream);
-        if (base) cudaFreeHost(base);
+        if (shared.empty()) {
+            if (base) cudaFreeHost(base);
+            return;
+        }
+        // A shared arena: other processes' mappings stay valid after the name goes.
+        if (registered) cudaHostUnregister(base);
+        if (base) munmap(base, capacity);
+        shm_unlink(shared.c_str());
     }
 
     Slot& slot(uint64_t id) {
@@ -153,6 +169,97 @@ extern "C" void* kvsnap_pool_create(size_t capacity, int device) {
     }
 }
 
+namespace {
+
+void check_shared_name(const char* name) {
+    if (!name || name[0] != '/' || std::strlen(name) < 2 || std::strlen(name) > 200 || std::strchr(name + 1, '/'))
+        throw Failure("a shared arena name is one path component that starts with '/'");
+}
+
+std::string os_error(const char* what) { return std::string(what) + ": " + std::strerror(errno); }
+
+}  // namespace
+
+extern "C" void* kvsnap_pool_create_shared(size_t capacity, int device, const char* name) {
+    try {
+        if (capacity == 0) throw Failure("pool capacity must be positive");
+        check_shared_name(name);
+        auto arena = std::make_unique<Arena>();
+        arena->capacity = capacity;
+        arena->device = device;
+        cuda(cudaSetDevice(device));
+        const int fd = shm_open(name, O_CREAT | O_EXCL | O_RDWR, 0600);
+        if (fd < 0) throw Failure(os_error("shm_open"));
+        arena->shared = name;     // from here the destructor unlinks the name
+        const bool sized = ftruncate(fd, static_cast<off_t>(capacity)) == 0;
+        void* base = sized ? mmap(nullptr, capacity, PROT_READ | PROT_WRITE, MAP_SHARED, fd, 0) : MAP_FAILED;
+        const std::string failed = sized ? os_error("mmap") : os_error("ftruncate");
+        close(fd);
+        if (base == MAP_FAILED) throw Failure(failed);
+        arena->base = static_cast<char*>(base);
+        // Portable: every device's context; mapped: kernels use it in place at its host address.
+        cuda(cudaHostRegister(base, capacity, cudaHostRegisterPortable | cudaHostRegisterMapped));
+        arena->registered = true;
+        cuda(cudaStreamCreateWithFlags(&arena->stream, cudaStreamNonBlocking));
+        return arena.release();
+    } catch (const std::exception& e) {
+        g_error = e.what();
+        return nullptr;
+    }
+}
+
+namespace {
+
+// Map the named segment and register it with CUDA: read-only where the platform
+// registers read-only host memory, else read-write (this process still only reads it).
+void* map_shared(const char* name, bool read_only, size_t* bytes, cudaError_t* registered) {
+    const int fd = shm_open(name, read_only ? O_RDONLY : O_RDWR, 0);
+    if (fd < 0) throw Failure(os_error("shm_open"));
+    struct stat st {};
+    if (fstat(fd, &st) != 0 || st.st_size <= 0) {
+        const std::string failed = os_error("fstat");
+        close(fd);
+        throw Failure(failed);
+    }
+    *bytes = static_cast<size_t>(st.st_size);
+    void* mapped = mmap(nullptr, *bytes, read_only ? PROT_READ : PROT_READ | PROT_WRITE, MAP_SHARED, fd, 0);
+    const std::string failed = os_error("mmap");
+    close(fd);
+    if (mapped == MAP_FAILED) throw Failure(failed);
+    const unsigned flags = cudaHostRegisterPortable | cudaHostRegisterMapped | (read_only ? cudaHostRegisterReadOnly : 0u);
+    *registered = cudaHostRegister(mapped, *bytes, flags);
+    if (*registered != cudaSuccess) munmap(mapped, *bytes);
+    return mapped;
+}
+
+}  // namespace
+
+extern "C" int kvsnap_shared_open(const char* name, int device, void** base, size_t* size) {
+    return guarded([&] {
+        check_shared_name(name);
+        if (!base || !size) throw Failure("opening a shared arena needs outputs");
+        cuda(cudaSetDevice(device));
+        size_t bytes = 0;
+        cudaError_t rc = cudaSuccess;
+        void* mapped = map_shared(name, true, &bytes, &rc);
+        if (rc != cudaSuccess) {
+            cudaGetLastError();                      // the read-only attempt's error is not this call's result
+            mapped = map_shared(name, false, &bytes, &rc);
+            cuda(rc);
+        }
+        *base = mapped;
+        *size = bytes;
+    });
+}
+
+extern "C" int kvsnap_shared_close(void* base, size_t size) {
+    return guarded([&] {
+        if (!base || !size) throw Failure("closing a shared arena needs its mapping");
+        cuda(cudaHostUnregister(base));
+        if (munmap(base, size) != 0) throw Failure(os_error("munmap"));
+    });
+}
+
 extern "C" void kvsnap_pool_destroy(void* pool) { delete static_cast<Arena*>(pool); }
 
 extern "C" int kvsnap_pool_close_checked(void* pool) {
@@ -163,6 +270,16 @@ extern "C" int kvsnap_pool_close_checked(void* pool) {
         cuda(cudaStreamSynchronize(a->stream));
         a->drained = true;
         delete a;
+    });
+}
+
+extern "C" int kvsnap_pool_arena(void* pool, void** base, size_t* capacity) {
+    return guarded([&] {
+        if (!pool || !base || !capacity) throw Failure("arena query requires a live pool and outputs");
+        Arena* a = static_cast<Arena*>(pool);
+        std::lock_guard<std::mutex> lock(a->mutex);
+        *base = a->base;
+        *capacity = a->capacity;
     });
 }
 

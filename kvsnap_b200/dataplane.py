@@ -214,7 +214,7 @@ class CudaPool:
     pool, its allocations and their tensor owners intact.
     """
 
-    def __init__(self, capacity_bytes: int, device: int = 0, library=None):
+    def __init__(self, capacity_bytes: int, device: int = 0, library=None, *, shared_name=None):
         self._pid = os.getpid()
         self._lock = threading.RLock()
         self._allocations = {}
@@ -223,7 +223,15 @@ class CudaPool:
         if self.abi_version != _abi.POOL_ABI_VERSION:
             raise RuntimeError("unsupported kvsnap CUDA pool ABI; rebuild both CUDA and torch extensions")
         self.device = device
-        self.handle = self.lib.kvsnap_pool_create(capacity_bytes, device)
+        # A shared pool's arena is POSIX shared memory other processes of this user map by name
+        # (kvsnap_b200.sharedtier), so they read its blocks in place instead of over a socket.
+        self.shared_name = shared_name
+        if shared_name is None:
+            self.handle = self.lib.kvsnap_pool_create(capacity_bytes, device)
+        else:
+            if not hasattr(self.lib, "kvsnap_pool_create_shared"):
+                raise RuntimeError("this CUDA library has no shared pools; rebuild with python -m kvsnap_b200.build")
+            self.handle = self.lib.kvsnap_pool_create_shared(capacity_bytes, device, shared_name.encode())
         if not self.handle:
             raise RuntimeError(self._error())
 
@@ -302,6 +310,13 @@ class CudaPool:
             if allocations:
                 ids = (C.c_uint64 * len(allocations))(*(a.ident for a in allocations))
                 self._native("kvsnap_pool_wait_many", len(allocations), ids)
+
+    def arena(self):
+        """``(address of the arena's first byte, capacity)``: an allocation lies at ``pointer - address``."""
+        with self.operation():
+            base, capacity = C.c_void_p(), C.c_size_t()
+            self._native("kvsnap_pool_arena", C.byref(base), C.byref(capacity))
+            return base.value, capacity.value
 
     def _owns(self, allocation):
         if allocation.pool is not self:
@@ -541,6 +556,10 @@ class TorchBlockDataPlane:
     it checks the CRCs over the pinned blocks first and then restores through
     the two-slot chunk ring; ``digest`` hashes the pinned blocks in place. A
     restore's chunk ring holds two ``chunk_bytes`` chunks.
+
+    ``shared_name`` puts the pinned pool in POSIX shared memory of that name, so
+    that other workers restore its host-tier blocks in place
+    (:mod:`kvsnap_b200.sharedtier`).
     """
 
     save_mode = "staged"
@@ -549,7 +568,7 @@ class TorchBlockDataPlane:
     sha_sms = 16
 
     def __init__(self, caches, block_size, capacity_bytes, *, save_mode=None, restore_mode=None, ctas=0,
-                 staging_bytes=512 << 20):
+                 staging_bytes=512 << 20, shared_name=None):
         import torch
         if not caches:
             raise ValueError("empty KV cache registration")
@@ -571,7 +590,7 @@ class TorchBlockDataPlane:
         # link, which 16-32 CTAs already saturate; the rest of the GPU stays free
         # for the engine and the SHA-256 kernel.
         self.host_ctas = ctas or 32
-        self.pool = CudaPool(capacity_bytes, device.index)
+        self.pool = CudaPool(capacity_bytes, device.index, shared_name=shared_name)
 
     @property
     def hbm_ctas(self):
@@ -816,7 +835,9 @@ class TorchBlockDataPlane:
         n, size = len(block_ids), self.block_bytes
         per_launch = max(1, chunk_bytes // size)
         verified = expected_crc32c is not None
-        mode = "staged" if verified else self.restore_mode
+        # Blocks of another process's shared arena (kvsnap_b200.sharedtier) are read in place.
+        foreign = any(getattr(allocation, "foreign", False) for allocation, _ in sources)
+        mode = "direct" if foreign else "staged" if verified else self.restore_mode
         copies, kernels = self._load_copy_stream, self._load_stream
         launches = 0
         done = None
@@ -835,6 +856,8 @@ class TorchBlockDataPlane:
                     if mode == "direct":
                         vec = self._vec_for(addresses)
                         table = torch.tensor(addresses, dtype=torch.int64).pin_memory().to(device, non_blocking=True)
+                        if verified:                 # every block checked where it lies, before any write
+                            self._verify(table, n, expected_crc32c, status, vec, self.host_ctas)
                         if progress is not None:
                             progress.append((None, n * size))
                         for first in range(0, n, per_launch):

@@ -26,6 +26,7 @@ std::deque<Copy> queue;            // not yet applied
 uint64_t enqueued = 0, applied = 0;
 std::string failing;
 int host_allocations = 0;
+int host_registrations = 0;
 uintptr_t last_stream = 0;
 
 bool fail(const char* name) {
@@ -137,3 +138,21 @@ void fake_cuda_discard_pending(void) {
     queue.clear();
 }
 }
+
+extern "C" cudaError_t cudaHostRegister(void* ptr, size_t size, unsigned) {
+    if (fail("cudaHostRegister")) return cudaErrorInjected;
+    if (!ptr || !size) return cudaErrorInjected;
+    ++host_registrations;
+    return cudaSuccess;
+}
+
+extern "C" cudaError_t cudaHostUnregister(void* ptr) {
+    if (fail("cudaHostUnregister")) return cudaErrorInjected;
+    if (!ptr) return cudaErrorInjected;
+    --host_registrations;
+    return cudaSuccess;
+}
+
+extern "C" int fake_cuda_live_host_registrations(void) { return host_registrations; }
+
+extern "C" cudaError_t cudaGetLastError(void) { return cudaSuccess; }

@@ -12,7 +12,8 @@ typedef struct FakeEvent* cudaEvent_t;
 
 enum : int { cudaSuccess = 0, cudaErrorNotReady = 600, cudaErrorInjected = 999 };
 enum : unsigned { cudaHostAllocPortable = 1, cudaHostAllocMapped = 2, cudaStreamNonBlocking = 1,
-                  cudaEventDisableTiming = 2 };
+                  cudaEventDisableTiming = 2, cudaHostRegisterPortable = 1, cudaHostRegisterMapped = 2,
+                  cudaHostRegisterReadOnly = 8 };
 enum cudaMemcpyKind { cudaMemcpyHostToDevice = 1, cudaMemcpyDeviceToHost = 2 };
 
 extern "C" {
@@ -20,6 +21,9 @@ const char* cudaGetErrorString(cudaError_t);
 cudaError_t cudaSetDevice(int);
 cudaError_t cudaHostAlloc(void**, size_t, unsigned);
 cudaError_t cudaFreeHost(void*);
+cudaError_t cudaHostRegister(void*, size_t, unsigned);
+cudaError_t cudaHostUnregister(void*);
+cudaError_t cudaGetLastError(void);
 cudaError_t cudaStreamCreateWithFlags(cudaStream_t*, unsigned);
 cudaError_t cudaStreamSynchronize(cudaStream_t);
 cudaError_t cudaDeviceSynchronize(void);
@@ -38,6 +42,7 @@ cudaError_t cudaMemcpy2DAsync(void*, size_t, const void*, size_t, size_t, size_t
 void fake_cuda_fail_next(const char* call);   // the next call of that name returns cudaErrorInjected
 int fake_cuda_pending(void);                   // queued copies not yet applied
 int fake_cuda_live_host_allocations(void);     // cudaHostAlloc minus cudaFreeHost
+int fake_cuda_live_host_registrations(void);   // cudaHostRegister minus cudaHostUnregister
 uintptr_t fake_cuda_last_stream(void);         // stream of the last queued copy
 void fake_cuda_discard_pending(void);          // drop queued copies without applying them
 }
