@@ -522,93 +522,143 @@ def reference_gpu(caches, save_ids, restore_ids, tokens, reps=5):
 
 # ---- the reference's CPU path ----------------------------------------------------------------------
 
-def reference_cpu(seconds, sample_blocks, threads, layers=LAYERS):
+class ReferenceCPU:
     """The reference's own host path on a bounded sample of the workload, timed on this host's cores.
 
-    Save: torch CPU ``index_select`` + ``cat`` of every layer's int64 rows
-    (kvsnap/connector/dataplane.py:417), then per block CRC32C by the
-    reference's compiled io.cpp (oracle/_ref; the oracle's C restatement if
-    that is absent) and ``hashlib.sha256`` over a thread pool
-    (kvsnap/store/store.py:616-629). Restore: ``index_copy_`` of each layer's
-    rows (bench/h2d_patterns.py:113-114). Returns GB/s of saved + restored bytes.
+    With the reference installed under baseline/_ref (kind "reference"), its
+    unmodified ``TorchBlockDataPlane`` runs on CPU tensors through the CUDA-free
+    stand-ins of ``oracle/refharness.py``: ``save_gather`` gathers with torch
+    ``index_select`` + ``cat`` and zeroes the last block's tail on the host
+    (kvsnap/connector/dataplane.py:388-437), the store hashes the packed blocks
+    with its own ``_prepare_payloads`` (SHA-256 and its compiled CRC32C on 8
+    threads, kvsnap/store/store.py:616-629), and ``load_scatter`` moves each
+    (block, layer) span the way its restore kernel does. Without it (kind
+    "port"): the same steps restated with torch, the oracle's CRC32C and
+    ``hashlib``. The cache is a ``pool_blocks`` Qwen3-8B pool in host memory,
+    far beyond the CPU caches, built once; each pass saves ``sample_blocks``
+    blocks (``ids``, seeded random ones by default) and restores them into
+    ``back``.
     """
-    import ctypes
-    import hashlib
 
-    import torch
-    torch.set_num_threads(threads)
-    ref = ROOT / "oracle" / "_ref" / "libkvsnap_io_ref.so"
-    kind = "reference"
-    if ref.is_file():
-        lib = ctypes.CDLL(str(ref))
-        crc_fn = lib.kvsnap_crc32c_extend
-    else:
-        from oracle import oracle as port
-        lib = port._lib()
-        crc_fn = lib.oracle_crc32c
-        kind = "port"
-    crc_fn.argtypes, crc_fn.restype = [ctypes.c_void_p, ctypes.c_size_t, ctypes.c_uint32], ctypes.c_uint32
-    pool_blocks = 2 * sample_blocks + 1
-    span_words = BLOCK * HEADS * HEAD_DIM * 2 // 8
-    gen = torch.Generator().manual_seed(1)
-    raw = [torch.randint(-2**62, 2**62, (2, pool_blocks, span_words), dtype=torch.int64, generator=gen)
-           for _ in range(layers)]
-    rows = [r[k] for r in raw for k in range(2)]
-    ids = torch.arange(1, sample_blocks + 1)
-    back = torch.arange(sample_blocks + 1, 2 * sample_blocks + 1)
-    size = len(rows) * span_words * 8
+    def __init__(self, sample_blocks, threads, layers=LAYERS, pool_blocks=1100, ids=None, back=None, tokens=None):
+        import numpy as np
+        import torch
+        torch.set_num_threads(threads)
+        self.threads, self.sample_blocks, self.pool_blocks = threads, sample_blocks, pool_blocks
+        caches = {}
+        for i in range(layers):
+            t = torch.empty((2, pool_blocks, BLOCK, HEADS, HEAD_DIM), dtype=torch.bfloat16)
+            t.view(torch.int16).fill_(0x1234 + i)
+            caches[f"model.layers.{i}.self_attn.attn"] = t
+        if ids is None:
+            order = np.random.Generator(np.random.PCG64(11)).permutation(pool_blocks - 1) + 1
+            ids = [int(b) for b in order[:sample_blocks]]
+            back = [int(b) for b in order[sample_blocks:2 * sample_blocks]]
+        tokens = sample_blocks * BLOCK - 5 if tokens is None else tokens
+        ref = ROOT / "baseline" / "_ref"
+        if (ref / "kvsnap" / "_native").is_dir():
+            self.kind = "reference"
+            if str(ref) not in sys.path:
+                sys.path.append(str(ref))
+            from unittest.mock import patch
+            from kvsnap.connector import dataplane as theirs
+            from kvsnap.store import store as their_store
+            from kvsnap_b200.dataplane import _split_paged
+            from oracle.refharness import HostBuffer, register, restore_by_memmove
+            plane = register(theirs, _split_paged(caches, BLOCK), BLOCK)
+            self.size = size = plane.block_bytes
+            targets = [(HostBuffer(size), 0) for _ in ids]      # reused, as the connector reuses pinned memory
 
-    def digest(block):
-        view = block.numpy()
-        return hashlib.sha256(view).hexdigest(), crc_fn(view.ctypes.data, view.nbytes, 0)
+            def one_pass():
+                plane.save_gather(ids, targets, tokens)
+                their_store._prepare_payloads([a.read_range(0, size) for a, _ in targets])
+                with patch.object(theirs, "copy_host_blocks", new=restore_by_memmove):
+                    plane.load_scatter(back, targets)
+        else:
+            import ctypes
+            import hashlib
+            self.kind = "port"
+            from oracle import oracle as port
+            crc_fn = port._lib().oracle_crc32c
+            crc_fn.argtypes, crc_fn.restype = [ctypes.c_void_p, ctypes.c_size_t, ctypes.c_uint32], ctypes.c_uint32
+            rows = [t[k].view(pool_blocks, -1).view(torch.int64) for t in caches.values() for k in range(2)]
+            span_words = rows[0].shape[1]
+            self.size = len(rows) * span_words * 8
+            id_t, back_t = torch.tensor(ids), torch.tensor(back)
 
-    done, start = 0, time.perf_counter()
-    with ThreadPoolExecutor(max_workers=threads) as pool:
+            def digest(block):
+                view = block.numpy()
+                return hashlib.sha256(view).hexdigest(), crc_fn(view.ctypes.data, view.nbytes, 0)
+
+            def one_pass():
+                stage = torch.cat([r.index_select(0, id_t) for r in rows], dim=1)
+                with ThreadPoolExecutor(max_workers=8) as hashers:
+                    list(hashers.map(digest, list(stage)))
+                offset = 0
+                for r in rows:
+                    r.index_copy_(0, back_t, stage[:, offset:offset + span_words])
+                    offset += span_words
+        self.one_pass = one_pass
+        one_pass()                                      # the pool's pages and the thread pools warm
+
+    def run(self, seconds):
+        """Passes for at least ``seconds`` (at least one); GB/s of saved + restored bytes."""
+        done, start = 0, time.perf_counter()
         while True:
-            stage = torch.cat([r.index_select(0, ids) for r in rows], dim=1)
-            list(pool.map(digest, list(stage)))
-            offset = 0
-            for r in rows:
-                r.index_copy_(0, back, stage[:, offset:offset + span_words])
-                offset += span_words
+            self.one_pass()
             done += 1
             if time.perf_counter() - start >= seconds:
                 break
-    elapsed = time.perf_counter() - start
-    moved = done * 2 * sample_blocks * size
-    return {"value": moved / elapsed / 1e9, "unit": UNIT, "cores": threads, "kind": kind,
-            "sample": f"{done} passes of save ({sample_blocks} Qwen3-8B blocks, {size} B each: torch CPU "
-                      f"index_select+cat gather, CRC32C + SHA-256 on {threads} threads) + restore (index_copy_), "
-                      f"{elapsed:.1f} s"}
+        elapsed = time.perf_counter() - start
+        moved = done * 2 * self.sample_blocks * self.size
+        return {"value": moved / elapsed / 1e9, "unit": UNIT, "cores": self.threads, "kind": self.kind,
+                "sample": f"{done} passes of save ({self.sample_blocks} Qwen3-8B blocks of {self.size} B from a "
+                          f"{self.pool_blocks}-block host pool: the reference's save_gather, its store's SHA-256 + "
+                          f"CRC32C on 8 threads) + restore (its load_scatter), {elapsed:.1f} s, {self.threads} "
+                          f"torch threads"}
 
 
 def run_reference(args, world, rank):
+    """``--impl reference``: the reference's own CPU path on this workload, rank 0 only.
+
+    Each step saves the session our arm saves (the same seeded block ids in a
+    pool of ``--pool-blocks`` blocks, in host memory) through the reference's
+    ``save_gather`` and store hashing, and restores it through its
+    ``load_scatter`` (see ``ReferenceCPU``), on every host thread.
+    """
     if rank != 0:
         return
     threads = os.cpu_count() or 1
-    steps, warm = args.steps, args.warmup
-    sample = 32
-    reference_cpu(0.1, sample, threads)            # warm caches and the thread pool
-    values = []
-    t0 = time.perf_counter()
-    for _ in range(warm):
-        reference_cpu(0.0, sample, threads)
-    for _ in range(steps):
-        values.append(reference_cpu(0.0, sample, threads))
+    n = (args.tokens + BLOCK - 1) // BLOCK
+    save_ids, restore_ids = session_blocks(args, n)
+    t_setup = time.perf_counter()
+    cpu = ReferenceCPU(n, threads, layers=args.layers, pool_blocks=args.pool_blocks, ids=save_ids,
+                       back=restore_ids, tokens=args.tokens)
+    log(f"reference CPU setup {time.perf_counter() - t_setup:.1f} s ({cpu.kind})")
+    for _ in range(args.warmup):
+        cpu.run(0.0)
+    values, t0 = [], time.perf_counter()
+    for _ in range(args.steps):
+        values.append(cpu.run(0.0))
     elapsed = time.perf_counter() - t0
-    value = statistics.mean(v["value"] for v in values)
-    base = values[-1]
-    session_bytes = args.tokens // BLOCK * LAYERS * 2 * BLOCK * HEADS * HEAD_DIM * 2
-    line = {"metric": METRIC, "value": round(value, 3), "unit": UNIT, "n_gpus": args.gpus, "steps": steps,
-            "warmup": warm, "ms_per_step": round(elapsed / (steps + warm) * 1e3, 3), "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "u8", "data": "synthetic",
-            "impl": "reference",
-            "config": {"workload": "qwen3-8b 8k-token session save+restore (CPU reference path, bounded sample)",
-                       "session_bytes": session_bytes, "sample_blocks_per_step": sample},
-            "cpu_baseline": {"value": round(value, 3), "unit": UNIT, "cores": threads, "kind": base["kind"],
-                             "sample": f"each step: {sample} blocks saved (gather, CRC32C, SHA-256) and restored"},
+    value = cpu.sample_blocks * cpu.size * 2 * args.steps / elapsed / 1e9
+    line = {"metric": METRIC, "value": round(value, 3), "unit": UNIT, "n_gpus": args.gpus, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(elapsed / args.steps * 1e3, 3), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "u8", "data": "synthetic", "impl": "reference",
+            "config": session_config(args, n, cpu.size),
+            "cpu_baseline": {"value": round(value, 3), "unit": UNIT, "cores": threads, "kind": cpu.kind,
+                             "sample": f"every step the whole session: {values[-1]['sample']}"},
             "e2e": {"value": round(value, 3), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
+
+
+def session_config(args, n, size):
+    """The ``config`` of the session workload (BASELINE config 2 by default)."""
+    return {"workload": ("qwen3-8b 8k-token session save+restore (BASELINE config 2)" if args.model == "qwen3-8b"
+                         else f"qwen3-32b 32k-token session, TP shard a rank (BASELINE config 5)"),
+            "layers": args.layers, "kv_heads": args.heads, "head_dim": HEAD_DIM, "block_size": BLOCK,
+            "pool_blocks": args.pool_blocks, "session_blocks": n, "session_bytes": n * size,
+            "l2": "inputs (1.2 GB a step) larger than L2; no flush", "kv": "bf16, seeded"}
 
 
 # ---- main ----------------------------------------------------------------------------------------------
@@ -792,7 +842,7 @@ def main():
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
-        cpu = reference_cpu(10.0, 32, os.cpu_count() or 1)
+        cpu = ReferenceCPU(n, os.cpu_count() or 1, ids=save_ids, back=restore_ids, tokens=args.tokens).run(10.0)
 
     peaks = json.loads(PEAKS.read_text()) if PEAKS.is_file() else {}
     hbm_peak = peaks.get("hbm_gbs", 6650.0)
@@ -807,12 +857,7 @@ def main():
         "metric": METRIC, "value": round(value, 3), "unit": UNIT, "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(ms, 3), "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "u8", "data": "synthetic",
-        "config": {"workload": ("qwen3-8b 8k-token session save+restore (BASELINE config 2)" if args.model == "qwen3-8b"
-                                else f"qwen3-32b 32k-token session, TP-{world} shard a rank (BASELINE config 5)"),
-                   "layers": args.layers, "kv_heads": args.heads, "head_dim": HEAD_DIM, "block_size": BLOCK,
-                   "pool_blocks": args.pool_blocks, "session_blocks": n, "session_bytes": session,
-                   "restore_mode": args.restore_mode, "l2": "inputs (1.2 GB a step) larger than L2; no flush",
-                   "kv": "bf16 N(0,1), seeded"},
+        "config": dict(session_config(args, n, size), restore_mode=args.restore_mode),
         "phases_ms": {k: round(v, 3) for k, v in phases.items()},
         "restore_ms": round(restore_ms, 3),
         "save_ms": round(save_ms, 3),

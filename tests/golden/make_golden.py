@@ -39,114 +39,11 @@ REPO = Path(__file__).resolve().parents[2]
 sys.path.insert(0, str(REPO / "tests"))
 import kvgen  # noqa: E402
 
-
-# ---- CUDA-free stand-ins the reference data plane runs against -------------
-
-class _Event:
-    def record(self, stream=None):
-        pass
-
-    def synchronize(self):
-        pass
-
-    def query(self):
-        return True
+sys.path.insert(0, str(REPO))
+from oracle.refharness import HostBuffer, register, restore_by_memmove  # noqa: E402
 
 
-class _Stream:
-    def synchronize(self):
-        pass
-
-
-class _Pinnable:
-    """What ``torch.tensor`` returns here: ``pin_memory()`` is the tensor itself."""
-    def __init__(self, tensor):
-        self._tensor = tensor
-
-    def pin_memory(self):
-        return self._tensor
-
-    def __getattr__(self, name):
-        return getattr(self._tensor, name)
-
-
-class _Torch:
-    """The ``torch`` module as the reference data plane sees it, minus CUDA."""
-    cuda = SimpleNamespace(stream=lambda stream: contextlib.nullcontext(), Event=_Event,
-                           ExternalStream=lambda handle, device=None: _Stream())
-
-    def __getattr__(self, name):
-        return getattr(torch, name)
-
-    def tensor(self, *args, **kwargs):
-        return _Pinnable(torch.tensor(*args, **kwargs))
-
-
-class _OnCuda:
-    """A CPU tensor that claims a CUDA device, for the registration-time device check."""
-    device = SimpleNamespace(type="cuda", index=0)
-
-    def __init__(self, tensor):
-        self._tensor = tensor
-
-    def __getattr__(self, name):
-        return getattr(self._tensor, name)
-
-    def __getitem__(self, index):
-        return self._tensor[index]
-
-
-class _HostBuffer:
-    """A pinned allocation stand-in: a host buffer whose copies are memmoves."""
-    def __init__(self, size):
-        self.size, self.closed = size, False
-        self._buffer = C.create_string_buffer(max(size, 1))
-        self.pointer = C.addressof(self._buffer)
-
-    def _open(self):
-        if self.closed:
-            raise RuntimeError("pinned allocation closed")
-
-    def copy(self, device_ptr, size, offset=0, *, to_host, producer_stream=0):
-        if offset < 0 or offset + size > self.size:
-            raise ValueError("copy outside allocation")
-        host = self.pointer + offset
-        C.memmove(host if to_host else device_ptr, device_ptr if to_host else host, size)
-
-    def wait(self):
-        pass
-
-    def zero(self, offset, size):
-        C.memset(self.pointer + offset, 0, size)
-
-    def read_range(self, offset, size):
-        return C.string_at(self.pointer + offset, size)
-
-
-class _Pool:
-    @contextlib.contextmanager
-    def borrow_copy_stream(self):
-        yield 1
-
-    @contextlib.contextmanager
-    def operation(self):
-        yield
-
-
-def _restore_by_memmove(sources, blocks, layer_offsets, layer_bases, layer_pitches, layer_words):
-    layers = list(zip(*(t.tolist() for t in (layer_offsets, layer_bases, layer_pitches, layer_words))))
-    for source, block in zip(sources.tolist(), blocks.tolist()):
-        for offset, base, pitch, words in layers:
-            C.memmove(base + block * pitch, source + offset, words * 8)
-
-
-def register(dataplane, caches, block_size):
-    with patch.dict(sys.modules, {"torch": _Torch()}), \
-         patch.object(dataplane, "CudaPool", return_value=_Pool()):
-        plane = dataplane.TorchBlockDataPlane({k: _OnCuda(v) for k, v in caches.items()}, block_size, 1 << 30)
-    plane.caches = dict(sorted(caches.items()))
-    return plane
-
+# ---- the CUDA-free stand-ins live in oracle/refharness.py ---------------------
 
 # ---- cache geometries -------------------------------------------------------
 
@@ -187,9 +84,9 @@ def save_case(dataplane, crc32c, caches, block_size, saved, restored, tokens, ch
     for kind in ("per-block", "staging"):
         for chunk in (64 << 20, chunk_blocks * size):
             if kind == "per-block":
-                targets = [(_HostBuffer(size), 0) for _ in saved]
+                targets = [(HostBuffer(size), 0) for _ in saved]
             else:
-                staged = _HostBuffer(size * len(saved))
+                staged = HostBuffer(size * len(saved))
                 targets = [(staged, i * size) for i in range(len(saved))]
             copies = plane.save_gather(saved, targets, tokens, chunk_bytes=chunk)
             out.setdefault("copies", {})[f"{kind}/{chunk}"] = copies
@@ -198,11 +95,11 @@ def save_case(dataplane, crc32c, caches, block_size, saved, restored, tokens, ch
             out.setdefault("digests", digests)
             assert out["digests"] == digests, "packed blocks depend on the target kind"
     # Restore the staged snapshot into other blocks, chunked, and record what moved.
-    staged = _HostBuffer(size * len(saved))
+    staged = HostBuffer(size * len(saved))
     targets = [(staged, i * size) for i in range(len(saved))]
     plane.save_gather(saved, targets, tokens)
     progress = []
-    with patch.object(dataplane, "copy_host_blocks", new=_restore_by_memmove):
+    with patch.object(dataplane, "copy_host_blocks", new=restore_by_memmove):
         launches = plane.load_scatter(restored, targets, progress=progress, chunk_bytes=chunk_blocks * size)
     out["launches"] = launches
     out["restore_chunk_bytes"] = chunk_blocks * size
@@ -271,10 +168,10 @@ def main():
         storage = raw.view(torch.bfloat16)
         cache = storage.as_strided((5, 3, 4, 8), strides)
         plane = register(dataplane, {"layer.0": cache}, 4)
-        targets = [(_HostBuffer(plane.block_bytes), 0) for _ in range(2)]
+        targets = [(HostBuffer(plane.block_bytes), 0) for _ in range(2)]
         plane.save_gather([1, 3], targets, 6)
         packed = [a.read_range(0, plane.block_bytes).hex() for a, _ in targets]
-        with patch.object(dataplane, "copy_host_blocks", new=_restore_by_memmove):
+        with patch.object(dataplane, "copy_host_blocks", new=restore_by_memmove):
             plane.load_scatter([0, 4], targets)
         small.append({"strides": list(strides), "seed": strides[0] + strides[1], "saved": [1, 3],
                       "num_kv_tokens": 6, "packed_hex": packed, "restored": [0, 4],
