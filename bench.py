@@ -630,6 +630,16 @@ def run_reference(args, world, rank):
         return
     threads = os.cpu_count() or 1
     n = (args.tokens + BLOCK - 1) // BLOCK
+    # The pool lives in host memory here: on a host with too little free memory for the configured pool,
+    # the largest one that fits in 60 % of it (the config line then records that size).
+    block = args.layers * 2 * BLOCK * args.heads * HEAD_DIM * 2
+    free = os.sysconf("SC_AVPHYS_PAGES") * os.sysconf("SC_PAGE_SIZE")
+    fits = int(0.6 * free) // block
+    if fits < args.pool_blocks:
+        if fits < 2 * n + 1:
+            raise SystemExit(f"host memory holds {fits} blocks; the session needs a pool of {2 * n + 1}")
+        log(f"host memory: pool of {fits} blocks instead of {args.pool_blocks}")
+        args.pool_blocks = fits
     save_ids, restore_ids = session_blocks(args, n)
     t_setup = time.perf_counter()
     cpu = ReferenceCPU(n, threads, layers=args.layers, pool_blocks=args.pool_blocks, ids=save_ids,
