@@ -885,13 +885,15 @@ def main():
                                   "the ceiling the whole-job value shares"},
         "roofline": {"bound": "hbm", "kernel": "span_kernel_hbm<gather>: KV -> device staging, tail zero, CRC32C",
                      "achieved": round(gather_gbs, 1), "peak": hbm_peak, "unit": "GB/s",
-                     "frac": round(gather_gbs / hbm_peak, 3), "traffic": 2.366e9,
-                     "traffic_note": "ncu dram read+write per launch, profiles/span_kernel_hbm_gather_qwen3-8b_512-blocks.md",
+                     "frac": round(gather_gbs / hbm_peak, 3),
+                     **captured_traffic("span_kernel_hbm<gather> qwen3-8b 512 blocks", args, n),
                      "algorithmic_bytes": 2 * session, "ms": round(kernel_ms["gather"], 4),
-                     "peak_source": f"{peak_src} hbm_gbs (burst copy)"},
+                     "launch": f"{engine.ctas} CTAs", "peak_source": f"{peak_src} hbm_gbs (burst copy)"},
         "roofline_scatter": {"bound": "hbm", "kernel": "span_kernel_hbm<scatter>: device staging -> KV, CRC32C check",
                              "achieved": round(scatter_gbs, 1), "peak": hbm_peak, "unit": "GB/s",
-                             "frac": round(scatter_gbs / hbm_peak, 3), "ms": round(kernel_ms["scatter"], 4)},
+                             "frac": round(scatter_gbs / hbm_peak, 3),
+                             **captured_traffic("span_kernel_hbm<scatter> qwen3-8b 512 blocks", args, n),
+                             "ms": round(kernel_ms["scatter"], 4)},
         "sha256_gbs": round(session / (phases["sha256"] / 1e3) / 1e9, 2),
         "e2e": {"value": round(e2e, 3), "unit": UNIT, "ms_per_step": round(e2e_ms, 3),
                 "h2d_bytes_per_step": session + 16 * n, "d2h_bytes_per_step": session + 36 * n},
@@ -920,6 +922,18 @@ def main():
     if world > 1:
         import torch.distributed as dist
         dist.destroy_process_group()
+
+
+def captured_traffic(kernel, args, n):
+    """``traffic`` of a roofline field: DRAM read + write bytes per launch of ``kernel`` from its ncu capture
+    (profiles/roofline_traffic.json, written from the summaries there), for the workload it was captured on."""
+    path = ROOT / "profiles" / "roofline_traffic.json"
+    entry = json.loads(path.read_text()).get(kernel) if path.is_file() else None
+    if entry is None or args.model != "qwen3-8b" or args.layers != LAYERS or n != 512:
+        return {"traffic": None, "traffic_note": "no ncu capture of this kernel on this workload"}
+    return {"traffic": entry["dram_read_bytes"] + entry["dram_write_bytes"],
+            "traffic_note": f"ncu dram__bytes_read.sum + dram__bytes_write.sum per launch ({entry['launch']}), "
+                            f"{entry['summary']}"}
 
 
 def release_device_memory():
