@@ -279,6 +279,7 @@ struct SpanArgs {
     int pairs = 0;           // runs of segment kernels: units are pairs of spans (KVSNAP_DP_PAIRS)
     int split = 0;           // grid-stride segment kernels: units are 1 / 2^split of a span (KVSNAP_DP_SPLIT*)
     int place = 0;           // grid-stride segment kernels: placement tables follow the line buffers
+    int spans_at = -1;       // segment kernels: byte offset of a shared-memory copy of the span table, or -1
 };
 
 template <int VEC, int MODE>
@@ -687,6 +688,7 @@ struct SpanUnits {
     int p, dp;           // piece of the cursor in its span, and its step (grid-stride)
     int width;           // spans a unit: 2 for pairs (RANGE only), else 1
     int split;           // log2 of the units a span (grid-stride only), else 0
+    int64_t held = -1, held_block = 0, held_packed = 0;   // packed block `held`'s cache id and address
     __device__ SpanUnits(const SpanArgs& args, int64_t w, int64_t warps) : a(args) {
         width = RANGE && args.pairs ? 2 : 1;
         split = RANGE ? 0 : args.split;
@@ -726,13 +728,18 @@ struct SpanUnits {
     __device__ __forceinline__ bool next(SegUnit& out, int lane) {
         for (; left > 0; step()) {
             const kvsnap_span& sp = a.spans[s];
-            const int64_t block = a.blocks[i];
+            if (i != held) {     // a block's units are mostly consecutive: its table entries are read once
+                held_block = a.blocks[i];
+                held_packed = a.packed[i];
+                held = i;
+            }
+            const int64_t block = held_block;
             if (block < 0 || block >= sp.nblocks) {
                 if (lane == 0) flag(a.status, KVSNAP_DP_BAD_BLOCK);
                 continue;
             }
             int64_t bytes = sp.bytes >> split;
-            const int64_t packed = a.packed[i] + sp.offset + p * bytes;
+            const int64_t packed = held_packed + sp.offset + p * bytes;
             const int64_t cache = sp.base + block * sp.pitch + p * bytes;
             if (split && (bytes << split != sp.bytes || bytes % kSegStep)) {   // whole steps a segment, no padding
                 if (lane == 0) flag(a.status, KVSNAP_DP_BAD_CUT);
@@ -1004,17 +1011,26 @@ __global__ void __launch_bounds__(kSegThreads, 1) span_kernel_hbm(SpanArgs a) {
             pl = Placement{reinterpret_cast<const char*>(win) + 4 * lane, win + kWinWords, seg, split};
         }
     }
+    // The span table each unit's description reads, copied where the launcher made room for it:
+    // small units (a TP shard's) look it up every other step.
+    SpanArgs b = a;
+    if (a.spans_at >= 0) {
+        uint4* to = reinterpret_cast<uint4*>(reinterpret_cast<char*>(smem) + a.spans_at);
+        const uint4* from = reinterpret_cast<const uint4*>(a.spans);
+        for (int k = threadIdx.x; k < a.nspans * int(sizeof(kvsnap_span) / 16); k += blockDim.x) to[k] = from[k];
+        b.spans = reinterpret_cast<const kvsnap_span*>(to);
+    }
     __syncthreads();
     if (MODE == kScatter && a.gate && *a.gate) return;
     const RepTables tl{reinterpret_cast<const char*>(tb), 4u * lane};
     const AppendBytes append{tx, span_bytes};
     const int64_t w = (int64_t)blockIdx.x * per_cta + warp, warps = (int64_t)gridDim.x * per_cta;
     if (!crc)
-        warp_stream<true, false, TAIL, false>(SpanUnits<MODE, false>(a, w, warps), tl, t4, append, ring, lane,
-                                              nullptr, a.spans, a.valid);
+        warp_stream<true, false, TAIL, false>(SpanUnits<MODE, false>(b, w, warps), tl, t4, append, ring, lane,
+                                              nullptr, b.spans, b.valid);
     else
         warp_stream<true, true, TAIL, RUNS, RUNS ? (MODE == kGather ? 1 : 2) : 0>(
-            SpanUnits<MODE, RUNS>(a, w, warps), tl, t4, append, ring, lane, a.crc, a.spans, a.valid, pl);
+            SpanUnits<MODE, RUNS>(b, w, warps), tl, t4, append, ring, lane, b.crc, b.spans, b.valid, pl);
 }
 
 // `place`: the launcher sized shared memory for placement tables with a shift row a piece.
@@ -1553,6 +1569,18 @@ extern "C" int kvsnap_dp_plan(kvsnap_span* spans, int nspans, uint64_t* block_by
 
 namespace {
 
+// Room for a shared-memory copy of the span table after a segment kernel's `bytes`, when it keeps
+// the launch within kSegCarveBytes (the L1 the loads in flight need); returns the launch's bytes.
+static_assert(sizeof(kvsnap_span) % 16 == 0, "the span table is copied in 16-byte vectors");
+int with_span_table(SpanArgs& a, int bytes, int nspans) {
+    const int at = (bytes + 15) / 16 * 16;
+    const int end = at + nspans * int(sizeof(kvsnap_span));
+    // The copy loads the table in 16-byte vectors: only a 16-byte aligned table is copied.
+    if (end > kSegCarveBytes || (reinterpret_cast<uintptr_t>(a.spans) & 15)) return bytes;
+    a.spans_at = at;
+    return end;
+}
+
 // The gather or scatter launches; throws Fail on a bad request or a CUDA error.
 template <int MODE>
 void spans_launch(const kvsnap_span* spans, int nspans, uint64_t block_bytes, const int64_t* blocks,
@@ -1590,10 +1618,10 @@ void spans_launch(const kvsnap_span* spans, int nspans, uint64_t block_bytes, co
                     body = n - 1;
                     SpanArgs last{spans, nspans, blocks + body, packed + body, 1, valid, crc ? crc + body : nullptr,
                                   gate, status};
+                    int bytes = crc ? seg_smem_bytes(kSegWarps, false) : seg_ring_bytes(kSegWarps);
+                    bytes = with_span_table(last, bytes, nspans);
                     configure_once(reinterpret_cast<const void*>(span_kernel_hbm<MODE, true, false>), kSegSmemMax);
-                    span_kernel_hbm<MODE, true, false><<<grid_of(1, kSegWarps), kSegThreads,
-                                                         crc ? seg_smem_bytes(kSegWarps, false) : seg_ring_bytes(kSegWarps),
-                                                         s>>>(last);
+                    span_kernel_hbm<MODE, true, false><<<grid_of(1, kSegWarps), kSegThreads, bytes, s>>>(last);
                     check(cudaGetLastError());
                 }
             }
@@ -1607,8 +1635,8 @@ void spans_launch(const kvsnap_span* spans, int nspans, uint64_t block_bytes, co
                 // Grid-stride units are placed by table when the rows fit within kSegCarveBytes.
                 const int rows = nspans << split;
                 a.place = crc && !runs && rows <= place_rows(warps);
-                const int bytes = !crc ? seg_ring_bytes(warps)
-                                       : seg_smem_bytes(warps, runs) + (a.place ? place_bytes(rows) : 0);
+                int bytes = !crc ? seg_ring_bytes(warps) : seg_smem_bytes(warps, runs) + (a.place ? place_bytes(rows) : 0);
+                bytes = with_span_table(a, bytes, nspans);
                 configure_once(reinterpret_cast<const void*>(kernel), kSegSmemMax);
                 kernel<<<grid_of(body, warps), 32 * warps, bytes, s>>>(a);
                 check(cudaGetLastError());
