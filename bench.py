@@ -852,7 +852,8 @@ def main():
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
-        cpu = ReferenceCPU(n, os.cpu_count() or 1, ids=save_ids, back=restore_ids, tokens=args.tokens).run(10.0)
+        # The whole session from the CPU arm's own host pool (its seeded block ids), for 10 s.
+        cpu = ReferenceCPU(n, os.cpu_count() or 1, pool_blocks=max(1100, 2 * n + 1), tokens=args.tokens).run(10.0)
 
     peaks = json.loads(PEAKS.read_text()) if PEAKS.is_file() else {}
     hbm_peak = peaks.get("hbm_gbs", 6650.0)
