@@ -850,10 +850,6 @@ def main():
         explore = explore_phases(plane, engine, save_ids, restore_ids, link)
         Path(args.explore).write_text(json.dumps(explore, indent=1))
 
-    cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu:
-        # The whole session from the CPU arm's own host pool (its seeded block ids), for 10 s.
-        cpu = ReferenceCPU(n, os.cpu_count() or 1, pool_blocks=max(1100, 2 * n + 1), tokens=args.tokens).run(10.0)
 
     peaks = json.loads(PEAKS.read_text()) if PEAKS.is_file() else {}
     hbm_peak = peaks.get("hbm_gbs", 6650.0)
@@ -905,8 +901,6 @@ def main():
                               note="both until the packed blocks are in pinned memory (save) or in the cache "
                                    "(restore); ours also computes CRC32C on the way and SHA-256 after"),
     }
-    if cpu is not None:
-        line["cpu_baseline"] = cpu
     for snap in engine.snapshot:
         snap.close()
     plane.close()
@@ -918,6 +912,11 @@ def main():
         line["sharded"] = measure_sharded(args, world, rank, device, box_duplex)
         if world >= 2 and world % 2 == 0:
             line["reshard"] = measure_reshard(args, world, rank, device)
+    if rank == 0 and world == 1 and not args.no_cpu:
+        # Last, so that its host-memory traffic touches no GPU measurement: the whole session from the
+        # CPU arm's own host pool (its seeded block ids), for 10 s.
+        line["cpu_baseline"] = ReferenceCPU(n, os.cpu_count() or 1, pool_blocks=max(1100, 2 * n + 1),
+                                            tokens=args.tokens).run(10.0)
     if rank == 0:
         print(json.dumps(line), flush=True)
     if world > 1:
