@@ -470,6 +470,15 @@ __device__ __forceinline__ uint4 seg_load(const char* src, int64_t at) {
     return v;
 }
 
+// The same load at an address known to be inside the source (no front padding).
+__device__ __forceinline__ uint4 seg_load_line(const char* p) {
+    uint4 v;
+    asm("ld.global.L1::no_allocate.L2::256B.v4.u32 {%0, %1, %2, %3}, [%4];"
+        : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+        : "l"(p));
+    return v;
+}
+
 // Both sides are streamed: a session is far larger than L2, so nothing a
 // gather or scatter touches is read again from L2.
 __device__ __forceinline__ void seg_store(char* dst, int64_t at, uint4 v) {
@@ -910,13 +919,28 @@ __device__ __forceinline__ void warp_stream(Units units, const RepTables& tl, co
         }
         const bool refill = loading;
         if (refill) load_addr();
+        if (!TAIL && P.pad == 0 && (!refill || L.pad == 0)) {
+            // No front padding on either side (every unit of a whole number of 4 KiB steps): each
+            // side's eight lines are one base plus constant offsets, with no per-line test. On
+            // B200 this path moved 4 and 8 KiB spans 4 to 5 % faster at 132 CTAs. Issuing each
+            // refill before its line is folded (a copy of the line kept) measured 8 % slower.
+            char* const sd = sbase + first;
+            const char* const ls = lbase + lfirst;
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
-            const int64_t at = first + j * kSegLine;     // the front padding can cover whole segments
-            if (TAIL && at >= 0) v[j] = mask.apply(v[j], at, sp, valid);
-            if (STORE && at >= 0) seg_store(sbase, at, v[j]);
-            if (CRC) r.fold(tl, v[j]);
-            if (refill) v[j] = seg_load(lbase, lfirst + j * kSegLine);
+            for (int j = 0; j < 8; ++j) {
+                if (STORE) __stcs(reinterpret_cast<uint4*>(sd + j * kSegLine), v[j]);
+                if (CRC) r.fold(tl, v[j]);
+                if (refill) v[j] = seg_load_line(ls + j * kSegLine);
+            }
+        } else {
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                const int64_t at = first + j * kSegLine;     // the front padding can cover whole segments
+                if (TAIL && at >= 0) v[j] = mask.apply(v[j], at, sp, valid);
+                if (STORE && at >= 0) seg_store(sbase, at, v[j]);
+                if (CRC) r.fold(tl, v[j]);
+                if (refill) v[j] = seg_load(lbase, lfirst + j * kSegLine);
+            }
         }
         if (refill) load_move();
         return refill;
@@ -1607,9 +1631,13 @@ void spans_launch(const kvsnap_span* spans, int nspans, uint64_t block_bytes, co
         if (crc && !accumulate) check(cudaMemsetAsync(crc, 0, sizeof(uint32_t) * size_t(n), s));
         SpanArgs a{spans, nspans, blocks, packed, n, valid, crc, gate, status, pairs ? 1 : 0, split};
         if (hbm) {
+            // Without a CTA count, the segment kernels run on all SMs but one in nine (132 of 148):
+            // with 12 warps a CTA, B200 moved every span size fastest at 128 to 136 CTAs, and 3 to
+            // 10 % slower from 140 CTAs on (4, 8, 16 and 32 KiB spans alike).
+            const int cap = ctas > 0 ? ctas : (sms - sms / 9 > 0 ? sms - sms / 9 : 1);
             auto grid_of = [&](int64_t blocks_of_work, int warps) {
                 const int64_t want = ((blocks_of_work * nspans << split) + warps - 1) / warps;
-                return ctas > 0 ? ctas : int(want < sms ? want : sms);
+                return ctas > 0 ? ctas : int(want < cap ? want : cap);
             };
 
             int64_t body = n;
@@ -1628,10 +1656,10 @@ void spans_launch(const kvsnap_span* spans, int nspans, uint64_t block_bytes, co
             if (body > 0) {
                 a.n = body;
                 auto kernel = runs ? span_kernel_hbm<MODE, false, true> : span_kernel_hbm<MODE, false, false>;
-                // A launch on fewer CTAs than SMs (one that leaves SMs to other kernels) keeps more loads in
-                // flight a CTA: at 132 of 148 SMs, 12 warps moved Qwen3-8B spans at 0.90 of the HBM copy
-                // rate where 10 reached 0.86; on every SM, 10 warps measured fastest.
-                const int warps = runs || (ctas > 0 && ctas < sms) ? kSegWarps : kSegBulkWarps;
+                // A launch on fewer CTAs than SMs keeps more loads in flight a CTA: at 132 of 148 SMs, 12
+                // warps moved Qwen3-8B spans at 0.93 of the HBM copy rate where 10 reached 0.91; a launch
+                // asked for on every SM takes 10 warps, which measured fastest there.
+                const int warps = runs || cap < sms ? kSegWarps : kSegBulkWarps;
                 // Grid-stride units are placed by table when the rows fit within kSegCarveBytes.
                 const int rows = nspans << split;
                 a.place = crc && !runs && rows <= place_rows(warps);
