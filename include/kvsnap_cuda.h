@@ -249,6 +249,18 @@ int kvsnap_dp_sha256_part(const int64_t* addrs, int64_t n, uint64_t part_bytes, 
 int kvsnap_dp_land(const void* src, int64_t src_stride, const int64_t* targets, int64_t offset, int64_t n,
                    int64_t len, uint32_t* status, int ctas, uintptr_t stream);
 
+/* Land one column of n packed blocks whose targets lie at one pitch: bytes
+   [0, len) at src + i * src_stride are copied to dst + i * dst_pitch, for
+   i < n, as one copy-engine transfer (cudaMemcpy2DAsync, device to host) on
+   `stream`. dst is pinned host memory. A bounded save's column is n small
+   pieces, so when its targets are evenly spaced (blocks reserved back to back,
+   or one buffer) this moves the column at the copy engine's rate while the SMs
+   gather the next one; otherwise kvsnap_dp_land. No counterpart in the
+   reference, whose save copies whole chunks with cudaMemcpyAsync
+   (kvsnap/connector/dataplane.py:418-427). */
+int kvsnap_dp_land_strided(const void* src, int64_t src_stride, void* dst, int64_t dst_pitch, int64_t n,
+                           int64_t len, uintptr_t stream);
+
 /* Finish raw CRC accumulators that KVSNAP_DP_HBM gathers or scatters left
    under KVSNAP_DP_CRC_ACCUMULATE: crc[i] becomes block i's CRC32C; with
    expect not NULL, mismatches set KVSNAP_DP_CRC_MISMATCH in *status. */

@@ -102,6 +102,7 @@ DP_API = {
     "kvsnap_dp_sha256_part": ([_P, _I64, _U64, _U64, _U64, _P, _P, _SZ], C.c_int),
     "kvsnap_dp_crc32c_finish": ([_P, _P, _I64, _U64, _P, _SZ], C.c_int),
     "kvsnap_dp_land": ([_P, _I64, _P, _I64, _I64, _I64, _P, C.c_int, _SZ], C.c_int),
+    "kvsnap_dp_land_strided": ([_P, _I64, _P, _I64, _I64, _I64, _SZ], C.c_int),
     "kvsnap_dp_copy_host_blocks": ([_P, _P, _I64, _P, _P, _P, _P, _I64, C.c_int, _SZ], C.c_int),
     "kvsnap_dp_regroup": ([_P, _P, C.c_int, _P, C.c_int, _P, _I64, _P, C.c_int, _SZ], C.c_int),
     "kvsnap_dp_device_alloc": ([_SZ, C.c_int, C.POINTER(C.c_void_p)], C.c_int),

@@ -1815,6 +1815,21 @@ extern "C" int kvsnap_dp_land(const void* src, int64_t src_stride, const int64_t
     });
 }
 
+extern "C" int kvsnap_dp_land_strided(const void* src, int64_t src_stride, void* dst, int64_t dst_pitch, int64_t n,
+                                      int64_t len, uintptr_t stream) {
+    return guarded([&] {
+        if (n < 0 || len < 0 || src_stride < 0 || dst_pitch < 0) throw Fail{"invalid landing request"};
+        if (n == 0 || len == 0) return;
+        if (!src || !dst) throw Fail{"landing needs a source and a destination"};
+        if (n > 1 && (src_stride < len || dst_pitch < len))
+            throw Fail{"landing rows overlap (a stride or pitch below the length)"};
+        enter_stream(stream);
+        // One copy-engine transfer for the whole column: n rows of len bytes.
+        check(cudaMemcpy2DAsync(dst, size_t(n > 1 ? dst_pitch : len), src, size_t(n > 1 ? src_stride : len),
+                                size_t(len), size_t(n), cudaMemcpyDeviceToHost, reinterpret_cast<cudaStream_t>(stream)));
+    });
+}
+
 extern "C" int kvsnap_dp_crc32c_finish(uint32_t* crc, const uint32_t* expect, int64_t n, uint64_t block_bytes,
                                        uint32_t* status, uintptr_t stream) {
     return guarded([&] {

@@ -488,6 +488,19 @@ def _layer_record(name, tensor, block_size, device):
             "bytes": shape[1] * shape[2] * shape[3] * tensor.element_size()}
 
 
+def _even_pitch(targets, first, end, size):
+    """The pitch at which targets[first:end] lie, if one pitch (at least ``size``) spaces them all, else None."""
+    if end - first == 1:
+        return size
+    pitch = targets[first + 1] - targets[first]
+    if pitch < size:
+        return None
+    for i in range(first + 2, end):
+        if targets[i] - targets[i - 1] != pitch:
+            return None
+    return pitch
+
+
 def column_plan(span_bytes, n, slot_bytes):
     """How a staged save moves through device slots of ``slot_bytes`` when its blocks do not fit at once.
 
@@ -528,6 +541,7 @@ class _SaveJob:
         self.block_ids, self.targets, self.valid = block_ids, targets, valid
         self.hashed, self.known, self.digests = hashed, known, digests
         self.status = self.crc = self.digest = self.side = self.keep = None
+        self.land = None                 # the stream its columns land on by the copy engine, if any
         self.rehash_from = []
 
 
@@ -557,6 +571,16 @@ class TorchBlockDataPlane:
     the two-slot chunk ring; ``digest`` hashes the pinned blocks in place. A
     restore's chunk ring holds two ``chunk_bytes`` chunks.
 
+    ``column_landing``: how such a save's columns reach pinned memory.
+    ``"kernel"`` (the default): a landing kernel stores them through the SMs.
+    ``"copy"``: where a group's targets lie at one pitch (blocks reserved back
+    to back, or one buffer), one copy-engine transfer a column on a stream of
+    its own, overlapping the gather of the next column; other targets still
+    land by kernel. On B200 a lone 8k Qwen3-8B save took 22.5 ms with "copy"
+    against 24.8 with "kernel", but with restores running at the same time
+    (a serving worker's connector threads) "copy" moved 5 % fewer bytes a
+    second end to end, so it suits saves that run alone.
+
     ``shared_name`` puts the pinned pool in POSIX shared memory of that name, so
     that other workers restore its host-tier blocks in place
     (:mod:`kvsnap_b200.sharedtier`).
@@ -568,7 +592,7 @@ class TorchBlockDataPlane:
     sha_sms = 16
 
     def __init__(self, caches, block_size, capacity_bytes, *, save_mode=None, restore_mode=None, ctas=0,
-                 staging_bytes=512 << 20, shared_name=None):
+                 staging_bytes=512 << 20, shared_name=None, column_landing="kernel"):
         import torch
         if not caches:
             raise ValueError("empty KV cache registration")
@@ -586,6 +610,9 @@ class TorchBlockDataPlane:
         if type(staging_bytes) is not int or staging_bytes < (1 << 20):
             raise ValueError("staging_bytes must be an int of at least 1 MiB")
         self.staging_bytes = staging_bytes
+        if column_landing not in ("kernel", "copy"):
+            raise ValueError("column_landing is 'kernel' or 'copy'")
+        self.column_landing = column_landing
         # Kernels that read or write pinned memory in place are bound by the host
         # link, which 16-32 CTAs already saturate; the rest of the GPU stays free
         # for the engine and the SHA-256 kernel.
@@ -654,6 +681,9 @@ class TorchBlockDataPlane:
             self._load_stream = torch.cuda.Stream(self._device())
             self._load_copy_stream = torch.cuda.Stream(self._device())
             self._sha_streams = [torch.cuda.Stream(self._device()) for _ in range(4)]
+            # A bounded save's columns land by the copy engine on a stream of their own, so the
+            # gather of the next column overlaps the landing of this one.
+            self._land_stream = torch.cuda.Stream(self._device())
             self._sha_next = 0
             self._sha_lock = threading.Lock()
         return self._span_table
@@ -1053,8 +1083,9 @@ class TorchBlockDataPlane:
                 done.record()
             except BaseException:
                 stream.synchronize()
-                if job.side is not None:
-                    job.side.synchronize()
+                for other in (job.side, job.land):
+                    if other is not None:
+                        other.synchronize()
                 raise
         done.synchronize()
         self.pool.wait_many({id(a): a for a, _ in targets}.values())
@@ -1133,15 +1164,19 @@ class TorchBlockDataPlane:
         """A save larger than ``staging_bytes``: a ring of device slots, one column of a group of blocks a slot.
 
         For each (group, column): the gather writes the column of every block
-        of the group into a free slot (CRC shares accumulate per block), a
-        landing kernel stores it at each target's column offset in pinned
-        memory (columns are too small for the copy engine to run at the link
-        rate), and the SHA-256 kernel advances every block's hash over it from
-        the state the previous column left. A slot is reused once it has
-        landed and its hash part is done, so device memory stays within
-        ``staging_bytes`` while all blocks hash at once. Needs 16-byte aligned
-        spans and targets (the CRC shares of the segment kernels accumulate
-        across calls; the landing stores are 16 bytes).
+        of the group into a free slot (CRC shares accumulate per block), the
+        column lands at each target's column offset in pinned memory, and the
+        SHA-256 kernel advances every block's hash over it from the state the
+        previous column left. A landing kernel stores the column (one copy a
+        block piece would be too small for the copy engine to run at the link
+        rate); with ``column_landing="copy"`` and a group whose targets lie at
+        one pitch, the column lands as one copy-engine transfer on the landing
+        stream while the SMs gather the next column.
+        A slot is reused once it has landed and its hash part is done, so
+        device memory stays within ``staging_bytes`` while all blocks hash at
+        once. Needs 16-byte aligned spans and targets (the CRC shares of the
+        segment kernels accumulate across calls; the landing stores are 16
+        bytes).
         """
         torch = self.torch
         lib = _dp(self.pool.lib)
@@ -1163,6 +1198,11 @@ class TorchBlockDataPlane:
             ring = torch.empty(slots * slot_bytes, dtype=torch.uint8, device=device)
             base = ring.data_ptr()
             groups = [(g0, min(n, g0 + group)) for g0 in range(0, n, group)]
+            pitches = [_even_pitch(targets, g0, g1, size) if self.column_landing == "copy" else None
+                       for g0, g1 in groups]
+            if any(p is not None for p in pitches):
+                job.land = self._land_stream
+                ring.record_stream(job.land)
             hashed_in = [[i for i in job.hashed if g0 <= i < g1] for g0, g1 in groups]
             # One upload: block ids, target addresses, each slot's block addresses, and for a group whose
             # blocks are not all hashed, per slot the addresses of those that are.
@@ -1190,24 +1230,40 @@ class TorchBlockDataPlane:
                     state = torch.empty(max(1, len(job.hashed)) * 8, dtype=torch.int32, device=device)
             launches, hashed_before, unit = 0, 0, 0
             read = []          # per unit: the event after which its slot's hash part is done, or None
+            landed = []        # per unit: the event after which the landing stream has moved its slot, or None
             for g, (g0, g1) in enumerate(groups):
                 for j, (s0, s1, offset, nbytes) in enumerate(columns):
                     r = unit % slots
                     slot = base + r * slot_bytes
                     slot_table = words + 8 * (slot_at + r * group)
-                    if unit >= slots and read[unit - slots] is not None:
-                        stream.wait_event(read[unit - slots])
+                    if unit >= slots:
+                        for before in (read[unit - slots], landed[unit - slots]):
+                            if before is not None:
+                                stream.wait_event(before)
                     self._check(lib.kvsnap_dp_gather(
                         tables[j].data_ptr(), s1 - s0, size, words + 8 * g0, slot_table, g1 - g0,
                         job.valid if g1 == n else 0, job.crc.data_ptr() + 4 * g0 if job.crc is not None else 0,
                         job.status.data_ptr(), flags[j], self._grid_beside(len(job.hashed)), stream.cuda_stream))
-                    self._check(lib.kvsnap_dp_land(slot, stride, words + 8 * (n + g0), offset, g1 - g0, nbytes,
-                                                   job.status.data_ptr(), 0, stream.cuda_stream))
+                    gathered = None
+                    if pitches[g] is not None:
+                        gathered = torch.cuda.Event()
+                        gathered.record(stream)
+                        job.land.wait_event(gathered)
+                        self._check(lib.kvsnap_dp_land_strided(slot, stride, targets[g0] + offset, pitches[g],
+                                                               g1 - g0, nbytes, job.land.cuda_stream))
+                        moved = torch.cuda.Event()
+                        moved.record(job.land)
+                        landed.append(moved)
+                    else:
+                        self._check(lib.kvsnap_dp_land(slot, stride, words + 8 * (n + g0), offset, g1 - g0, nbytes,
+                                                       job.status.data_ptr(), 0, stream.cuda_stream))
+                        landed.append(None)
                     launches += 1
                     event = None
                     if job.digests and hashed_in[g]:
-                        gathered = torch.cuda.Event()
-                        gathered.record(stream)
+                        if gathered is None:
+                            gathered = torch.cuda.Event()
+                            gathered.record(stream)
                         job.side.wait_event(gathered)
                         at = words + 8 * own_table[g, r] if (g, r) in own_table else slot_table
                         last = j == len(columns) - 1
@@ -1219,6 +1275,10 @@ class TorchBlockDataPlane:
                     read.append(event)
                     unit += 1
                 hashed_before += len(hashed_in[g])
+            if job.land is not None:
+                last = torch.cuda.Event()
+                last.record(job.land)
+                stream.wait_event(last)                  # the targets are written once the copy stream passes here
             if job.crc is not None:
                 self._check(lib.kvsnap_dp_crc32c_finish(job.crc.data_ptr(), 0, n, size, job.status.data_ptr(),
                                                         stream.cuda_stream))

@@ -268,3 +268,17 @@ def test_column_plan_covers_every_block_byte_in_sha_chunks(spans, n, slot):
     assert stride % 16 == 0 and stride >= max(c[3] for c in columns)
     assert 1 <= group <= n
     assert group * stride <= slot or group == 1
+
+
+def test_even_pitch_finds_one_spacing_or_none():
+    """A bounded save lands a group's column by one copy-engine transfer only when one pitch, at least
+    a block, spaces all its targets."""
+    from kvsnap_b200.dataplane import _even_pitch
+    size = 4096
+    assert _even_pitch([1000], 0, 1, size) == size
+    assert _even_pitch([0, 4096, 8192, 12288], 0, 4, size) == 4096
+    assert _even_pitch([0, 4112, 8224, 12336], 1, 4, size) == 4112
+    assert _even_pitch([0, 4096, 8192, 12300], 0, 4, size) is None       # the last gap differs
+    assert _even_pitch([0, 2048, 4096], 0, 3, size) is None                # targets would overlap
+    assert _even_pitch([8192, 4096, 0], 0, 3, size) is None                # descending addresses
+    assert _even_pitch([5, 0, 4096, 8192, 1], 1, 4, size) == 4096          # only the group's range counts

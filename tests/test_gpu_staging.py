@@ -14,6 +14,7 @@ pinned blocks in place. SHA-256 in parts (``kvsnap_dp_sha256_part``) equals
 """
 import ctypes as C
 import hashlib
+import random
 
 import numpy as np
 import pytest
@@ -72,6 +73,20 @@ def test_save_and_verified_restore_stay_within_the_staging_bound(tokens):
         assert digest_cache.hits == len(range(0, n - 1, 2)) and digest_cache.rejected == 0
         for i, a in enumerate(owned):
             assert np.array_equal(pinned(a), expected[i]), f"per-block target {i}"
+        # Columns landed by the copy engine: per-block targets at one pitch (one transfer a column), then
+        # the same allocations in shuffled order, where no one pitch spaces them and the kernel lands them.
+        plane.column_landing = "copy"
+        from kvsnap_b200.dataplane import _even_pitch
+        assert _even_pitch([a.pointer for a in owned], 0, n, size) is not None   # reserved back to back
+        for targets_now in (list(owned), random.Random(5).sample(owned, n)):
+            for a in owned:
+                C.memset(a.pointer, 0, size)
+            got_digests = []
+            plane.save_gather(saved, [(a, 0) for a in targets_now], tokens, digests=got_digests)
+            assert [tuple(d) for d in got_digests] == want
+            for i, a in enumerate(targets_now):
+                assert np.array_equal(pinned(a), expected[i]), f"copy-engine landing, target {i}"
+        plane.column_landing = "kernel"
 
         crcs = [c for _, c in want]
         bits = {name: t.view(torch.int16) for name, t in cache.caches.items()}
@@ -164,6 +179,34 @@ def test_landing_kernel_stores_columns_at_their_targets():
                     continue
                 assert np.array_equal(got[at:at + length], want[i * stride:i * stride + length]), i
         assert lib.kvsnap_dp_land(src.data_ptr(), 8, targets.data_ptr(), 0, n, 16, status.data_ptr(), 0, stream) == -1
+        host.close()
+    finally:
+        pool.close()
+
+
+def test_strided_landing_moves_a_column_to_evenly_spaced_targets():
+    """kvsnap_dp_land_strided: row i of a device column (src + i * stride) to dst + i * pitch in pinned
+    memory, one copy-engine transfer; rows that would overlap are refused."""
+    from kvsnap_b200.dataplane import CudaPool, _dp
+    pool = CudaPool(4 << 20, 0)
+    lib = _dp(pool.lib)
+    try:
+        n, stride, length, pitch, offset = 7, 12288, 10000, 32768 + 48, 4096 + 8
+        src = torch.from_numpy(kvgen.random_bytes(4, n * stride)).cuda()
+        host = pool.reserve(n * pitch + offset)
+        C.memset(host.pointer, 0xA5, n * pitch + offset)
+        stream = torch.cuda.current_stream().cuda_stream
+        assert lib.kvsnap_dp_land_strided(src.data_ptr(), stride, host.pointer + offset, pitch, n, length, stream) == 0
+        torch.cuda.synchronize()
+        got, want = pinned(host), src.cpu().numpy()
+        for i in range(n):
+            at = offset + i * pitch
+            assert np.array_equal(got[at:at + length], want[i * stride:i * stride + length]), i
+            assert (got[at + length:at + pitch] == 0xA5).all(), f"row {i} wrote past its length"
+        assert (got[:offset] == 0xA5).all()
+        assert lib.kvsnap_dp_land_strided(src.data_ptr(), stride, host.pointer, length - 1, n, length, stream) == -1
+        assert lib.kvsnap_dp_land_strided(src.data_ptr(), length - 16, host.pointer, pitch, n, length, stream) == -1
+        assert lib.kvsnap_dp_land_strided(src.data_ptr(), stride, host.pointer, pitch, 0, length, stream) == 0
         host.close()
     finally:
         pool.close()
