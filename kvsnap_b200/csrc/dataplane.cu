@@ -650,8 +650,10 @@ constexpr int kRing = kSegDepth + 2 <= 4 ? 4 : 8;
 static_assert(kRing >= kSegDepth + 2 && (kRing & (kRing - 1)) == 0, "ring of unit descriptions");
 
 // Dynamic shared memory of a segment kernel of `warps` warps, in order: the
-// unit rings, T_0..T_3 (the chain combine) and, for runs, the append table,
-// then the replicated tables. It is sized to the launch: shared memory and L1
+// replicated tables, T_0..T_3 (the chain combine), for runs the append table,
+// then the unit rings (a launch without a CRC holds only the rings). The
+// replicated tables start the layout so that their base is a constant: each
+// lookup addresses a constant plus its byte-permuted index. It is sized to the launch: shared memory and L1
 // split one 256 KiB array a SM, and what L1 keeps holds the loads in flight
 // (a 200 KiB layout, which leaves 28 KiB of L1 instead of 60, measured 13 %
 // slower).
@@ -674,11 +676,11 @@ struct SegSmem {
     uint32_t* t4;        // T_0..T_3
     uint32_t* tx;        // the append table (runs only)
     uint32_t* tb;        // the replicated tables
-    __device__ SegSmem(uint4* smem, int warp, int warps, bool runs) {
-        ring = reinterpret_cast<SegUnit*>(smem) + warp * kRing;
-        t4 = reinterpret_cast<uint32_t*>(smem + seg_ring_bytes(warps) / 16);
+    __device__ SegSmem(uint4* smem, int warp, bool runs, bool crc) {
+        tb = reinterpret_cast<uint32_t*>(smem);
+        t4 = tb + kRepWords;
         tx = t4 + 4 * 256;
-        tb = t4 + (runs ? 2 : 1) * 4 * 256;
+        ring = reinterpret_cast<SegUnit*>(crc ? t4 + (runs ? 2 : 1) * 4 * 256 : tb) + warp * kRing;
     }
 };
 
@@ -1009,10 +1011,10 @@ template <int MODE, bool TAIL, bool RUNS>
 __global__ void __launch_bounds__(kSegThreads, 1) span_kernel_hbm(SpanArgs a) {
     extern __shared__ uint4 smem[];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, per_cta = blockDim.x >> 5;
-    const SegSmem sm(smem, warp, per_cta, RUNS);
+    const bool crc = a.crc != nullptr;
+    const SegSmem sm(smem, warp, RUNS, crc);
     SegUnit* ring = sm.ring;
     uint32_t *t4 = sm.t4, *tx = sm.tx, *tb = sm.tb;
-    const bool crc = a.crc != nullptr;
     // Runs are folded with the first unit's size (a pair: two spans); units of other sizes take the multiply.
     const int64_t first_bytes = (RUNS && a.pairs ? 2 : 1) * a.spans[0].bytes;
     const int64_t span_bytes = first_bytes >= 4 ? first_bytes : 4;
@@ -1071,7 +1073,7 @@ __global__ void __launch_bounds__(32 * kSegCrcWarps, 1) crc_kernel_hbm(const int
                                                                  uint32_t* status, int place) {
     extern __shared__ uint4 smem[];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, per_cta = blockDim.x >> 5;
-    const SegSmem sm(smem, warp, per_cta, false);
+    const SegSmem sm(smem, warp, false, true);
     SegUnit* ring = sm.ring;
     uint32_t *t4 = sm.t4, *tx = sm.tx, *tb = sm.tb;     // tx: unused without runs
     load_seg_tables(tb, t4);
