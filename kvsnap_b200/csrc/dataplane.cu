@@ -276,10 +276,10 @@ struct SpanArgs {
     uint32_t* crc;           // raw XOR accumulators, zeroed before launch, or null
     const uint32_t* gate;    // scatter: skip all writes when *gate != 0
     uint32_t* status;
-    int pairs = 0;           // runs of segment kernels: units are pairs of spans (KVSNAP_DP_PAIRS)
     int split = 0;           // grid-stride segment kernels: units are 1 / 2^split of a span (KVSNAP_DP_SPLIT*)
     int place = 0;           // grid-stride segment kernels: placement tables follow the line buffers
     int spans_at = -1;       // segment kernels: byte offset of a shared-memory copy of the span table, or -1
+    int clean = 0;           // segment kernels, set in the kernel: the table passed the checks every unit needs
 };
 
 template <int VEC, int MODE>
@@ -690,18 +690,18 @@ struct SegSmem {
 // [u*w/W, u*(w+1)/W), whose neighbours are mostly the next span of the same
 // block (runs); otherwise warp w takes units w, w + W, ..., so that
 // concurrent warps move neighbouring bytes.
-template <int MODE, bool RANGE>
+template <int MODE, bool RANGE, int WIDTH = 1>
 struct SpanUnits {
+    static_assert(WIDTH == 1 || (RANGE && WIDTH == 2), "units of two spans walk contiguous ranges");
+    static constexpr int width = WIDTH;    // spans a unit: 2 for pairs, else 1
     SpanArgs a;
     int64_t i, left;     // packed block of the cursor, and units left to walk
     int64_t di;          // block step (grid-stride)
     int s, ds;           // span of the cursor, and its step (grid-stride)
     int p, dp;           // piece of the cursor in its span, and its step (grid-stride)
-    int width;           // spans a unit: 2 for pairs (RANGE only), else 1
     int split;           // log2 of the units a span (grid-stride only), else 0
     int64_t held = -1, held_block = 0, held_packed = 0;   // packed block `held`'s cache id and address
     __device__ SpanUnits(const SpanArgs& args, int64_t w, int64_t warps) : a(args) {
-        width = RANGE && args.pairs ? 2 : 1;
         split = RANGE ? 0 : args.split;
         const int per_block = args.nspans / width << split;
         const int64_t count = args.n * per_block;
@@ -752,7 +752,9 @@ struct SpanUnits {
             int64_t bytes = sp.bytes >> split;
             const int64_t packed = held_packed + sp.offset + p * bytes;
             const int64_t cache = sp.base + block * sp.pitch + p * bytes;
-            if (split && (bytes << split != sp.bytes || bytes % kSegStep)) {   // whole steps a segment, no padding
+            // A clean table (every span 16-byte aligned, whole steps a piece, pairs adjacent and equal)
+            // leaves a unit only its block bounds and packed address to check.
+            if (!a.clean && split && (bytes << split != sp.bytes || bytes % kSegStep)) {
                 if (lane == 0) flag(a.status, KVSNAP_DP_BAD_CUT);
                 continue;
             }
@@ -761,11 +763,11 @@ struct SpanUnits {
             if (width == 2) {            // the pair's second span follows in the packed block
                 const kvsnap_span& sq = a.spans[s + 1];
                 uint32_t bad = 0;
-                if (sq.bytes != bytes || sq.offset != sp.offset + bytes || (2 * bytes) % kSegStep)
+                if (!a.clean && (sq.bytes != bytes || sq.offset != sp.offset + bytes || (2 * bytes) % kSegStep))
                     bad |= KVSNAP_DP_BAD_CUT;
                 if (block >= sq.nblocks) bad |= KVSNAP_DP_BAD_BLOCK;
                 const int64_t other = sq.base + block * sq.pitch;
-                if (other & 15) bad |= KVSNAP_DP_MISALIGNED;
+                if (!a.clean && (other & 15)) bad |= KVSNAP_DP_MISALIGNED;
                 if (bad) {
                     if (lane == 0) flag(a.status, bad);
                     continue;
@@ -774,7 +776,7 @@ struct SpanUnits {
                 shift = sq.crc_shift;
                 bytes *= 2;
             }
-            if ((packed | cache | bytes) & 15) {
+            if ((a.clean ? packed : packed | cache | bytes) & 15) {
                 if (lane == 0) flag(a.status, KVSNAP_DP_MISALIGNED);
                 continue;
             }
@@ -1007,8 +1009,9 @@ __device__ __forceinline__ void warp_stream(Units units, const RepTables& tl, co
 // its own, so the common kernel carries none of the masking code.
 // Shared memory: unit rings, then (with a CRC) the tables, and in the
 // grid-stride path the placement tables when the launcher sized for them.
-template <int MODE, bool TAIL, bool RUNS>
+template <int MODE, bool TAIL, bool RUNS, bool PAIRS = false>
 __global__ void __launch_bounds__(kSegThreads, 1) span_kernel_hbm(SpanArgs a) {
+    static_assert(!PAIRS || RUNS, "pairs of spans fold in runs");
     extern __shared__ uint4 smem[];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, per_cta = blockDim.x >> 5;
     const bool crc = a.crc != nullptr;
@@ -1016,7 +1019,7 @@ __global__ void __launch_bounds__(kSegThreads, 1) span_kernel_hbm(SpanArgs a) {
     SegUnit* ring = sm.ring;
     uint32_t *t4 = sm.t4, *tx = sm.tx, *tb = sm.tb;
     // Runs are folded with the first unit's size (a pair: two spans); units of other sizes take the multiply.
-    const int64_t first_bytes = (RUNS && a.pairs ? 2 : 1) * a.spans[0].bytes;
+    const int64_t first_bytes = (PAIRS ? 2 : 1) * a.spans[0].bytes;
     const int64_t span_bytes = first_bytes >= 4 ? first_bytes : 4;
     Placement pl;
     if (crc) {
@@ -1046,7 +1049,19 @@ __global__ void __launch_bounds__(kSegThreads, 1) span_kernel_hbm(SpanArgs a) {
         for (int k = threadIdx.x; k < a.nspans * int(sizeof(kvsnap_span) / 16); k += blockDim.x) to[k] = from[k];
         b.spans = reinterpret_cast<const kvsnap_span*>(to);
     }
-    __syncthreads();
+    // The table checks that hold for every unit, made once a CTA (TP shards' small units would
+    // otherwise repeat them every other step).
+    int ok = 1;
+    for (int k = threadIdx.x; k < a.nspans; k += blockDim.x) {
+        const kvsnap_span& sp = a.spans[k];
+        if ((sp.base | sp.pitch | sp.offset | sp.bytes) & 15) ok = 0;
+        if (a.split && ((sp.bytes >> a.split) << a.split != sp.bytes || (sp.bytes >> a.split) % kSegStep)) ok = 0;
+        if (PAIRS && (k & 1)) {
+            const kvsnap_span& sq = a.spans[k - 1];
+            if (sp.bytes != sq.bytes || sp.offset != sq.offset + sq.bytes || (2 * sp.bytes) % kSegStep) ok = 0;
+        }
+    }
+    b.clean = __syncthreads_and(ok);
     if (MODE == kScatter && a.gate && *a.gate) return;
     const RepTables tl{reinterpret_cast<const char*>(tb), 4u * lane};
     const AppendBytes append{tx, span_bytes};
@@ -1056,7 +1071,8 @@ __global__ void __launch_bounds__(kSegThreads, 1) span_kernel_hbm(SpanArgs a) {
                                               nullptr, b.spans, b.valid);
     else
         warp_stream<true, true, TAIL, RUNS, RUNS ? (MODE == kGather ? 1 : 2) : 0>(
-            SpanUnits<MODE, RUNS>(b, w, warps), tl, t4, append, ring, lane, b.crc, b.spans, b.valid, pl);
+            SpanUnits<MODE, RUNS, PAIRS ? 2 : 1>(b, w, warps), tl, t4, append, ring, lane, b.crc, b.spans, b.valid,
+            pl);
 }
 
 // `place`: the launcher sized shared memory for placement tables with a shift row a piece.
@@ -1631,7 +1647,7 @@ void spans_launch(const kvsnap_span* spans, int nspans, uint64_t block_bytes, co
         const int sms = enter_stream(stream);
         cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
         if (crc && !accumulate) check(cudaMemsetAsync(crc, 0, sizeof(uint32_t) * size_t(n), s));
-        SpanArgs a{spans, nspans, blocks, packed, n, valid, crc, gate, status, pairs ? 1 : 0, split};
+        SpanArgs a{spans, nspans, blocks, packed, n, valid, crc, gate, status, split};
         if (hbm) {
             // Without a CTA count, the segment kernels run on all SMs but one in nine (132 of 148):
             // with 12 warps a CTA, B200 moved every span size fastest at 128 to 136 CTAs, and 3 to
@@ -1657,7 +1673,8 @@ void spans_launch(const kvsnap_span* spans, int nspans, uint64_t block_bytes, co
             }
             if (body > 0) {
                 a.n = body;
-                auto kernel = runs ? span_kernel_hbm<MODE, false, true> : span_kernel_hbm<MODE, false, false>;
+                auto kernel = !runs ? span_kernel_hbm<MODE, false, false>
+                              : pairs ? span_kernel_hbm<MODE, false, true, true> : span_kernel_hbm<MODE, false, true>;
                 // A launch on fewer CTAs than SMs keeps more loads in flight a CTA: at 132 of 148 SMs, 12
                 // warps moved Qwen3-8B spans at 0.93 of the HBM copy rate where 10 reached 0.91; a launch
                 // asked for on every SM takes 10 warps, which measured fastest there.
