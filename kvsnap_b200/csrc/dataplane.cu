@@ -386,19 +386,34 @@ constexpr int kSegThreads = 32 * kSegWarps;
 
 // Replicated layout, 256 bytes an entry so one byte permute forms an address:
 // entry v of T_{127-(2h+p)} for lane l lies at byte h*65536 + v*256 + p*128 + 4l,
-// which puts every lane in its own bank whatever v is. The 32 lane copies of a
-// value are 128 contiguous bytes: eight threads store them as 16-byte vectors
-// after one load, so a CTA reads each table value once (filling the table a
-// word at a time measured 6.5 to 9 microseconds a launch).
-__device__ __forceinline__ void load_rep_tables(uint32_t* tb) {
-    uint4* out = reinterpret_cast<uint4*>(tb);
-#pragma unroll 4
-    for (int i = threadIdx.x; i < kRepWords / 4; i += blockDim.x) {
-        const int e = i >> 3;                          // byte offset / 128: h * 512 + v * 2 + p
-        const int h = e >> 9, v = (e >> 1) & 255, p = e & 1;
-        const uint32_t x = g_tables.t[27 - (2 * h + p)][v];   // slot 27 - q holds T_{127-q}
-        out[i] = make_uint4(x, x, x, x);
+// which puts every lane in its own bank whatever v is. The layout is built at
+// compile time into a 128 KiB image in global memory, and each CTA copies it
+// with asynchronous 16-byte copies, all of a thread's in flight at once.
+struct alignas(16) RepImage {
+    uint32_t w[kRepWords];
+};
+
+constexpr RepImage make_rep_image() {
+    const CrcTables t = make_tables();
+    RepImage r{};
+    for (int i = 0; i < kRepWords; ++i) {
+        const int h = i >> 14, v = (i >> 6) & 255, p = (i >> 5) & 1;
+        r.w[i] = t.t[27 - (2 * h + p)][v];   // slot 27 - q holds T_{127-q}
     }
+    return r;
+}
+
+__device__ const RepImage g_rep = make_rep_image();
+
+// Each thread waits for its own copies here; the prologue's closing barrier makes them visible
+// to the CTA.
+__device__ __forceinline__ void load_rep_tables(uint32_t* tb) {
+    const uint32_t to = static_cast<uint32_t>(__cvta_generic_to_shared(tb));
+    const uint4* from = reinterpret_cast<const uint4*>(g_rep.w);
+    for (int i = threadIdx.x; i < kRepWords / 4; i += blockDim.x)
+        asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(to + 16u * uint32_t(i)), "l"(from + i)
+                     : "memory");
+    asm volatile("cp.async.wait_all;" ::: "memory");
 }
 
 // The replicated T_124..T_127 and one plain copy of T_0..T_3.
